@@ -1,0 +1,130 @@
+"""ctypes binding of ``libgemma4_b200.so`` (C ABI: ``include/gemma4_b200.h``).
+
+The library is loaded from the package directory.  There is no fallback: if it
+is missing or fails to load, every operator raises ``LibraryUnavailable``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG_DIR, "libgemma4_b200.so")
+
+ABI_VERSION = 1
+
+G4_OK = 0
+G4_ERR_INVALID = 1
+G4_ERR_UNSUPPORTED = 2
+G4_ERR_CUDA = 3
+G4_ERR_DEVICE = 4
+G4_ERR_WORKSPACE = 5
+
+# Every exported entry point declared in include/gemma4_b200.h.
+EXPORTED_SYMBOLS = (
+    "g4_abi_version",
+    "g4_last_error",
+    "g4_attn_fwd_workspace_bytes",
+    "g4_attn_fwd",
+    "g4_attn_bwd_workspace_bytes",
+    "g4_attn_bwd",
+    "g4_read_device_error",
+    "g4_build_mask",
+)
+
+
+class LibraryUnavailable(RuntimeError):
+    """The native library could not be loaded (build it with ``build.py``)."""
+
+
+class G4AttnArgs(ctypes.Structure):
+    """Mirror of ``g4_attn_args``."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("dout", ctypes.c_void_p),
+        ("dlse", ctypes.c_void_p),
+        ("dq", ctypes.c_void_p),
+        ("dk", ctypes.c_void_p),
+        ("dv", ctypes.c_void_p),
+        ("q_stride", ctypes.c_int64 * 3),
+        ("k_stride", ctypes.c_int64 * 3),
+        ("v_stride", ctypes.c_int64 * 3),
+        ("o_stride", ctypes.c_int64 * 3),
+        ("do_stride", ctypes.c_int64 * 3),
+        ("dq_stride", ctypes.c_int64 * 3),
+        ("dk_stride", ctypes.c_int64 * 3),
+        ("dv_stride", ctypes.c_int64 * 3),
+        ("lse_stride", ctypes.c_int64 * 2),
+        ("batch", ctypes.c_int32),
+        ("seqlen_q", ctypes.c_int32),
+        ("seqlen_k", ctypes.c_int32),
+        ("cu_seqlens_q", ctypes.c_void_p),
+        ("cu_seqlens_k", ctypes.c_void_p),
+        ("max_seqlen_q", ctypes.c_int32),
+        ("max_seqlen_k", ctypes.c_int32),
+        ("num_q_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim_qk", ctypes.c_int32),
+        ("head_dim_v", ctypes.c_int32),
+        ("window", ctypes.c_int32),
+        ("vision_ids", ctypes.c_void_p),
+        ("document_ids", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the native library."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise LibraryUnavailable(
+                f"{LIB_PATH} is missing; run `python -m gemma4_fa4_kernels_b200.build`")
+        try:
+            lib = ctypes.CDLL(LIB_PATH)
+        except OSError as exc:
+            raise LibraryUnavailable(f"cannot load {LIB_PATH}: {exc}") from exc
+        P = ctypes.POINTER(G4AttnArgs)
+        lib.g4_abi_version.restype = ctypes.c_int
+        lib.g4_last_error.restype = ctypes.c_char_p
+        for name in ("g4_attn_fwd_workspace_bytes", "g4_attn_bwd_workspace_bytes"):
+            fn = getattr(lib, name)
+            fn.argtypes = [P]
+            fn.restype = ctypes.c_size_t
+        for name in ("g4_attn_fwd", "g4_attn_bwd"):
+            fn = getattr(lib, name)
+            fn.argtypes = [P, ctypes.c_void_p]
+            fn.restype = ctypes.c_int
+        lib.g4_read_device_error.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int),
+                                             ctypes.c_void_p]
+        lib.g4_read_device_error.restype = ctypes.c_int
+        lib.g4_build_mask.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                      ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_void_p]
+        lib.g4_build_mask.restype = ctypes.c_int
+        if lib.g4_abi_version() != ABI_VERSION:
+            raise LibraryUnavailable(
+                f"ABI mismatch: library {lib.g4_abi_version()}, bindings {ABI_VERSION}")
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return load().g4_last_error().decode(errors="replace")

@@ -1,0 +1,438 @@
+// Gemma-4 attention forward for sm_100a: TMA-staged Q/K/V tiles feeding
+// tcgen05 MMAs with S/P and O accumulators in tensor memory.
+//
+// One CTA owns a 128-row query tile of one query head and one 256-wide slab
+// of the value/output head dimension (local d256: one slab; global d512: two
+// slabs, each recomputing the 512-deep QK^T because a 128x512 fp32 O would
+// fill all of TMEM).  Warp roles (192 threads):
+//   warps 0-3  softmax + epilogue: thread r owns query row r (TMEM lane r)
+//   warp  4    TMA producer (one elected lane); also allocates TMEM
+//   warp  5    MMA issuer (one elected lane)
+// TMEM columns: S0 [0,128), S1 [128,256), O [256,512); P (bf16 pairs) is
+// written over the first 64 columns of its S buffer and consumed from TMEM by
+// the PV MMA.  K/V chunks stream through a ring of 32 KB shared stages in the
+// exact order the MMA warp consumes them: K(0), K(1), V(0), K(2), V(1), ...
+//
+// Online softmax in the exp2 domain with lazy rescaling: the running max only
+// moves (and O is only rescaled) when a tile's max exceeds it by more than 8,
+// so P <= 2^8.  Fully masked rows give O = 0 and LSE = -inf (reference.py:70-75).
+//
+// Reference interface replaced: flash_attn.cute.flash_attn_func /
+// flash_attn_varlen_func forward as called by src/gemma4_fa4/h100.py:766-778,
+// 800-815, 864-910, 1013-1036, 1174-1190, 1356-1377.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "g4_attn.cuh"
+#include "g4_kernels.h"
+#include "g4_sm100.cuh"
+
+namespace g4 {
+
+template <int DQK>
+struct FwdCfg {
+  static constexpr int kQBytes = DQK * kTileM * 2;
+  static constexpr int kStageBytes = 32768;
+  static constexpr int kStages = DQK == 256 ? 5 : 3;
+  static constexpr int kKChunks = DQK / 128;  // 128-deep K chunks per key tile
+  static constexpr int kVChunks = 2;          // 64 keys x 256 values per chunk
+  static constexpr int kMiscBytes = 2048;
+  static constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + kMiscBytes + 1024;
+};
+
+struct FwdMisc {
+  uint64_t q_full;
+  uint64_t ring_full[8];
+  uint64_t ring_empty[8];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int k_lo;
+  int k_hi;
+  int pad[4];
+  int kvis[kTileN];
+  int kdoc[kTileN];
+};
+
+template <int DQK>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  using Cfg = FwdCfg<DQK>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* q_s = smem;
+  uint8_t* ring = smem + Cfg::kQBytes;
+  FwdMisc* misc = reinterpret_cast<FwdMisc*>(ring + Cfg::kStages * Cfg::kStageBytes);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int head = blockIdx.y;
+  const int slab = blockIdx.z;
+  const int kv_head = head / p.group;
+
+  // ---- work item -> (sequence, query tile) ----
+  int seq, qt;
+  if (p.tiles != nullptr) {
+    if (static_cast<int>(blockIdx.x) >= *p.n_tiles) return;
+    const int2 t = p.tiles[blockIdx.x];
+    seq = t.x;
+    qt = t.y;
+  } else {
+    const int nqt = (p.layout.seqlen_q + kTileM - 1) / kTileM;
+    seq = blockIdx.x / nqt;
+    qt = nqt - 1 - static_cast<int>(blockIdx.x % nqt);  // longest causal rows first
+  }
+  const SeqInfo si = p.layout.seq(seq);
+  const int q_off = si.len_k - si.len_q;
+
+  if (tid == 0) {
+    mbar_init(&misc->q_full, 1);
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&misc->ring_full[s], 1);
+      mbar_init(&misc->ring_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&misc->s_full[b], 1);
+      mbar_init(&misc->p_full[b], kTileM);
+    }
+    mbar_init(&misc->o_done, 1);
+    mbar_init(&misc->drain, 1);
+    misc->abort = 0;
+    misc->k_lo = 0x7fffffff;
+    misc->k_hi = -1;
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(&misc->tmem_base, 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+
+  // ---- key range of this query tile (exact bounds; tiles inside are classified) ----
+  const int row = tid;  // valid for tid < 128
+  const int q_idx = qt * kTileM + row;
+  const bool row_valid = tid < kTileM && q_idx < si.len_q;
+  const int q_abs = q_idx + q_off;
+  int qvis = -1, qdoc = 0;
+  if (row_valid) {
+    if (p.mask.vis) qvis = p.mask.vis[si.meta_base + q_abs];
+    if (p.mask.doc) qdoc = p.mask.doc[si.meta_base + q_abs];
+    int lo = p.mask.window > 0 ? max(0, q_abs - p.mask.window + 1) : 0;
+    int hi = q_abs;
+    if (p.mask.window > 0 && qvis >= 0) {
+      hi = p.mask.pair_last ? max(hi, p.mask.pair_last[si.meta_base + q_abs]) : si.len_k - 1;
+    }
+    atomicMin(&misc->k_lo, lo);
+    atomicMax(&misc->k_hi, min(hi, si.len_k - 1));
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem = misc->tmem_base;
+  const int kt_lo = misc->k_hi >= 0 ? misc->k_lo / kTileN : 0;
+  const int n_kt = misc->k_hi >= 0 ? misc->k_hi / kTileN - kt_lo + 1 : 0;
+  const CtaAbort ab{&misc->abort, p.err};
+
+  if (warp == 4) {
+    // ============================ TMA producer ============================
+    if (lane == 0 && n_kt > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_expect_tx(&misc->q_full, Cfg::kQBytes);
+      for (int blk = 0; blk < DQK / 64; ++blk)
+        tma_load_4d(q_s + blk * 16384, &tmQ, &misc->q_full, blk * 64, head,
+                    si.q_base + qt * kTileM, si.b_coord);
+      uint32_t it = 0;
+      bool ok = true;
+      auto acquire = [&](uint32_t& stage) -> bool {
+        stage = it % Cfg::kStages;
+        const uint32_t ph = (it / Cfg::kStages) & 1;
+        if (!mbar_wait(&misc->ring_empty[stage], ph ^ 1, ab, kDevTimeoutMma)) return false;
+        mbar_expect_tx(&misc->ring_full[stage], Cfg::kStageBytes);
+        return true;
+      };
+      auto load_k = [&](int kt) {
+        for (int c = 0; c < Cfg::kKChunks && ok; ++c) {
+          uint32_t st;
+          if (!(ok = acquire(st))) break;
+          uint8_t* dst = ring + st * Cfg::kStageBytes;
+          for (int h = 0; h < 2; ++h)
+            tma_load_4d(dst + h * 16384, &tmK, &misc->ring_full[st], (2 * c + h) * 64, kv_head,
+                        si.k_base + kt * kTileN, si.b_coord);
+          ++it;
+        }
+      };
+      auto load_v = [&](int kt) {
+        for (int c = 0; c < Cfg::kVChunks && ok; ++c) {
+          uint32_t st;
+          if (!(ok = acquire(st))) break;
+          uint8_t* dst = ring + st * Cfg::kStageBytes;
+          for (int blk = 0; blk < 4; ++blk)
+            tma_load_4d(dst + blk * 8192, &tmV, &misc->ring_full[st], slab * 256 + blk * 64,
+                        kv_head, si.k_base + kt * kTileN + c * 64, si.b_coord);
+          ++it;
+        }
+      };
+      load_k(kt_lo);
+      for (int j = 0; j < n_kt && ok; ++j) {
+        if (j + 1 < n_kt) load_k(kt_lo + j + 1);
+        load_v(kt_lo + j);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ============================ MMA issuer ============================
+    if (lane == 0 && n_kt > 0) {
+      constexpr uint32_t kIdS = idesc_bf16(128, 128, false, false);
+      constexpr uint32_t kIdPV = idesc_bf16(128, 256, false, true);
+      const uint32_t q_base = smem_addr(q_s);
+      const uint32_t ring_base = smem_addr(ring);
+      uint32_t it = 0;
+      bool ok = mbar_wait(&misc->q_full, 0, ab, kDevTimeoutTma);
+      auto take = [&](uint32_t& stage) -> bool {
+        stage = it % Cfg::kStages;
+        const uint32_t ph = (it / Cfg::kStages) & 1;
+        if (!mbar_wait(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
+        tc_fence_after();
+        return true;
+      };
+      auto issue_s = [&](int j) {
+        const uint32_t d = tmem + (j & 1) * 128;
+        for (int c = 0; c < Cfg::kKChunks && ok; ++c) {
+          uint32_t st;
+          if (!(ok = take(st))) break;
+          const uint32_t kb = ring_base + st * Cfg::kStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const int g = c * 8 + kk;
+            const uint64_t a = sdesc_sw128(q_base + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024);
+            const uint64_t b = sdesc_sw128(kb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+            umma_ss(d, a, b, kIdS, (c | kk) != 0);
+          }
+          umma_commit(&misc->ring_empty[st]);
+          ++it;
+        }
+        umma_commit(&misc->s_full[j & 1]);
+      };
+      auto issue_pv = [&](int j) {
+        const uint32_t a_t = tmem + (j & 1) * 128;
+        for (int c = 0; c < Cfg::kVChunks && ok; ++c) {
+          uint32_t st;
+          if (!(ok = take(st))) break;
+          const uint32_t vb = ring_base + st * Cfg::kStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t b = sdesc_sw128(vb + kk * 2048, 8192, 1024);
+            umma_ts(tmem + 256, a_t + c * 32 + kk * 8, b, kIdPV, (j | c | kk) != 0);
+          }
+          umma_commit(&misc->ring_empty[st]);
+          ++it;
+        }
+        umma_commit(&misc->o_done);
+      };
+      if (ok) issue_s(0);
+      for (int j = 0; j < n_kt && ok; ++j) {
+        if (j + 1 < n_kt) issue_s(j + 1);
+        if (!(ok = mbar_wait(&misc->p_full[j & 1], (j >> 1) & 1, ab, kDevTimeoutPeer))) break;
+        tc_fence_after();
+        issue_pv(j);
+      }
+      // Drain: every MMA this thread issued has completed before TMEM is freed.
+      umma_commit(&misc->drain);
+      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+    }
+    __syncwarp();
+  } else {
+    // ======================= softmax + epilogue (warps 0-3) =======================
+    // Every tcgen05.ld/st below is .sync.aligned, so all control flow around
+    // them is kept warp-uniform: `ok` is reduced with __all_sync after each
+    // wait and the rescale decision with __any_sync.  Loops never break, so
+    // the named barriers are reached the same number of times by all warps.
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const bool meta = p.mask.has_meta();
+    const int qa0 = qt * kTileM + q_off;
+    const int qa1 = min((qt + 1) * kTileM, si.len_q) - 1 + q_off;
+    float m_run = -INFINITY;  // running max, log2 domain
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kt; ++j) {
+      const int k0 = (kt_lo + j) * kTileN;
+      const int cls = meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
+      if (meta) {
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int kk = k0 + tid;
+        const bool in = kk < si.len_k;
+        misc->kvis[tid] = (p.mask.vis && in) ? p.mask.vis[si.meta_base + kk] : -1;
+        misc->kdoc[tid] = (p.mask.doc && in) ? p.mask.doc[si.meta_base + kk] : 0;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      if (ok) ok = mbar_wait(&misc->s_full[j & 1], (j >> 1) & 1, ab, kDevTimeoutMma);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) continue;
+      tc_fence_after();
+      float s[kTileN];
+      {
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        const uint32_t sb = lane_base + (j & 1) * 128;
+        tmem_ld32(sb + 0, r0);
+        tmem_ld32(sb + 32, r1);
+        tmem_ld32(sb + 64, r2);
+        tmem_ld32(sb + 96, r3);
+        tmem_wait_ld();
+        reg_fence32(r0);
+        reg_fence32(r1);
+        reg_fence32(r2);
+        reg_fence32(r3);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          s[i] = __uint_as_float(r0[i]);
+          s[32 + i] = __uint_as_float(r1[i]);
+          s[64 + i] = __uint_as_float(r2[i]);
+          s[96 + i] = __uint_as_float(r3[i]);
+        }
+      }
+      if (cls != 1) {
+#pragma unroll
+        for (int i = 0; i < kTileN; ++i) {
+          const int k = k0 + i;
+          bool keep;
+          if (k >= si.len_k) {
+            keep = false;
+          } else if (meta) {
+            keep = mask_allows(p.mask.window, q_abs, k, qvis, qdoc, misc->kvis[i], misc->kdoc[i]);
+          } else {
+            keep = mask_allows(p.mask.window, q_abs, k, -1, 0, -1, 0);
+          }
+          if (!keep) s[i] = -INFINITY;
+        }
+      }
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kTileN; ++i) mt = fmaxf(mt, s[i]);
+      mt *= kLog2e;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mt > m_run + 8.f) {  // also true for the first finite tile (m_run = -inf)
+        alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - mt);
+        m_run = mt;
+        rescale = true;
+      }
+      const float m_sub = (m_run == -INFINITY) ? 0.f : m_run;
+      float rowsum = 0.f;
+      {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float p0 = ex2(fmaf(s[c * 64 + 2 * i], kLog2e, -m_sub));
+            const float p1 = ex2(fmaf(s[c * 64 + 2 * i + 1], kLog2e, -m_sub));
+            rowsum += p0 + p1;
+            pk[i] = pack_bf16x2(p0, p1);
+          }
+          tmem_st32(lane_base + (j & 1) * 128 + c * 32, pk);
+        }
+      }
+      l_run = l_run * alpha + rowsum;
+      tmem_wait_st();
+      if (j > 0) {
+        ok = mbar_wait(&misc->o_done, (j - 1) & 1, ab, kDevTimeoutMma);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok && __any_sync(0xffffffffu, rescale)) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 8; c += 2) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(lane_base + 256 + c * 32, r0);
+            tmem_ld32(lane_base + 256 + c * 32 + 32, r1);
+            tmem_wait_ld();
+            reg_fence32(r0);
+            reg_fence32(r1);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              r0[i] = __float_as_uint(__uint_as_float(r0[i]) * alpha);
+              r1[i] = __float_as_uint(__uint_as_float(r1[i]) * alpha);
+            }
+            tmem_st32(lane_base + 256 + c * 32, r0);
+            tmem_st32(lane_base + 256 + c * 32 + 32, r1);
+          }
+          tmem_wait_st();
+        }
+      }
+      tc_fence_before();
+      if (ok) mbar_arrive(&misc->p_full[j & 1]);
+    }
+    // ---- epilogue: O / l -> bf16, LSE ----
+    if (ok && n_kt > 0) ok = mbar_wait(&misc->o_done, (n_kt - 1) & 1, ab, kDevTimeoutMma);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    const bool have_o = ok && n_kt > 0;
+    const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+    __nv_bfloat16* orow = p.o + static_cast<int64_t>(si.b_coord) * p.o_stride[0] +
+                          static_cast<int64_t>(si.q_base + q_idx) * p.o_stride[1] +
+                          static_cast<int64_t>(head) * p.o_stride[2] + slab * 256;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      uint32_t r[32];
+      if (have_o) {
+        tmem_ld32(lane_base + 256 + c * 32, r);
+        tmem_wait_ld();
+        reg_fence32(r);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = 0u;
+      }
+      if (row_valid) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l,
+                              __uint_as_float(r[2 * i + 1]) * inv_l);
+        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
+    }
+    if (row_valid && slab == 0) {
+      const float lse = (l_run > 0.f) ? (m_run + __log2f(l_run)) * kLn2 : -INFINITY;
+      p.lse[static_cast<int64_t>(si.b_coord) * p.lse_stride[0] +
+            static_cast<int64_t>(head) * p.lse_stride[1] + si.q_base + q_idx] = lse;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int DQK>
+int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+               const FwdParams& p, int grid_x, int num_q_heads, int slabs, cudaStream_t stream) {
+  using Cfg = FwdCfg<DQK>;
+  cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<DQK>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  dim3 grid(grid_x, num_q_heads, slabs);
+  attn_fwd_kernel<DQK><<<grid, 192, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template int launch_fwd<256>(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                             const FwdParams&, int, int, int, cudaStream_t);
+template int launch_fwd<512>(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                             const FwdParams&, int, int, int, cudaStream_t);
+
+}  // namespace g4

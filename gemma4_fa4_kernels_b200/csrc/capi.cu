@@ -1,0 +1,286 @@
+// C-ABI layer of libgemma4_b200.so: argument validation, workspace planning,
+// TMA tensor-map construction and kernel launches.  See include/gemma4_b200.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "../../include/gemma4_b200.h"
+#include "g4_kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(G4_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------------------
+// TMA tensor maps (driver entry point fetched through the runtime, no -lcuda needed)
+// ---------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// bf16 tensor viewed as (D, H, S, B) with a (64, 1, rows, 1) box, 128-B swizzle.
+int make_map(CUtensorMap* map, const void* ptr, int64_t d, int64_t h, int64_t s, int64_t b,
+             int64_t stride_h, int64_t stride_s, int64_t stride_b, int rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(G4_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (b <= 1) stride_b = stride_s * (s > 0 ? s : 1);
+  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)h, (cuuint64_t)(s > 0 ? s : 1),
+                        (cuuint64_t)(b > 0 ? b : 1)};
+  cuuint64_t strides[3] = {(cuuint64_t)(stride_h * 2), (cuuint64_t)(stride_s * 2),
+                           (cuuint64_t)(stride_b * 2)};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(G4_ERR_INVALID, "tensor map encoding failed (CUresult %d)", (int)r);
+  return G4_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// argument checks shared by forward and backward
+// ---------------------------------------------------------------------------------------
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_strides(const int64_t* st, const char* name, bool packed) {
+  for (int i = packed ? 1 : 0; i < 3; ++i)
+    if (st[i] <= 0 || (st[i] % 8) != 0)
+      return fail(G4_ERR_INVALID, "%s strides must be positive multiples of 8 elements", name);
+  return G4_OK;
+}
+
+int check_common(const g4_attn_args* a) {
+  if (!a) return fail(G4_ERR_INVALID, "null argument block");
+  const bool packed = a->cu_seqlens_q != nullptr;
+  if ((a->cu_seqlens_k != nullptr) != packed)
+    return fail(G4_ERR_INVALID, "cu_seqlens_q and cu_seqlens_k must both be set or both be null");
+  if (!a->q || !a->k || !a->v || !a->o || !a->lse)
+    return fail(G4_ERR_INVALID, "q, k, v, o and lse are required");
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o))
+    return fail(G4_ERR_INVALID, "q, k, v and o base pointers must be 16-byte aligned");
+  if (a->k == a->v) return fail(G4_ERR_INVALID, "K and V must be distinct operands");
+  if (a->batch <= 0 || a->seqlen_q <= 0 || a->seqlen_k <= 0)
+    return fail(G4_ERR_INVALID, "batch and sequence lengths must be positive");
+  if (!packed && a->seqlen_q > a->seqlen_k)
+    return fail(G4_ERR_UNSUPPORTED, "fixed layout requires Sq <= Sk");
+  if (a->num_kv_heads <= 0 || a->num_q_heads <= 0 || a->num_q_heads % a->num_kv_heads)
+    return fail(G4_ERR_INVALID, "query heads must be a positive multiple of KV heads");
+  if (a->head_dim_qk != a->head_dim_v || (a->head_dim_qk != 256 && a->head_dim_qk != 512))
+    return fail(G4_ERR_UNSUPPORTED, "head dims must be (256,256) or (512,512)");
+  if (a->window < 0) return fail(G4_ERR_INVALID, "window must be >= 0");
+  if (a->window == 0 && (a->vision_ids || a->document_ids))
+    return fail(G4_ERR_UNSUPPORTED, "vision/document metadata applies to local layers only");
+  int rc;
+  if ((rc = check_strides(a->q_stride, "q", packed))) return rc;
+  if ((rc = check_strides(a->k_stride, "k", packed))) return rc;
+  if ((rc = check_strides(a->v_stride, "v", packed))) return rc;
+  if ((rc = check_strides(a->o_stride, "o", packed))) return rc;
+  if (packed && (a->max_seqlen_q <= 0 || a->max_seqlen_k <= 0 || a->max_seqlen_q > a->max_seqlen_k))
+    return fail(G4_ERR_UNSUPPORTED, "packed maxima must satisfy 1 <= max Sq <= max Sk");
+  return G4_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// workspace layout
+// ---------------------------------------------------------------------------------------
+struct Workspace {
+  size_t header = 0;       // int err, n_q_tiles, n_k_tiles
+  size_t q_tiles = 0;      // int2[max_q_tiles]
+  size_t k_tiles = 0;      // int2[max_k_tiles]
+  size_t pair_last = 0;    // int[meta_len]
+  size_t delta = 0;        // float[Hq * tokens_q]
+  size_t lse2 = 0;         // float[Hq * tokens_q]
+  size_t total = 0;
+  int max_q_tiles = 0;
+  int max_k_tiles = 0;
+  int64_t tokens_q = 0;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+Workspace plan_workspace(const g4_attn_args* a, bool backward) {
+  Workspace w;
+  const bool packed = a->cu_seqlens_q != nullptr;
+  size_t off = 256;
+  if (packed) {
+    w.max_q_tiles = a->seqlen_q / g4::kTileM + a->batch + 1;
+    w.q_tiles = off;
+    off = align256(off + sizeof(int2) * w.max_q_tiles);
+    if (backward) {
+      w.max_k_tiles = a->seqlen_k / g4::kTileN + a->batch + 1;
+      w.k_tiles = off;
+      off = align256(off + sizeof(int2) * w.max_k_tiles);
+    }
+  }
+  if (a->vision_ids && a->window > 0) {
+    const int64_t meta_len = packed ? a->seqlen_k : int64_t(a->batch) * a->seqlen_k;
+    w.pair_last = off;
+    off = align256(off + sizeof(int) * meta_len);
+  }
+  if (backward) {
+    w.tokens_q = packed ? a->seqlen_q : int64_t(a->batch) * a->seqlen_q;
+    w.delta = off;
+    off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
+    w.lse2 = off;
+    off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
+  }
+  w.total = off;
+  return w;
+}
+
+template <typename T>
+T* ws_ptr(const g4_attn_args* a, size_t off) {
+  return reinterpret_cast<T*>(static_cast<uint8_t*>(a->workspace) + off);
+}
+
+g4::SeqLayout make_layout(const g4_attn_args* a) {
+  g4::SeqLayout l;
+  l.batch = a->batch;
+  l.seqlen_q = a->seqlen_q;
+  l.seqlen_k = a->seqlen_k;
+  l.cu_q = a->cu_seqlens_q;
+  l.cu_k = a->cu_seqlens_k;
+  l.meta_stride = a->seqlen_k;
+  return l;
+}
+
+// Common prologue: zero the header, plan packed tiles and metadata bounds.
+int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream_t st,
+            g4::MaskSpec* mask) {
+  if (!a->workspace || a->workspace_bytes < w.total)
+    return fail(G4_ERR_WORKSPACE, "workspace of %zu bytes required", w.total);
+  cudaError_t e = cudaMemsetAsync(a->workspace, 0, 256, st);
+  if (e != cudaSuccess) return cuda_fail(e, "workspace reset");
+  const g4::SeqLayout layout = make_layout(a);
+  int* hdr = ws_ptr<int>(a, 0);
+  if (a->cu_seqlens_q) {
+    int rc = g4::launch_plan_tiles(a->cu_seqlens_q, a->batch, g4::kTileM,
+                                   ws_ptr<int2>(a, w.q_tiles), hdr + 1, st);
+    if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "q tile planning");
+    if (backward) {
+      rc = g4::launch_plan_tiles(a->cu_seqlens_k, a->batch, g4::kTileN,
+                                 ws_ptr<int2>(a, w.k_tiles), hdr + 2, st);
+      if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "k tile planning");
+    }
+  }
+  mask->window = a->window;
+  mask->vis = a->window > 0 ? a->vision_ids : nullptr;
+  mask->doc = a->window > 0 ? a->document_ids : nullptr;
+  mask->pair_last = nullptr;
+  if (w.pair_last) {
+    int* pl = ws_ptr<int>(a, w.pair_last);
+    int rc = g4::launch_pair_last(layout, a->vision_ids, a->document_ids, pl, a->batch, st);
+    if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "vision pair planning");
+    mask->pair_last = pl;
+  }
+  return G4_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int g4_abi_version(void) { return G4_ABI_VERSION; }
+
+const char* g4_last_error(void) { return g_last_error.c_str(); }
+
+size_t g4_attn_fwd_workspace_bytes(const g4_attn_args* args) {
+  if (!args) return 0;
+  return plan_workspace(args, false).total;
+}
+
+size_t g4_attn_bwd_workspace_bytes(const g4_attn_args* args) {
+  if (!args) return 0;
+  return plan_workspace(args, true).total;
+}
+
+int g4_attn_fwd(const g4_attn_args* a, void* stream) {
+  g_last_error.clear();
+  int rc = check_common(a);
+  if (rc) return rc;
+  const bool packed = a->cu_seqlens_q != nullptr;
+  if (!packed && (a->lse_stride[0] <= 0 || a->lse_stride[1] <= 0))
+    return fail(G4_ERR_INVALID, "lse strides must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Workspace w = plan_workspace(a, false);
+  g4::FwdParams p;
+  memset(&p, 0, sizeof(p));
+  if ((rc = prepare(a, w, false, st, &p.mask))) return rc;
+  p.layout = make_layout(a);
+  p.group = a->num_q_heads / a->num_kv_heads;
+  p.o = static_cast<__nv_bfloat16*>(a->o);
+  for (int i = 0; i < 3; ++i) p.o_stride[i] = a->o_stride[i];
+  p.lse = a->lse;
+  p.lse_stride[0] = packed ? 0 : a->lse_stride[0];
+  p.lse_stride[1] = packed ? a->seqlen_q : a->lse_stride[1];
+  p.err = ws_ptr<int>(a, 0);
+  if (packed) {
+    p.tiles = ws_ptr<int2>(a, w.q_tiles);
+    p.n_tiles = ws_ptr<int>(a, 0) + 1;
+  }
+  const int D = a->head_dim_qk;
+  const int64_t bq = packed ? 1 : a->batch;
+  CUtensorMap tq, tk, tv;
+  if ((rc = make_map(&tq, a->q, D, a->num_q_heads, a->seqlen_q, bq, a->q_stride[2], a->q_stride[1],
+                     a->q_stride[0], 128)))
+    return rc;
+  if ((rc = make_map(&tk, a->k, D, a->num_kv_heads, a->seqlen_k, bq, a->k_stride[2],
+                     a->k_stride[1], a->k_stride[0], 128)))
+    return rc;
+  if ((rc = make_map(&tv, a->v, a->head_dim_v, a->num_kv_heads, a->seqlen_k, bq, a->v_stride[2],
+                     a->v_stride[1], a->v_stride[0], 64)))
+    return rc;
+  const int grid_x = packed ? w.max_q_tiles
+                            : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
+  const int slabs = a->head_dim_v / 256;
+  int e = D == 256 ? g4::launch_fwd<256>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st)
+                   : g4::launch_fwd<512>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st);
+  if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward launch");
+  return G4_OK;
+}
+
+int g4_read_device_error(const void* workspace, int* code, void* stream) {
+  if (!workspace || !code) return fail(G4_ERR_INVALID, "workspace and code are required");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+  e = cudaMemcpy(code, workspace, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "error word read");
+  return G4_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,76 @@
+// Internal launch interface between the C-ABI layer (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "g4_attn.cuh"
+
+namespace g4 {
+
+struct FwdParams {
+  SeqLayout layout;
+  MaskSpec mask;
+  int group;                       // query heads per KV head
+  __nv_bfloat16* o;
+  int64_t o_stride[3];             // batch, token, head (elements)
+  float* lse;
+  int64_t lse_stride[2];           // batch, head (floats); token stride 1
+  const int2* tiles;               // packed: (segment, q tile) work list, else null
+  const int* n_tiles;
+  int* err;                        // device error word
+};
+
+struct BwdParams {
+  SeqLayout layout;
+  MaskSpec mask;
+  int group;
+  int num_q_heads;
+  const __nv_bfloat16* o;
+  int64_t o_stride[3];
+  const __nv_bfloat16* dout;
+  int64_t do_stride[3];
+  const float* lse;                // natural-log LSE from the forward
+  int64_t lse_stride[2];
+  const float* dlse;               // nullable, same layout as lse
+  float* delta;                    // workspace: rowsum(dO*O) - dLSE, [head][token]
+  float* lse2;                     // workspace: LSE * log2(e), [head][token]
+  int64_t ws_head_stride;          // token count of the workspace rows
+  __nv_bfloat16* dq;
+  int64_t dq_stride[3];
+  __nv_bfloat16* dk;
+  int64_t dk_stride[3];
+  __nv_bfloat16* dv;
+  int64_t dv_stride[3];
+  const int2* q_tiles;             // packed: (segment, q tile) work list
+  const int* n_q_tiles;
+  const int2* k_tiles;             // packed: (segment, k tile) work list
+  const int* n_k_tiles;
+  int* err;
+};
+
+template <int DQK>
+int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+               const FwdParams& p, int grid_x, int num_q_heads, int slabs, cudaStream_t stream);
+
+int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int grid_tokens, cudaStream_t stream);
+
+template <int D>
+int launch_bwd_dq(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                  const CUtensorMap& tdo, const BwdParams& p, int grid_x, int slabs,
+                  cudaStream_t stream);
+
+template <int D>
+int launch_bwd_dkv(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tq,
+                   const CUtensorMap& tdo, const BwdParams& p, int grid_x, int num_kv_heads,
+                   int slabs, cudaStream_t stream);
+
+// planning kernels (plan.cu)
+int launch_plan_tiles(const int* cu, int nseg, int tile, int2* tiles, int* n_tiles,
+                      cudaStream_t stream);
+int launch_pair_last(const SeqLayout& layout, const int* vis, const int* doc, int* pair_last,
+                     int nseq, cudaStream_t stream);
+
+}  // namespace g4

@@ -1,0 +1,153 @@
+"""Low-level operators: torch tensors in, C-ABI call, torch tensors out.
+
+These functions do only what the native boundary needs (pointer/stride
+marshalling, output and workspace allocation on the caller's stream, status
+to exception mapping).  Contract validation that the reference performs in its
+adapters lives in ``adapters.py``.  Every call runs on the current CUDA
+stream; nothing here synchronises the host.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .errors import UnsupportedB200Path
+
+
+def _raise_for(status: int, what: str) -> None:
+    if status == _lib.G4_OK:
+        return
+    msg = f"{what}: {_lib.last_error()}"
+    if status == _lib.G4_ERR_INVALID:
+        raise ValueError(msg)
+    if status == _lib.G4_ERR_UNSUPPORTED:
+        raise UnsupportedB200Path(msg)
+    raise RuntimeError(msg)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _strides3(t: torch.Tensor, packed: bool):
+    arr = (ctypes.c_int64 * 3)()
+    if packed:  # (T, H, D)
+        arr[0], arr[1], arr[2] = 0, t.stride(0), t.stride(1)
+    else:  # (B, S, H, D)
+        arr[0], arr[1], arr[2] = t.stride(0), t.stride(1), t.stride(2)
+    return arr
+
+
+def _meta(x: torch.Tensor | None, device) -> torch.Tensor | None:
+    if x is None:
+        return None
+    if x.device != device:
+        raise ValueError("metadata must be on the operand device")
+    return x.to(torch.int32).contiguous()
+
+
+def _build_args(q, k, v, o, lse, *, window, vision_ids, document_ids, cu_seqlens_q,
+                cu_seqlens_k, max_seqlen_q, max_seqlen_k):
+    packed = cu_seqlens_q is not None
+    a = _lib.G4AttnArgs()
+    a.q, a.k, a.v, a.o, a.lse = _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse)
+    a.q_stride = _strides3(q, packed)
+    a.k_stride = _strides3(k, packed)
+    a.v_stride = _strides3(v, packed)
+    a.o_stride = _strides3(o, packed)
+    if packed:
+        a.batch = cu_seqlens_q.numel() - 1
+        a.seqlen_q, a.seqlen_k = q.shape[0], k.shape[0]
+        a.cu_seqlens_q, a.cu_seqlens_k = _ptr(cu_seqlens_q), _ptr(cu_seqlens_k)
+        a.max_seqlen_q, a.max_seqlen_k = int(max_seqlen_q), int(max_seqlen_k)
+        a.num_q_heads, a.num_kv_heads = q.shape[1], k.shape[1]
+        a.lse_stride[0], a.lse_stride[1] = 0, lse.stride(0)
+    else:
+        a.batch, a.seqlen_q, a.seqlen_k = q.shape[0], q.shape[1], k.shape[1]
+        a.num_q_heads, a.num_kv_heads = q.shape[2], k.shape[2]
+        a.lse_stride[0], a.lse_stride[1] = lse.stride(0), lse.stride(1)
+    a.head_dim_qk, a.head_dim_v = q.shape[-1], v.shape[-1]
+    a.window = int(window or 0)
+    a.vision_ids, a.document_ids = _ptr(vision_ids), _ptr(document_ids)
+    return a
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def attn_fwd(q, k, v, *, window=0, vision_ids=None, document_ids=None, cu_seqlens_q=None,
+             cu_seqlens_k=None, max_seqlen_q=None, max_seqlen_k=None, out=None):
+    """Forward through ``g4_attn_fwd``.  Fixed BSHD (4-D) or packed THD (3-D)
+    inputs; returns ``(out, lse)`` with LSE ``(B,Hq,Sq)`` or ``(Hq,Tq)``."""
+    lib = _lib.load()
+    packed = cu_seqlens_q is not None
+    dev = q.device
+    if out is None:
+        out = torch.empty(*q.shape[:-1], v.shape[-1], dtype=q.dtype, device=dev)
+    if packed:
+        lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=dev)
+    else:
+        lse = torch.empty(q.shape[0], q.shape[2], q.shape[1], dtype=torch.float32, device=dev)
+    vis, doc = _meta(vision_ids, dev), _meta(document_ids, dev)
+    a = _build_args(q, k, v, out, lse, window=window, vision_ids=vis, document_ids=doc,
+                    cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
+                    max_seqlen_q=max_seqlen_q, max_seqlen_k=max_seqlen_k)
+    ws = _workspace(lib.g4_attn_fwd_workspace_bytes(ctypes.byref(a)), dev)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    _raise_for(lib.g4_attn_fwd(ctypes.byref(a), _stream(dev)), "g4_attn_fwd")
+    return out, lse
+
+
+def attn_bwd(q, k, v, out, lse, dout, *, dlse=None, window=0, vision_ids=None,
+             document_ids=None, cu_seqlens_q=None, cu_seqlens_k=None, max_seqlen_q=None,
+             max_seqlen_k=None, dq=None, dk=None, dv=None):
+    """Backward through ``g4_attn_bwd``; returns ``(dq, dk, dv)``."""
+    lib = _lib.load()
+    packed = cu_seqlens_q is not None
+    dev = q.device
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(k) if dk is None else dk
+    dv = torch.empty_like(v) if dv is None else dv
+    vis, doc = _meta(vision_ids, dev), _meta(document_ids, dev)
+    a = _build_args(q, k, v, out, lse, window=window, vision_ids=vis, document_ids=doc,
+                    cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
+                    max_seqlen_q=max_seqlen_q, max_seqlen_k=max_seqlen_k)
+    if dout.stride(-1) != 1:
+        dout = dout.contiguous()
+    a.dout = _ptr(dout)
+    if dlse is not None:
+        dlse = dlse.to(torch.float32).contiguous()
+        if dlse.shape != lse.shape:
+            raise ValueError("dlse must match the LSE shape")
+        a.dlse = _ptr(dlse)
+    a.do_stride = _strides3(dout, packed)
+    a.dq, a.dk, a.dv = _ptr(dq), _ptr(dk), _ptr(dv)
+    a.dq_stride = _strides3(dq, packed)
+    a.dk_stride = _strides3(dk, packed)
+    a.dv_stride = _strides3(dv, packed)
+    ws = _workspace(lib.g4_attn_bwd_workspace_bytes(ctypes.byref(a)), dev)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    _raise_for(lib.g4_attn_bwd(ctypes.byref(a), _stream(dev)), "g4_attn_bwd")
+    return dq, dk, dv
+
+
+def build_mask(batch, q_len, kv_len, *, window, allow_vision_bidirectional, vision_ids=None,
+               document_ids=None, key_padding_mask=None, device):
+    """Dense ``(B, Q, K)`` uint8 mask from ``g4_build_mask``."""
+    lib = _lib.load()
+    out = torch.empty(batch, q_len, kv_len, dtype=torch.uint8, device=device)
+    vis, doc = _meta(vision_ids, device), _meta(document_ids, device)
+    pad = None if key_padding_mask is None else key_padding_mask.to(torch.uint8).contiguous()
+    rc = lib.g4_build_mask(_ptr(out), batch, q_len, kv_len, int(window or 0),
+                           int(bool(allow_vision_bidirectional)), _ptr(vis), _ptr(doc), _ptr(pad),
+                           _stream(device))
+    _raise_for(rc, "g4_build_mask")
+    return out

@@ -1,0 +1,149 @@
+/*
+ * gemma4_b200.h -- C ABI of the B200 (sm_100a) Gemma-4 attention library
+ * (libgemma4_b200.so).
+ *
+ * The reference project reaches its GPU kernels through the FlashAttention-4
+ * CuTe-DSL Python interface; these entry points are the native boundary that
+ * replaces those calls.  Each declaration names the reference call site it
+ * stands in for (paths inside amazingvince/gemma4-fa4-kernels).
+ *
+ * Conventions
+ *  - All tensors are device pointers owned by the caller; the library never
+ *    allocates or frees caller memory.  Scratch memory is passed in as
+ *    `workspace` (size from the matching *_workspace_bytes query).
+ *  - Q/K/V/O and gradients are bf16 with unit stride along the head dimension;
+ *    the other strides are in elements and must be multiples of 8 (16 bytes),
+ *    base pointers 16-byte aligned.  LSE/dLSE are fp32 natural-log values.
+ *  - Fixed layout (cu_seqlens_q == NULL): Q (B,Sq,Hq,D), K/V (B,Sk,Hkv,D),
+ *    LSE (B,Hq,Sq).  Packed layout: Q (Tq,Hq,D), K/V (Tk,Hkv,D), LSE (Hq,Tq),
+ *    cu_seqlens int32 (B+1); each query segment is the lower-right suffix of
+ *    its key segment.
+ *  - softmax scale is exactly 1.0.  window == 0 selects the global causal mask;
+ *    window > 0 the local mask  k > q-W AND (k <= q OR same vision id >= 0)
+ *    AND same document id (vision/document ids follow the K stream).
+ *  - Calls are asynchronous on `stream` (a cudaStream_t, NULL = legacy default)
+ *    and return G4_OK or an error code; g4_last_error() describes the last
+ *    failure of the calling thread.  All argument checks happen before any
+ *    launch.
+ */
+#ifndef GEMMA4_B200_H_
+#define GEMMA4_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define G4_ABI_VERSION 1
+
+enum g4_status {
+  G4_OK = 0,
+  G4_ERR_INVALID = 1,     /* malformed arguments (reference: ValueError) */
+  G4_ERR_UNSUPPORTED = 2, /* outside the supported contract (reference: UnsupportedH100Path) */
+  G4_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  G4_ERR_DEVICE = 4,      /* a kernel reported a device-side failure (bounded wait expired) */
+  G4_ERR_WORKSPACE = 5    /* workspace missing or too small */
+};
+
+typedef struct g4_attn_args {
+  /* forward operands */
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;          /* forward output; backward input */
+  float* lse;       /* forward output; backward input */
+  /* backward operands (ignored by the forward) */
+  const void* dout;
+  const float* dlse; /* nullable: gradient w.r.t. LSE */
+  void* dq;
+  void* dk;
+  void* dv;
+  /* strides in elements: [batch, token, head]; batch ignored for packed */
+  int64_t q_stride[3];
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int64_t do_stride[3];
+  int64_t dq_stride[3];
+  int64_t dk_stride[3];
+  int64_t dv_stride[3];
+  int64_t lse_stride[2]; /* [batch, head] in floats; token stride is 1 */
+  /* geometry */
+  int32_t batch;        /* fixed: B; packed: number of segments */
+  int32_t seqlen_q;     /* fixed: Sq; packed: total Tq */
+  int32_t seqlen_k;     /* fixed: Sk; packed: total Tk */
+  const int32_t* cu_seqlens_q; /* packed only, device, B+1 entries */
+  const int32_t* cu_seqlens_k;
+  int32_t max_seqlen_q; /* packed: maxima of the segment lengths */
+  int32_t max_seqlen_k;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim_qk;  /* 256 (local) or 512 (global) */
+  int32_t head_dim_v;   /* equal to head_dim_qk */
+  int32_t window;       /* 0 = global causal; > 0 = sliding window W */
+  /* contiguous int32 metadata along the K stream: fixed (B,Sk), packed (Tk,); nullable */
+  const int32_t* vision_ids;
+  const int32_t* document_ids;
+  /* scratch */
+  void* workspace;
+  size_t workspace_bytes;
+} g4_attn_args;
+
+/* ABI version of the loaded library (G4_ABI_VERSION). */
+int g4_abi_version(void);
+
+/* Description of the last failure on the calling thread ("" if none). */
+const char* g4_last_error(void);
+
+/* Workspace bytes g4_attn_fwd needs for these arguments (no device access). */
+size_t g4_attn_fwd_workspace_bytes(const g4_attn_args* args);
+
+/*
+ * Attention forward: O and LSE.
+ * Replaces the FA4 forward launches of src/gemma4_fa4/h100.py:
+ *   flash_attn_func (fa4_local_text_forward :766-778, fa4_local_forward :800-815,
+ *   fa4_global_forward_only :1013-1036, _FA4GlobalTextFunction.forward :1352-1386)
+ *   flash_attn_varlen_func (fa4_local_varlen_forward :864-910,
+ *   _run_global_varlen_slabs :1174-1190).
+ * The global d512 output is produced in one launch, not two V256 slab calls.
+ */
+int g4_attn_fwd(const g4_attn_args* args, void* stream);
+
+/* Workspace bytes g4_attn_bwd needs for these arguments (no device access). */
+size_t g4_attn_bwd_workspace_bytes(const g4_attn_args* args);
+
+/*
+ * Attention backward: dQ, dK, dV from (Q, K, V, O, LSE, dO[, dLSE]).
+ * Replaces FA4's autograd backward for the local adapters (h100.py:766-910)
+ * and flash_attn.cute.interface._flash_attn_bwd_gemma4_global_d512
+ * (patches/flash-attention/0002-...patch:1021-1512, called from
+ * h100.py:1304-1317 and :1389-1394).  dQ/dK/dV are fully overwritten;
+ * keys no query attends to receive exact zeros.
+ */
+int g4_attn_bwd(const g4_attn_args* args, void* stream);
+
+/*
+ * Synchronise `stream` and read the device error word of a workspace used by
+ * a previous call; *code receives 0 or a G4 device error (1 = TMA wait
+ * expired, 2 = MMA wait expired, 3 = role hand-off wait expired).
+ */
+int g4_read_device_error(const void* workspace, int* code, void* stream);
+
+/*
+ * Dense Gemma-4 mask builder: writes out[b][q][k] = 1 if allowed, else 0
+ * (uint8, (B,Sq,Sk) contiguous), with lower-right query alignment.
+ * Replaces src/gemma4_fa4/masks.py:8-80 (gemma4_attention_mask) for the
+ * sliding (window > 0, vision bidirectional) and global (window == 0) layers;
+ * vision/document ids and key padding (uint8, nullable) are (B,Sk) contiguous.
+ */
+int g4_build_mask(uint8_t* out, int32_t batch, int32_t q_len, int32_t kv_len, int32_t window,
+                  int32_t allow_vision_bidirectional, const int32_t* vision_ids,
+                  const int32_t* document_ids, const uint8_t* key_padding, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GEMMA4_B200_H_ */
