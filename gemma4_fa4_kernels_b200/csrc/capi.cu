@@ -122,6 +122,7 @@ struct Workspace {
   size_t q_tiles = 0;      // int2[max_q_tiles]
   size_t k_tiles = 0;      // int2[max_k_tiles]
   size_t pair_last = 0;    // int[meta_len]
+  size_t pair_first = 0;   // int[meta_len] (backward)
   size_t delta = 0;        // float[Hq * tokens_q]
   size_t lse2 = 0;         // float[Hq * tokens_q]
   size_t total = 0;
@@ -150,6 +151,10 @@ Workspace plan_workspace(const g4_attn_args* a, bool backward) {
     const int64_t meta_len = packed ? a->seqlen_k : int64_t(a->batch) * a->seqlen_k;
     w.pair_last = off;
     off = align256(off + sizeof(int) * meta_len);
+    if (backward) {
+      w.pair_first = off;
+      off = align256(off + sizeof(int) * meta_len);
+    }
   }
   if (backward) {
     w.tokens_q = packed ? a->seqlen_q : int64_t(a->batch) * a->seqlen_q;
@@ -201,11 +206,14 @@ int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream
   mask->vis = a->window > 0 ? a->vision_ids : nullptr;
   mask->doc = a->window > 0 ? a->document_ids : nullptr;
   mask->pair_last = nullptr;
+  mask->pair_first = nullptr;
   if (w.pair_last) {
     int* pl = ws_ptr<int>(a, w.pair_last);
-    int rc = g4::launch_pair_last(layout, a->vision_ids, a->document_ids, pl, a->batch, st);
+    int* pf = w.pair_first ? ws_ptr<int>(a, w.pair_first) : nullptr;
+    int rc = g4::launch_pair_last(layout, a->vision_ids, a->document_ids, pl, pf, a->batch, st);
     if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "vision pair planning");
     mask->pair_last = pl;
+    mask->pair_first = pf;
   }
   return G4_OK;
 }
@@ -270,6 +278,86 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
   int e = D == 256 ? g4::launch_fwd<256>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st)
                    : g4::launch_fwd<512>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st);
   if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward launch");
+  return G4_OK;
+}
+
+int g4_attn_bwd(const g4_attn_args* a, void* stream) {
+  g_last_error.clear();
+  int rc = check_common(a);
+  if (rc) return rc;
+  const bool packed = a->cu_seqlens_q != nullptr;
+  if (!a->dout || !a->dq || !a->dk || !a->dv)
+    return fail(G4_ERR_INVALID, "dout, dq, dk and dv are required");
+  if (!aligned16(a->dout) || !aligned16(a->dq) || !aligned16(a->dk) || !aligned16(a->dv))
+    return fail(G4_ERR_INVALID, "dout, dq, dk and dv base pointers must be 16-byte aligned");
+  if ((rc = check_strides(a->do_stride, "dout", packed))) return rc;
+  if ((rc = check_strides(a->dq_stride, "dq", packed))) return rc;
+  if ((rc = check_strides(a->dk_stride, "dk", packed))) return rc;
+  if ((rc = check_strides(a->dv_stride, "dv", packed))) return rc;
+  if (!packed && (a->lse_stride[0] <= 0 || a->lse_stride[1] <= 0))
+    return fail(G4_ERR_INVALID, "lse strides must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Workspace w = plan_workspace(a, true);
+  g4::BwdParams p;
+  memset(&p, 0, sizeof(p));
+  if ((rc = prepare(a, w, true, st, &p.mask))) return rc;
+  p.layout = make_layout(a);
+  p.group = a->num_q_heads / a->num_kv_heads;
+  p.num_q_heads = a->num_q_heads;
+  p.o = static_cast<const __nv_bfloat16*>(a->o);
+  p.dout = static_cast<const __nv_bfloat16*>(a->dout);
+  p.dq = static_cast<__nv_bfloat16*>(a->dq);
+  p.dk = static_cast<__nv_bfloat16*>(a->dk);
+  p.dv = static_cast<__nv_bfloat16*>(a->dv);
+  for (int i = 0; i < 3; ++i) {
+    p.o_stride[i] = a->o_stride[i];
+    p.do_stride[i] = a->do_stride[i];
+    p.dq_stride[i] = a->dq_stride[i];
+    p.dk_stride[i] = a->dk_stride[i];
+    p.dv_stride[i] = a->dv_stride[i];
+  }
+  p.lse = a->lse;
+  p.dlse = a->dlse;
+  p.lse_stride[0] = packed ? 0 : a->lse_stride[0];
+  p.lse_stride[1] = packed ? a->seqlen_q : a->lse_stride[1];
+  p.delta = ws_ptr<float>(a, w.delta);
+  p.lse2 = ws_ptr<float>(a, w.lse2);
+  p.ws_head_stride = w.tokens_q;
+  p.err = ws_ptr<int>(a, 0);
+  if (packed) {
+    p.q_tiles = ws_ptr<int2>(a, w.q_tiles);
+    p.n_q_tiles = ws_ptr<int>(a, 0) + 1;
+    p.k_tiles = ws_ptr<int2>(a, w.k_tiles);
+    p.n_k_tiles = ws_ptr<int>(a, 0) + 2;
+  }
+  int e = g4::launch_bwd_preprocess(p, a->head_dim_v, w.tokens_q, st);
+  if (e) return cuda_fail(static_cast<cudaError_t>(e), "backward preprocess launch");
+  const int D = a->head_dim_qk;
+  const int64_t bq = packed ? 1 : a->batch;
+  CUtensorMap tq, tk, tk64, tv, tdo;
+  if ((rc = make_map(&tq, a->q, D, a->num_q_heads, a->seqlen_q, bq, a->q_stride[2], a->q_stride[1],
+                     a->q_stride[0], 128)))
+    return rc;
+  if ((rc = make_map(&tk, a->k, D, a->num_kv_heads, a->seqlen_k, bq, a->k_stride[2],
+                     a->k_stride[1], a->k_stride[0], 128)))
+    return rc;
+  if ((rc = make_map(&tk64, a->k, D, a->num_kv_heads, a->seqlen_k, bq, a->k_stride[2],
+                     a->k_stride[1], a->k_stride[0], 64)))
+    return rc;
+  if ((rc = make_map(&tv, a->v, a->head_dim_v, a->num_kv_heads, a->seqlen_k, bq, a->v_stride[2],
+                     a->v_stride[1], a->v_stride[0], 128)))
+    return rc;
+  if ((rc = make_map(&tdo, a->dout, a->head_dim_v, a->num_q_heads, a->seqlen_q, bq,
+                     a->do_stride[2], a->do_stride[1], a->do_stride[0], 128)))
+    return rc;
+  const int gq = packed ? w.max_q_tiles : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
+  const int gk = packed ? w.max_k_tiles : a->batch * ((a->seqlen_k + g4::kTileN - 1) / g4::kTileN);
+  e = D == 256 ? g4::launch_bwd_dq<256>(tq, tk, tk64, tv, tdo, p, gq, st)
+               : g4::launch_bwd_dq<512>(tq, tk, tk64, tv, tdo, p, gq, st);
+  if (e) return cuda_fail(static_cast<cudaError_t>(e), "dQ launch");
+  e = D == 256 ? g4::launch_bwd_dkv<256>(tq, tk, tv, tdo, p, gk, st)
+               : g4::launch_bwd_dkv<512>(tq, tk, tv, tdo, p, gk, st);
+  if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK/dV launch");
   return G4_OK;
 }
 

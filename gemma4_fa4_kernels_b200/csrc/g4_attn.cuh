@@ -66,6 +66,7 @@ struct MaskSpec {
   const int* vis;            // nullable
   const int* doc;            // nullable
   const int* pair_last;      // nullable: last key with the same (doc, vis) pair (sequence-local)
+  const int* pair_first;     // nullable: first position with the same pair (backward only)
 
   __device__ __forceinline__ bool has_meta() const { return vis != nullptr || doc != nullptr; }
 };

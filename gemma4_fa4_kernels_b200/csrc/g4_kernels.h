@@ -55,22 +55,25 @@ template <int DQK>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                const FwdParams& p, int grid_x, int num_q_heads, int slabs, cudaStream_t stream);
 
-int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int grid_tokens, cudaStream_t stream);
+int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int64_t tokens_q,
+                          cudaStream_t stream);
 
+// dQ: grid (grid_x query tiles, Hq, D/256 slabs).  Maps: Q/K/V/dO with 128-row
+// boxes and K with 64-row boxes.
 template <int D>
-int launch_bwd_dq(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                  const CUtensorMap& tdo, const BwdParams& p, int grid_x, int slabs,
+int launch_bwd_dq(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tk64,
+                  const CUtensorMap& tv, const CUtensorMap& tdo, const BwdParams& p, int grid_x,
                   cudaStream_t stream);
 
+// dK/dV: grid (grid_x key tiles, Hkv, D/128 slabs).  Maps with 128-row boxes.
 template <int D>
-int launch_bwd_dkv(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tq,
-                   const CUtensorMap& tdo, const BwdParams& p, int grid_x, int num_kv_heads,
-                   int slabs, cudaStream_t stream);
+int launch_bwd_dkv(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                   const CUtensorMap& tdo, const BwdParams& p, int grid_x, cudaStream_t stream);
 
 // planning kernels (plan.cu)
 int launch_plan_tiles(const int* cu, int nseg, int tile, int2* tiles, int* n_tiles,
                       cudaStream_t stream);
 int launch_pair_last(const SeqLayout& layout, const int* vis, const int* doc, int* pair_last,
-                     int nseq, cudaStream_t stream);
+                     int* pair_first, int nseq, cudaStream_t stream);
 
 }  // namespace g4

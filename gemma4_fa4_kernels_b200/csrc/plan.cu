@@ -3,11 +3,13 @@
 // * plan_tiles: turns cu_seqlens into a compact (segment, tile) work list so
 //   that a fixed-size grid (an upper bound known on the host without reading
 //   cu_seqlens) covers every tile of every segment; no host synchronisation.
-// * pair_last: for every key with a non-negative vision id, the last key of
-//   the same sequence carrying the same (document, vision) pair.  A query's
-//   allowed keys extend rightwards exactly to that key (the vision exception
-//   has no right window cap, reference masks.py:55-66), so it bounds the key
-//   tiles a query tile visits.  The reference builds the equivalent
+// * pair_last / pair_first: for every position with a non-negative vision id,
+//   the last / first position of the same sequence carrying the same
+//   (document, vision) pair.  A query's allowed keys extend rightwards exactly
+//   to pair_last (the vision exception has no right window cap, reference
+//   masks.py:55-66), which bounds the key tiles a query tile visits; a key is
+//   seen by earlier queries down to pair_first, which bounds the query tiles
+//   a key tile visits in the backward pass.  The reference builds the equivalent
 //   information on the host per segment (sparse_schedule.py:146-178, the
 //   pair_blocks index); here one CTA per sequence uses a shared-memory hash
 //   table.  If the table overflows, the bound falls back to the sequence end,
@@ -64,14 +66,17 @@ __device__ __forceinline__ unsigned hash_key(unsigned long long key) {
 }
 
 __global__ void pair_last_kernel(SeqLayout layout, const int* __restrict__ vis,
-                                 const int* __restrict__ doc, int* __restrict__ pair_last) {
+                                 const int* __restrict__ doc, int* __restrict__ pair_last,
+                                 int* __restrict__ pair_first) {
   __shared__ unsigned long long keys[kHashCap];
   __shared__ int last[kHashCap];
+  __shared__ int first[kHashCap];
   __shared__ int overflow;
   const SeqInfo si = layout.seq(blockIdx.x);
   for (int i = threadIdx.x; i < kHashCap; i += blockDim.x) {
     keys[i] = kHashEmpty;
     last[i] = -1;
+    first[i] = 0x7fffffff;
   }
   if (threadIdx.x == 0) overflow = 0;
   __syncthreads();
@@ -88,6 +93,7 @@ __global__ void pair_last_kernel(SeqLayout layout, const int* __restrict__ vis,
       const unsigned long long prev = atomicCAS(&keys[h], kHashEmpty, key);
       if (prev == kHashEmpty || prev == key) {
         atomicMax(&last[h], k);
+        atomicMin(&first[h], k);
         placed = true;
         break;
       }
@@ -98,10 +104,11 @@ __global__ void pair_last_kernel(SeqLayout layout, const int* __restrict__ vis,
   __syncthreads();
   for (int k = threadIdx.x; k < si.len_k; k += blockDim.x) {
     const int v = vis[si.meta_base + k];
-    int out = k;
+    int out = k, out_first = k;
     if (v >= 0) {
       if (overflow) {
         out = si.len_k - 1;
+        out_first = 0;
       } else {
         const int d = doc ? doc[si.meta_base + k] : 0;
         const unsigned long long key =
@@ -111,6 +118,7 @@ __global__ void pair_last_kernel(SeqLayout layout, const int* __restrict__ vis,
         for (int probe = 0; probe < kHashCap; ++probe) {
           if (keys[h] == key) {
             out = max(k, last[h]);
+            out_first = min(k, first[h]);
             break;
           }
           h = (h + 1) & (kHashCap - 1);
@@ -118,13 +126,14 @@ __global__ void pair_last_kernel(SeqLayout layout, const int* __restrict__ vis,
       }
     }
     pair_last[si.meta_base + k] = out;
+    if (pair_first) pair_first[si.meta_base + k] = out_first;
   }
 }
 
 int launch_pair_last(const SeqLayout& layout, const int* vis, const int* doc, int* pair_last,
-                     int nseq, cudaStream_t stream) {
+                     int* pair_first, int nseq, cudaStream_t stream) {
   if (nseq <= 0) return 0;
-  pair_last_kernel<<<nseq, 1024, 0, stream>>>(layout, vis, doc, pair_last);
+  pair_last_kernel<<<nseq, 1024, 0, stream>>>(layout, vis, doc, pair_last, pair_first);
   return static_cast<int>(cudaGetLastError());
 }
 
