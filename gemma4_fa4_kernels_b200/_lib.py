@@ -116,8 +116,8 @@ def load() -> ctypes.CDLL:
         lib.g4_read_device_error.restype = ctypes.c_int
         lib.g4_build_mask.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
-                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                      ctypes.c_void_p]
+                                      ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_void_p, ctypes.c_void_p]
         lib.g4_build_mask.restype = ctypes.c_int
         if lib.g4_abi_version() != ABI_VERSION:
             raise LibraryUnavailable(

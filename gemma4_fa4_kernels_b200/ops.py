@@ -3,7 +3,7 @@
 These functions do only what the native boundary needs (pointer/stride
 marshalling, output and workspace allocation on the caller's stream, status
 to exception mapping).  Contract validation that the reference performs in its
-adapters lives in ``adapters.py``.  Every call runs on the current CUDA
+adapters lives in ``b200.py``.  Every call runs on the current CUDA
 stream; nothing here synchronises the host.
 """
 
@@ -140,13 +140,14 @@ def attn_bwd(q, k, v, out, lse, dout, *, dlse=None, window=0, vision_ids=None,
 
 
 def build_mask(batch, q_len, kv_len, *, window, allow_vision_bidirectional, vision_ids=None,
-               document_ids=None, key_padding_mask=None, device):
+               document_ids=None, key_padding_mask=None, q_start=None, device):
     """Dense ``(B, Q, K)`` uint8 mask from ``g4_build_mask``."""
     lib = _lib.load()
     out = torch.empty(batch, q_len, kv_len, dtype=torch.uint8, device=device)
     vis, doc = _meta(vision_ids, device), _meta(document_ids, device)
     pad = None if key_padding_mask is None else key_padding_mask.to(torch.uint8).contiguous()
-    rc = lib.g4_build_mask(_ptr(out), batch, q_len, kv_len, int(window or 0),
+    rc = lib.g4_build_mask(_ptr(out), batch, q_len, kv_len, -1 if q_start is None else int(q_start),
+                           int(window or 0),
                            int(bool(allow_vision_bidirectional)), _ptr(vis), _ptr(doc), _ptr(pad),
                            _stream(device))
     _raise_for(rc, "g4_build_mask")

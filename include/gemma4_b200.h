@@ -133,13 +133,14 @@ int g4_read_device_error(const void* workspace, int* code, void* stream);
 
 /*
  * Dense Gemma-4 mask builder: writes out[b][q][k] = 1 if allowed, else 0
- * (uint8, (B,Sq,Sk) contiguous), with lower-right query alignment.
- * Replaces src/gemma4_fa4/masks.py:8-80 (gemma4_attention_mask) for the
- * sliding (window > 0, vision bidirectional) and global (window == 0) layers;
- * vision/document ids and key padding (uint8, nullable) are (B,Sk) contiguous.
+ * (uint8, (B,Sq,Sk) contiguous).  Query row i sits at absolute position
+ * q_start + i (q_start < 0 selects lower-right alignment, kv_len - q_len).
+ * window == 0 means no sliding window.  Replaces src/gemma4_fa4/masks.py:8-80
+ * (gemma4_attention_mask); vision/document ids (int32) and key padding
+ * (uint8) are (B,Sk) contiguous and nullable.
  */
-int g4_build_mask(uint8_t* out, int32_t batch, int32_t q_len, int32_t kv_len, int32_t window,
-                  int32_t allow_vision_bidirectional, const int32_t* vision_ids,
+int g4_build_mask(uint8_t* out, int32_t batch, int32_t q_len, int32_t kv_len, int32_t q_start,
+                  int32_t window, int32_t allow_vision_bidirectional, const int32_t* vision_ids,
                   const int32_t* document_ids, const uint8_t* key_padding, void* stream);
 
 #ifdef __cplusplus
