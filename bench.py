@@ -1,0 +1,436 @@
+#!/usr/bin/env python
+"""Headline benchmark: mask-aware fwd+bwd TFLOP/s of Gemma-4 attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload: global causal d512 attention, B=1 per GPU,
+S=4096, 32 query / 4 KV heads, BF16, softmax scale 1.0; Q/K/V are N(0,1) with
+every head vector RMS-normalised, dO ~ N(0,1).  One step = forward + backward
+(dQ, dK, dV) of one sequence per GPU.  Multi-GPU runs (one process per GPU,
+launched with torchrun) shard sequences across ranks with no collective on the
+data path ("weak" scaling); timing is the max over ranks of CUDA-event time.
+
+The JSON line carries, besides the contract keys:
+  roofline      dominant kernel's algorithmic TFLOP/s (live CUDA events over the
+                timed region) against the measured BF16 peak;
+  cpu_baseline  the numpy oracle (the reference CPU path restated) on a bounded
+                sample of the same workload on this host's cores;
+  e2e           the same metric through the public adapter with pinned host
+                buffers: H2D of q, k, v, dO and D2H of dq, dk, dv every step;
+  local_c0      the local d256 S2048 config measured the same way (secondary).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "mask-aware fwd+bwd TFLOP/s/GPU, local d256 & global d512; % BF16 TC peak"
+L2_BYTES = 126 * 1024**2
+
+C1 = dict(name="c1 global d512 causal fwd+bwd", seq=4096, hq=32, hkv=4, d=512, window=0)
+C0 = dict(name="c0 local d256 W1024 fwd+bwd", seq=2048, hq=32, hkv=16, d=256, window=1024)
+
+
+# ------------------------------------------------------------------------------------
+# shared helpers
+# ------------------------------------------------------------------------------------
+def pairs_of(cfg) -> int:
+    s, w = cfg["seq"], cfg["window"]
+    if not w:
+        return s * (s + 1) // 2
+    w = min(w, s)
+    return s * w - w * (w - 1) // 2
+
+
+def flops_of(cfg) -> dict:
+    p, h, d = pairs_of(cfg), cfg["hq"], cfg["d"]
+    fwd = 2.0 * h * p * (d + d)
+    bwd = 2.0 * h * p * (3 * d + 2 * d)
+    # algorithmic work attributed per kernel: the dK/dV kernel owns the S and dP
+    # recomputation plus dV and dK; the dQ kernel owns only dQ (its own S/dP
+    # recomputation is overhead of the split design).
+    return {"fwd": fwd, "bwd": bwd, "total": fwd + bwd,
+            "attn_fwd": fwd, "bwd_dkv": 2.0 * h * p * (4 * d), "bwd_dq": 2.0 * h * p * d,
+            "bwd_preprocess": 0.0}
+
+
+def make_inputs(cfg, seed, device, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    s, hq, hkv, d = cfg["seq"], cfg["hq"], cfg["hkv"], cfg["d"]
+
+    def rms(x):
+        return x * torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + 1e-6)
+
+    q = rms(torch.randn(1, s, hq, d, generator=g)).to(dtype)
+    k = rms(torch.randn(1, s, hkv, d, generator=g)).to(dtype)
+    v = rms(torch.randn(1, s, hkv, d, generator=g)).to(dtype)
+    do = torch.randn(1, s, hq, d, generator=g).to(dtype)
+    return [t.to(device) for t in (q, k, v, do)]
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            pk = json.load(f)
+        return pk.get("bf16_tflops_sustained"), pk.get("bf16_tflops"), "measured"
+    return 1400.0, 1590.0, "fallback"
+
+
+def load_traffic():
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r[2] > 300.0] or rows
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in loaded:
+            for name, flag in zip(names, r[3][1:]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r[0] for r in loaded),
+                "sm_max_mhz": max(r[1] for r in rows), "samples": len(loaded),
+                "power_w_max": max(r[2] for r in rows), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------------------------
+# distributed plumbing (one process per GPU; no collective on the data path)
+# ------------------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------
+# CPU baseline (oracle = the reference's CPU path restated in numpy)
+# ------------------------------------------------------------------------------------
+def cpu_sample(cfg, heads: int, seed: int = 0):
+    """Time fwd+bwd of `heads` query heads (with their KV head) of one sequence in
+    float64 numpy; returns (TFLOP/s, seconds, sample description, cores)."""
+    import oracle
+
+    g = torch.Generator().manual_seed(seed)
+    s, d = cfg["seq"], cfg["d"]
+
+    def rms(x):
+        return x * torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + 1e-6)
+
+    q = rms(torch.randn(1, heads, s, d, generator=g)).to(torch.bfloat16).double().numpy()
+    k = rms(torch.randn(1, 1, s, d, generator=g)).to(torch.bfloat16).double().numpy()
+    v = rms(torch.randn(1, 1, s, d, generator=g)).to(torch.bfloat16).double().numpy()
+    do = torch.randn(1, heads, s, d, generator=g).to(torch.bfloat16).double().numpy()
+    window = cfg["window"] or None
+    t0 = time.perf_counter()
+    oracle.attention_fwd(q, k, v, sliding_window=window, allow_vision_bidirectional=bool(window))
+    oracle.attention_bwd(q, k, v, do, sliding_window=window, allow_vision_bidirectional=bool(window))
+    dt = time.perf_counter() - t0
+    flops = flops_of(cfg)["total"] * heads / cfg["hq"]
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max(int(i.get("num_threads", 1)) for i in threadpool_info()) or 1
+    except Exception:  # pragma: no cover
+        cores = os.cpu_count() or 1
+    desc = (f"{heads} of {cfg['hq']} query heads of one {cfg['name']} sequence, float64 numpy "
+            f"oracle, forward + backward")
+    return flops / dt / 1e12, dt, desc, cores
+
+
+# ------------------------------------------------------------------------------------
+# B200 arm
+# ------------------------------------------------------------------------------------
+def run_b200(args, world, rank, local):
+    from gemma4_fa4_kernels_b200 import _lib, ops
+    from gemma4_fa4_kernels_b200 import fa4_global_text_forward
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = C1
+    fl = flops_of(cfg)
+    q, k, v, do = make_inputs(cfg, seed=1000 + rank, device=dev)
+
+    def step():
+        out, lse = ops.attn_fwd(q, k, v, window=cfg["window"])
+        ops.attn_bwd(q, k, v, out, lse, do, window=cfg["window"])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # ---- timed region (device time, max over ranks) ----
+    launches0 = _lib.launch_counts()
+    _lib.profile_reset()
+    _lib.profile_enable(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+    _lib.profile_enable(False)
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = max_over_ranks(ms, world, dev)
+    launches1 = _lib.launch_counts()
+    prof = _lib.profile_read()
+    gpu_launches = sum(launches1[n] - launches0[n] for n in launches1)
+
+    # ---- roofline of the dominant kernel ----
+    dom = max((n for n in prof if prof[n][0] > 0), key=lambda n: prof[n][1])
+    n_launch, tot_ms = prof[dom]
+    per_launch_ms = tot_ms / n_launch
+    per_launch_flops = fl.get(dom, 0.0) * args.steps / n_launch
+    achieved = per_launch_flops / (per_launch_ms * 1e-3) / 1e12
+    peak_sus, peak_burst, peak_kind = load_peaks()
+    traffic = load_traffic().get(f"{dom}@c1")
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 1),
+                "peak": peak_sus, "unit": "TFLOP/s", "frac": round(achieved / peak_sus, 4),
+                "peak_kind": f"{peak_kind} sustained bf16 (cuBLAS, power-capped)",
+                "frac_of_burst_peak": round(achieved / peak_burst, 4),
+                "traffic": traffic, "launch_ms": round(per_launch_ms, 4),
+                "kernel_share": {n: round(prof[n][1] / sum(x[1] for x in prof.values()), 4)
+                                 for n in prof if prof[n][0] > 0}}
+
+    # ---- local c0 (secondary line item) ----
+    lq, lk, lv, ldo = make_inputs(C0, seed=2000 + rank, device=dev)
+
+    def lstep():
+        o, l_ = ops.attn_fwd(lq, lk, lv, window=C0["window"])
+        ops.attn_bwd(lq, lk, lv, o, l_, ldo, window=C0["window"])
+
+    for _ in range(3):
+        lstep()
+    torch.cuda.synchronize(dev)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for _ in range(max(args.steps, 5)):
+        lstep()
+    a1.record()
+    torch.cuda.synchronize(dev)
+    lms = a0.elapsed_time(a1) / max(args.steps, 5)
+    local_tf = flops_of(C0)["total"] / (lms * 1e-3) / 1e12
+    del lq, lk, lv, ldo
+
+    # ---- end to end through the public adapter, host buffers ----
+    hq_, hk_, hv_, hdo_ = (t.cpu().pin_memory() for t in (q, k, v, do))
+    hgrads = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, k, v)]
+    h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_, hdo_))
+    d2h = sum(t.numel() * t.element_size() for t in hgrads)
+
+    def e2e_step():
+        dq_in = hq_.to(dev, non_blocking=True).requires_grad_(True)
+        dk_in = hk_.to(dev, non_blocking=True).requires_grad_(True)
+        dv_in = hv_.to(dev, non_blocking=True).requires_grad_(True)
+        ddo = hdo_.to(dev, non_blocking=True)
+        out, _lse = fa4_global_text_forward(dq_in, dk_in, dv_in)
+        out.backward(ddo)
+        for h, t in zip(hgrads, (dq_in.grad, dk_in.grad, dv_in.grad)):
+            h.copy_(t, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    b1.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(b0.elapsed_time(b1) / args.steps, world, dev)
+
+    # ---- CPU baseline (rank 0, N=1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        tf, secs, desc, cores = cpu_sample(C1, heads=args.cpu_heads)
+        cpu = {"value": round(tf, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+               "sample": f"{desc} ({secs:.1f} s)"}
+
+    clocks = clk.summary()
+    value = world * fl["total"] / (ms_max * 1e-3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1), per-head RMS-normalised Q/K/V, N(0,1) dO)",
+            "config": {"workload": C1["name"] + " (BASELINE configs[1])", "global_batch": world,
+                       "seq_len": C1["seq"], "q_heads": C1["hq"], "kv_heads": C1["hkv"],
+                       "head_dim": C1["d"], "mask": "lower-right causal", "softmax_scale": 1.0,
+                       "parallelism": f"dp{world} (one sequence per GPU, no data-path collective)",
+                       "l2": "working set per step (q,k,v,dO,O,grads ~0.9 GB) exceeds the 126 MB L2; "
+                             "no explicit flush",
+                       "flops_per_step_per_gpu": fl["total"]},
+            "pct_peak": round(value / world / peak_sus, 4),
+            "per_gpu": round(value / world, 2),
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * fl["total"] / (e2e_ms * 1e-3) / 1e12, 2),
+                    "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 3),
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "fa4_global_text_forward + autograd backward"},
+            "clocks": clocks,
+            "gpu_launches": gpu_launches,
+            "local_c0": {"workload": C0["name"] + " (BASELINE configs[0])",
+                         "ms_per_step": round(lms, 4), "value": round(local_tf, 2),
+                         "unit": "TFLOP/s", "pct_peak": round(local_tf / peak_sus, 4)},
+        }
+        print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------
+# reference arm: the reference's CPU path (oracle port) on the host cores
+# ------------------------------------------------------------------------------------
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    times = []
+    desc, cores = "", 1
+    for i in range(args.warmup + args.steps):
+        tf, secs, desc, cores = cpu_sample(C1, heads=args.ref_heads, seed=i)
+        if i >= args.warmup:
+            times.append(secs)
+    sec = statistics.mean(times)
+    flops = flops_of(C1)["total"] * args.ref_heads / C1["hq"]
+    value = flops / sec / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": C1["name"] + " (BASELINE configs[1])", "global_batch": 1,
+                   "seq_len": C1["seq"], "q_heads": C1["hq"], "kv_heads": C1["hkv"],
+                   "head_dim": C1["d"], "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": cores,
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--cpu-heads", type=int, default=4,
+                    help="query heads in the CPU-baseline sample")
+    ap.add_argument("--ref-heads", type=int, default=1,
+                    help="query heads per step of the reference arm")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("at least 3 warm-up steps are required")
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_b200(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

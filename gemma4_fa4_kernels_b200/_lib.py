@@ -32,6 +32,12 @@ EXPORTED_SYMBOLS = (
     "g4_attn_bwd",
     "g4_read_device_error",
     "g4_build_mask",
+    "g4_kernel_count",
+    "g4_kernel_name",
+    "g4_launch_count",
+    "g4_profile_enable",
+    "g4_profile_reset",
+    "g4_profile_read",
 )
 
 
@@ -119,6 +125,17 @@ def load() -> ctypes.CDLL:
                                       ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p]
         lib.g4_build_mask.restype = ctypes.c_int
+        lib.g4_kernel_count.restype = ctypes.c_int
+        lib.g4_kernel_name.argtypes = [ctypes.c_int]
+        lib.g4_kernel_name.restype = ctypes.c_char_p
+        lib.g4_launch_count.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_longlong)]
+        lib.g4_launch_count.restype = ctypes.c_int
+        lib.g4_profile_enable.argtypes = [ctypes.c_int]
+        lib.g4_profile_enable.restype = ctypes.c_int
+        lib.g4_profile_reset.restype = ctypes.c_int
+        lib.g4_profile_read.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_longlong),
+                                        ctypes.POINTER(ctypes.c_double)]
+        lib.g4_profile_read.restype = ctypes.c_int
         if lib.g4_abi_version() != ABI_VERSION:
             raise LibraryUnavailable(
                 f"ABI mismatch: library {lib.g4_abi_version()}, bindings {ABI_VERSION}")
@@ -128,3 +145,40 @@ def load() -> ctypes.CDLL:
 
 def last_error() -> str:
     return load().g4_last_error().decode(errors="replace")
+
+
+def kernel_names() -> list[str]:
+    lib = load()
+    return [lib.g4_kernel_name(i).decode() for i in range(lib.g4_kernel_count())]
+
+
+def launch_counts() -> dict[str, int]:
+    """Launches per kernel issued by this process so far."""
+    lib = load()
+    out = {}
+    for i, name in enumerate(kernel_names()):
+        c = ctypes.c_longlong(0)
+        lib.g4_launch_count(i, ctypes.byref(c))
+        out[name] = int(c.value)
+    return out
+
+
+def profile_enable(enable: bool) -> None:
+    load().g4_profile_enable(1 if enable else 0)
+
+
+def profile_reset() -> None:
+    load().g4_profile_reset()
+
+
+def profile_read() -> dict[str, tuple[int, float]]:
+    """Per kernel: (launches, summed device ms) since the last reset."""
+    lib = load()
+    out = {}
+    for i, name in enumerate(kernel_names()):
+        n, ms = ctypes.c_longlong(0), ctypes.c_double(0.0)
+        rc = lib.g4_profile_read(i, ctypes.byref(n), ctypes.byref(ms))
+        if rc != G4_OK:
+            raise RuntimeError(f"g4_profile_read: {last_error()}")
+        out[name] = (int(n.value), float(ms.value))
+    return out

@@ -7,7 +7,10 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/gemma4_b200.h"
 #include "g4_kernels.h"
@@ -30,6 +33,47 @@ int fail(int code, const char* fmt, ...) {
 int cuda_fail(cudaError_t e, const char* what) {
   return fail(G4_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
+
+// ---------------------------------------------------------------------------------------
+// launch accounting / opt-in event timing
+// ---------------------------------------------------------------------------------------
+enum KernelId { kKFwd = 0, kKBwdPre, kKBwdDq, kKBwdDkv, kKPlan, kKMask, kKCount };
+const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
+                                           "plan", "mask"};
+std::atomic<long long> g_launches[kKCount];
+std::atomic<bool> g_profile{false};
+struct ProfRecord {
+  int id;
+  cudaEvent_t start, stop;
+};
+std::mutex g_prof_mu;
+std::vector<ProfRecord> g_prof_records;
+
+// Brackets one launch: counts it and, when profiling, records events around it.
+class LaunchScope {
+ public:
+  LaunchScope(int id, cudaStream_t st) : id_(id), st_(st) {
+    g_launches[id].fetch_add(1);
+    if (g_profile.load()) {
+      if (cudaEventCreate(&a_) == cudaSuccess && cudaEventCreate(&b_) == cudaSuccess) {
+        cudaEventRecord(a_, st_);
+        timed_ = true;
+      }
+    }
+  }
+  ~LaunchScope() {
+    if (!timed_) return;
+    cudaEventRecord(b_, st_);
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof_records.push_back({id_, a_, b_});
+  }
+
+ private:
+  int id_;
+  cudaStream_t st_;
+  cudaEvent_t a_{}, b_{};
+  bool timed_ = false;
+};
 
 // ---------------------------------------------------------------------------------------
 // TMA tensor maps (driver entry point fetched through the runtime, no -lcuda needed)
@@ -193,10 +237,12 @@ int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream
   const g4::SeqLayout layout = make_layout(a);
   int* hdr = ws_ptr<int>(a, 0);
   if (a->cu_seqlens_q) {
+    LaunchScope ls(kKPlan, st);
     int rc = g4::launch_plan_tiles(a->cu_seqlens_q, a->batch, g4::kTileM,
                                    ws_ptr<int2>(a, w.q_tiles), hdr + 1, st);
     if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "q tile planning");
     if (backward) {
+      LaunchScope ls2(kKPlan, st);
       rc = g4::launch_plan_tiles(a->cu_seqlens_k, a->batch, g4::kTileN,
                                  ws_ptr<int2>(a, w.k_tiles), hdr + 2, st);
       if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "k tile planning");
@@ -210,6 +256,7 @@ int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream
   if (w.pair_last) {
     int* pl = ws_ptr<int>(a, w.pair_last);
     int* pf = w.pair_first ? ws_ptr<int>(a, w.pair_first) : nullptr;
+    LaunchScope ls(kKPlan, st);
     int rc = g4::launch_pair_last(layout, a->vision_ids, a->document_ids, pl, pf, a->batch, st);
     if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "vision pair planning");
     mask->pair_last = pl;
@@ -275,6 +322,7 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
   const int grid_x = packed ? w.max_q_tiles
                             : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
   const int slabs = a->head_dim_v / 256;
+  LaunchScope ls(kKFwd, st);
   int e = D == 256 ? g4::launch_fwd<256>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st)
                    : g4::launch_fwd<512>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st);
   if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward launch");
@@ -330,7 +378,11 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     p.k_tiles = ws_ptr<int2>(a, w.k_tiles);
     p.n_k_tiles = ws_ptr<int>(a, 0) + 2;
   }
-  int e = g4::launch_bwd_preprocess(p, a->head_dim_v, w.tokens_q, st);
+  int e;
+  {
+    LaunchScope ls(kKBwdPre, st);
+    e = g4::launch_bwd_preprocess(p, a->head_dim_v, w.tokens_q, st);
+  }
   if (e) return cuda_fail(static_cast<cudaError_t>(e), "backward preprocess launch");
   const int D = a->head_dim_qk;
   const int64_t bq = packed ? 1 : a->batch;
@@ -352,12 +404,63 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     return rc;
   const int gq = packed ? w.max_q_tiles : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
   const int gk = packed ? w.max_k_tiles : a->batch * ((a->seqlen_k + g4::kTileN - 1) / g4::kTileN);
-  e = D == 256 ? g4::launch_bwd_dq<256>(tq, tk, tk64, tv, tdo, p, gq, st)
-               : g4::launch_bwd_dq<512>(tq, tk, tk64, tv, tdo, p, gq, st);
+  {
+    LaunchScope ls(kKBwdDq, st);
+    e = D == 256 ? g4::launch_bwd_dq<256>(tq, tk, tk64, tv, tdo, p, gq, st)
+                 : g4::launch_bwd_dq<512>(tq, tk, tk64, tv, tdo, p, gq, st);
+  }
   if (e) return cuda_fail(static_cast<cudaError_t>(e), "dQ launch");
-  e = D == 256 ? g4::launch_bwd_dkv<256>(tq, tk, tv, tdo, p, gk, st)
-               : g4::launch_bwd_dkv<512>(tq, tk, tv, tdo, p, gk, st);
+  {
+    LaunchScope ls(kKBwdDkv, st);
+    e = D == 256 ? g4::launch_bwd_dkv<256>(tq, tk, tv, tdo, p, gk, st)
+                 : g4::launch_bwd_dkv<512>(tq, tk, tv, tdo, p, gk, st);
+  }
   if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK/dV launch");
+  return G4_OK;
+}
+
+int g4_kernel_count(void) { return kKCount; }
+
+const char* g4_kernel_name(int id) { return (id >= 0 && id < kKCount) ? kKernelNames[id] : ""; }
+
+int g4_launch_count(int id, long long* count) {
+  if (id < 0 || id >= kKCount || !count) return fail(G4_ERR_INVALID, "bad kernel id");
+  *count = g_launches[id].load();
+  return G4_OK;
+}
+
+int g4_profile_enable(int enable) {
+  g_profile.store(enable != 0);
+  return G4_OK;
+}
+
+int g4_profile_reset(void) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto& r : g_prof_records) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  g_prof_records.clear();
+  return G4_OK;
+}
+
+int g4_profile_read(int id, long long* launches, double* total_ms) {
+  if (id < 0 || id >= kKCount || !launches || !total_ms) return fail(G4_ERR_INVALID, "bad kernel id");
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  long long n = 0;
+  double ms = 0.0;
+  for (auto& r : g_prof_records) {
+    if (r.id != id) continue;
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "profile event");
+    float t = 0.f;
+    e = cudaEventElapsedTime(&t, r.start, r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "profile elapsed time");
+    ms += t;
+    ++n;
+  }
+  *launches = n;
+  *total_ms = ms;
   return G4_OK;
 }
 

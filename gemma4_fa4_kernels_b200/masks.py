@@ -50,6 +50,8 @@ def gemma4_attention_mask(
     _check_meta(document_ids, batch_size, kv_len, "document_ids")
     _check_meta(key_padding_mask, batch_size, kv_len, "key_padding_mask")
     device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     use_vision = vision_block_ids is not None and allow_vision_bidirectional
 
     if device.type == "cuda":

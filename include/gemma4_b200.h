@@ -143,6 +143,24 @@ int g4_build_mask(uint8_t* out, int32_t batch, int32_t q_len, int32_t kv_len, in
                   int32_t window, int32_t allow_vision_bidirectional, const int32_t* vision_ids,
                   const int32_t* document_ids, const uint8_t* key_padding, void* stream);
 
+/*
+ * Launch accounting and opt-in timing (benchmark/profiling support; no
+ * reference counterpart -- the reference times whole Python calls).
+ * Kernel ids: 0 forward, 1 backward preprocess, 2 backward dQ, 3 backward
+ * dK/dV, 4 planning (tile lists, vision pairs), 5 mask builder.
+ *  - g4_launch_count: launches of `kernel_id` issued by this process so far.
+ *  - g4_profile_enable(1): every later launch is bracketed by CUDA events on
+ *    its own stream; g4_profile_read synchronises those events and returns the
+ *    launches and summed device milliseconds per kernel id since the last
+ *    g4_profile_reset.  Not for use inside CUDA graph capture.
+ */
+int g4_kernel_count(void);
+const char* g4_kernel_name(int kernel_id);
+int g4_launch_count(int kernel_id, long long* count);
+int g4_profile_enable(int enable);
+int g4_profile_reset(void);
+int g4_profile_read(int kernel_id, long long* launches, double* total_ms);
+
 #ifdef __cplusplus
 }
 #endif
