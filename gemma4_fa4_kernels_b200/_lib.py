@@ -22,6 +22,9 @@ G4_ERR_CUDA = 3
 G4_ERR_DEVICE = 4
 G4_ERR_WORKSPACE = 5
 
+# Size of the static scratch array behind g4_attn_bwd_noalloc.
+NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
+
 # Every exported entry point declared in include/gemma4_b200.h.
 EXPORTED_SYMBOLS = (
     "g4_abi_version",
@@ -30,6 +33,7 @@ EXPORTED_SYMBOLS = (
     "g4_attn_fwd",
     "g4_attn_bwd_workspace_bytes",
     "g4_attn_bwd",
+    "g4_attn_bwd_noalloc",
     "g4_read_device_error",
     "g4_build_mask",
     "g4_kernel_count",
@@ -113,7 +117,7 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = [P]
             fn.restype = ctypes.c_size_t
-        for name in ("g4_attn_fwd", "g4_attn_bwd"):
+        for name in ("g4_attn_fwd", "g4_attn_bwd", "g4_attn_bwd_noalloc"):
             fn = getattr(lib, name)
             fn.argtypes = [P, ctypes.c_void_p]
             fn.restype = ctypes.c_int

@@ -265,6 +265,31 @@ int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream
   return G4_OK;
 }
 
+// Scratch for g4_attn_bwd_noalloc: a fixed-size static device array instead of
+// a caller-provided workspace.  Host code must not use the symbol itself as a
+// device address; noalloc_scratch() fetches the real address once per device.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[G4_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(G4_ERR_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return G4_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -417,6 +442,24 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
   }
   if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK/dV launch");
   return G4_OK;
+}
+
+int g4_attn_bwd_noalloc(const g4_attn_args* a, void* stream) {
+  g_last_error.clear();
+  if (!a) return fail(G4_ERR_INVALID, "null argument block");
+  const size_t need = plan_workspace(a, true).total;
+  if (need > G4_NOALLOC_SCRATCH_BYTES)
+    return fail(G4_ERR_WORKSPACE,
+                "this backward needs %zu bytes of scratch; the allocation-free entry point has "
+                "%u bytes (use g4_attn_bwd with a caller workspace)",
+                need, G4_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  g4_attn_args local = *a;
+  local.workspace = scratch;
+  local.workspace_bytes = G4_NOALLOC_SCRATCH_BYTES;
+  return g4_attn_bwd(&local, stream);
 }
 
 int g4_kernel_count(void) { return kKCount; }

@@ -125,6 +125,25 @@ size_t g4_attn_bwd_workspace_bytes(const g4_attn_args* args);
 int g4_attn_bwd(const g4_attn_args* args, void* stream);
 
 /*
+ * Backward that allocates nothing, for callers that cannot allocate device
+ * memory at call time (no reference counterpart: the reference allocates its
+ * backward workspaces with torch).  Examples: a runtime that plans all device
+ * memory ahead of time and forbids cudaMalloc while it executes, or a plugin
+ * host that hands an op its tensors but no scratch buffer.  Same arguments
+ * and results as g4_attn_bwd, except that `workspace`/`workspace_bytes` are
+ * ignored: scratch comes from one static device array of
+ * G4_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads the
+ * library keeps until process exit.  A call whose scratch need
+ * (g4_attn_bwd_workspace_bytes) exceeds that size fails with
+ * G4_ERR_WORKSPACE before any launch.  The first call on a device looks the
+ * array up for that device, so make it before any CUDA graph capture.  All
+ * calls share the one array: calls that overlap on the GPU (other streams,
+ * other threads) race and must be serialised by the caller.
+ */
+#define G4_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+int g4_attn_bwd_noalloc(const g4_attn_args* args, void* stream);
+
+/*
  * Synchronise `stream` and read the device error word of a workspace used by
  * a previous call; *code receives 0 or a G4 device error (1 = TMA wait
  * expired, 2 = MMA wait expired, 3 = role hand-off wait expired).
