@@ -59,12 +59,16 @@ def flops_of(cfg) -> dict:
     p, h, d = pairs_of(cfg), cfg["hq"], cfg["d"]
     fwd = 2.0 * h * p * (d + d)
     bwd = 2.0 * h * p * (3 * d + 2 * d)
-    # algorithmic work attributed per kernel: the dK/dV kernel owns the S and dP
-    # recomputation plus dV and dK; the dQ kernel owns only dQ (its own S/dP
-    # recomputation is overhead of the split design).
+    # algorithmic work attributed per kernel (recompute path): the dK/dV kernel
+    # owns S, dP, dV and dK; the dQ kernel owns only dQ (its own S/dP
+    # recomputation is overhead of that design).
     return {"fwd": fwd, "bwd": bwd, "total": fwd + bwd,
             "attn_fwd": fwd, "bwd_dkv": 2.0 * h * p * (4 * d), "bwd_dq": 2.0 * h * p * d,
-            "bwd_preprocess": 0.0}
+            "bwd_preprocess": 0.0,
+            # materialised path: the score kernels compute S and dP once; each
+            # tile GEMM does one of dV, dK, dQ
+            "bwd_score": 2.0 * h * p * (2 * d), "bwd_gemm_dv": 2.0 * h * p * d,
+            "bwd_gemm_dk": 2.0 * h * p * d, "bwd_gemm_dq": 2.0 * h * p * d}
 
 
 def make_inputs(cfg, seed, device, dtype=torch.bfloat16):

@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "g4_attn_fwd_workspace_bytes",
     "g4_attn_fwd",
     "g4_attn_bwd_workspace_bytes",
+    "g4_attn_bwd_min_workspace_bytes",
     "g4_attn_bwd",
     "g4_attn_bwd_noalloc",
     "g4_read_device_error",
@@ -113,7 +114,8 @@ def load() -> ctypes.CDLL:
         P = ctypes.POINTER(G4AttnArgs)
         lib.g4_abi_version.restype = ctypes.c_int
         lib.g4_last_error.restype = ctypes.c_char_p
-        for name in ("g4_attn_fwd_workspace_bytes", "g4_attn_bwd_workspace_bytes"):
+        for name in ("g4_attn_fwd_workspace_bytes", "g4_attn_bwd_workspace_bytes",
+                     "g4_attn_bwd_min_workspace_bytes"):
             fn = getattr(lib, name)
             fn.argtypes = [P]
             fn.restype = ctypes.c_size_t

@@ -1,0 +1,650 @@
+// Gemma-4 attention backward for sm_100a with materialised P / dS tiles.
+//
+// A 128x512 fp32 accumulator fills all of tensor memory, so a KV-major kernel
+// cannot hold dK and dV (or dQ next to S and dP) for d512; splitting their
+// columns over CTAs forces every CTA to recompute the 512-deep S = QK^T and
+// dP = dO V^T.  This path instead spends HBM (ample on B200) to compute each of
+// the five backward matmuls exactly once:
+//
+//   plan   per query tile: first key tile, key-tile count and the offset of its
+//          tiles in the scratch (prefix sum over the causal / window band);
+//   score  Q-major.  S = Q K^T and/or dP = dO V^T into double-buffered TMEM;
+//          the four math warps write P = exp(S - LSE) and dS = P (dP - delta)
+//          as bf16 128x128 tiles straight into HBM scratch, pre-swizzled in the
+//          exact shared-memory layout the consumers load with one bulk copy.
+//          d256: one kernel computes both (Q and dO fit in shared memory);
+//          d512: one launch writes P (Q resident), a second reads P and writes
+//          dS (dO resident);
+//   gemm   dV = P^T dO and dK = dS^T Q (KV-major, summing every query head of
+//          the GQA group in TMEM) and dQ = dS K (Q-major), each a tile-sparse
+//          GEMM with a full-width (256 or 512 column) TMEM accumulator.
+//
+// Scratch tile layout (32 KB): [key block 0..1][query row 0..127][64 keys],
+// 128-B swizzled (16-B chunk c of row r stored at chunk c ^ (r % 8)).  The
+// same bytes are the K-major A operand of dQ = dS K (rows = queries) and the
+// MN-major A operand of dV = P^T dO / dK = dS^T Q (rows = queries = K index).
+//
+// Masked pairs hold exact zeros, so consumers never re-evaluate the mask.
+// This path serves the causal and sliding-window (+document) masks; vision
+// metadata (whose key range per query tile is data-dependent) and workspaces
+// too small for the scratch use the recompute kernels in attn_bwd.cu.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "g4_attn.cuh"
+#include "g4_kernels.h"
+#include "g4_sm100.cuh"
+
+namespace g4 {
+
+constexpr int kTileBytes = 32768;  // one 128x128 bf16 scratch tile
+
+__device__ __forceinline__ uint8_t* scratch_tile(uint8_t* base, const MatParams& p, int head,
+                                                 int offset, int slot) {
+  return base + ((static_cast<int64_t>(head) * p.head_cap_tiles + offset + slot) * kTileBytes);
+}
+
+// byte offset of the 16-B chunk holding columns [8c, 8c+8) of row r
+__device__ __forceinline__ uint32_t tile_chunk_offset(int r, int c) {
+  const int blk = c >> 3, ch = c & 7;
+  return blk * 16384 + r * 128 + ((ch ^ (r & 7)) << 4);
+}
+
+// =====================================================================================
+// plan: per query tile (kt_lo, n_kt, scratch offset, sequence)
+// =====================================================================================
+__global__ void plan_qtile_ranges_kernel(const MatParams p) {
+  __shared__ int scan[1024];
+  __shared__ int carry;
+  const int tid = threadIdx.x;
+  const bool packed = p.layout.packed();
+  const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < n; base += 1024) {
+    const int g = base + tid;
+    int cnt = 0, kt_lo = 0, seq = 0;
+    if (g < n) {
+      int qt;
+      if (packed) {
+        const int2 t = p.q_tiles[g];
+        seq = t.x;
+        qt = t.y;
+      } else {
+        seq = g / p.n_qt_fixed;
+        qt = g % p.n_qt_fixed;
+      }
+      const SeqInfo si = p.layout.seq(seq);
+      const int q_off = si.len_k - si.len_q;
+      const int qa0 = qt * kTileM + q_off;
+      const int qa1 = min((qt + 1) * kTileM, si.len_q) - 1 + q_off;
+      const int lo = p.mask.window > 0 ? max(0, qa0 - p.mask.window + 1) : 0;
+      const int hi = min(qa1, si.len_k - 1);
+      if (hi >= lo) {
+        kt_lo = lo / kTileN;
+        cnt = hi / kTileN - kt_lo + 1;
+      }
+    }
+    scan[tid] = cnt;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {
+      const int v = tid >= off ? scan[tid - off] : 0;
+      __syncthreads();
+      scan[tid] += v;
+      __syncthreads();
+    }
+    if (g < n) p.ranges[g] = make_int4(kt_lo, cnt, carry + scan[tid] - cnt, seq);
+    __syncthreads();
+    if (tid == 1023) carry += scan[1023];
+    __syncthreads();
+  }
+  if (tid == 0 && carry > p.head_cap_tiles && p.err) atomicCAS(p.err, 0, 6);
+}
+
+// =====================================================================================
+// score kernel
+// =====================================================================================
+enum ScoreMode : int { kScorePdS = 0, kScoreP = 1, kScoreDs = 2 };
+
+template <int D, int MODE>
+struct ScoreCfg {
+  static constexpr bool kS = MODE != kScoreDs;   // computes S (needs Q, K)
+  static constexpr bool kDP = MODE != kScoreP;   // computes dP (needs dO, V)
+  static constexpr int kQBytes = kS ? D * kTileM * 2 : 0;
+  static constexpr int kDoBytes = kDP ? D * kTileM * 2 : 0;
+  static constexpr int kStages = 3;
+  static constexpr int kChunksPerTile = (kS ? D / 128 : 0) + (kDP ? D / 128 : 0);
+};
+
+struct ScoreMisc {
+  uint64_t res_full;
+  uint64_t ring_full[4];
+  uint64_t ring_empty[4];
+  uint64_t s_full[2];
+  uint64_t buf_free[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int D, int MODE>
+__global__ void __launch_bounds__(192, 1)
+    bwd_score_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV,
+                     const __grid_constant__ CUtensorMap tmDO, const MatParams p) {
+  using Cfg = ScoreCfg<D, MODE>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_addr(smem) & 1023u) != 0) {
+    if (p.err) atomicCAS(p.err, 0, 5);
+    return;
+  }
+  uint8_t* q_s = smem;
+  uint8_t* do_s = smem + Cfg::kQBytes;
+  uint8_t* ring = do_s + Cfg::kDoBytes;
+  ScoreMisc* misc = reinterpret_cast<ScoreMisc*>(ring + Cfg::kStages * 32768);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = blockIdx.x;
+  const int head = blockIdx.y;
+  const int kv_head = head / p.group;
+  const bool packed = p.layout.packed();
+  if (packed && g >= *p.n_q_tiles) return;
+  if (!packed && g >= p.layout.batch * p.n_qt_fixed) return;
+  const int4 rg = p.ranges[g];
+  const int kt_lo = rg.x, n_kt = rg.y, t_off = rg.z, seq = rg.w;
+  const int qt = packed ? p.q_tiles[g].y : g % p.n_qt_fixed;
+  const SeqInfo si = p.layout.seq(seq);
+  const int q_off = si.len_k - si.len_q;
+  const int64_t tok_base = packed ? si.q_base : static_cast<int64_t>(seq) * p.layout.seqlen_q;
+  const bool cap_ok = t_off + n_kt <= p.head_cap_tiles;
+
+  if (tid == 0) {
+    mbar_init(&misc->res_full, 1);
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&misc->ring_full[s], 1);
+      mbar_init(&misc->ring_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&misc->s_full[b], 1);
+      mbar_init(&misc->buf_free[b], kTileM);
+    }
+    mbar_init(&misc->drain, 1);
+    misc->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(&misc->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc->tmem_base;
+  const CtaAbort ab{&misc->abort, p.err};
+  const int work = cap_ok ? n_kt : 0;
+  // TMEM per buffer b: S at b*256, dP at b*256+128 (P-only / dS-only modes use one of them)
+  auto s_col = [](int b) { return static_cast<uint32_t>(b * 256); };
+  auto dp_col = [](int b) { return static_cast<uint32_t>(b * 256 + 128); };
+
+  if (warp == 4) {
+    if (lane == 0 && work > 0) {
+      mbar_expect_tx(&misc->res_full, Cfg::kQBytes + Cfg::kDoBytes);
+      const int qrow = si.q_base + qt * kTileM;
+      if (Cfg::kS)
+        for (int blk = 0; blk < D / 64; ++blk)
+          tma_load_4d(q_s + blk * 16384, &tmQ, &misc->res_full, blk * 64, head, qrow, si.b_coord);
+      if (Cfg::kDP)
+        for (int blk = 0; blk < D / 64; ++blk)
+          tma_load_4d(do_s + blk * 16384, &tmDO, &misc->res_full, blk * 64, head, qrow, si.b_coord);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int j = 0; j < work && ok; ++j) {
+        const int krow = si.k_base + (kt_lo + j) * kTileN;
+        for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
+          const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+          ++it;
+          if (!(ok = mbar_wait(&misc->ring_empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
+          mbar_expect_tx(&misc->ring_full[st], 32768);
+          const bool is_k = Cfg::kS && c < D / 128;
+          const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
+          for (int h = 0; h < 2; ++h)
+            tma_load_4d(ring + st * 32768 + h * 16384, is_k ? &tmK : &tmV, &misc->ring_full[st],
+                        (2 * cc + h) * 64, kv_head, krow, si.b_coord);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0 && work > 0) {
+      constexpr uint32_t kId = idesc_bf16(128, 128, false, false);
+      const uint32_t qb = smem_addr(q_s), db = smem_addr(do_s), rb = smem_addr(ring);
+      uint32_t it = 0;
+      bool ok = mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
+      for (int j = 0; j < work && ok; ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !(ok = mbar_wait(&misc->buf_free[b], ((j - 2) >> 1) & 1, ab, kDevTimeoutPeer)))
+          break;
+        tc_fence_after();
+        for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
+          const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+          ++it;
+          if (!(ok = mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma))) break;
+          tc_fence_after();
+          const bool is_k = Cfg::kS && c < D / 128;
+          const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
+          const uint32_t abase = is_k ? qb : db;
+          const uint32_t dcol = is_k ? s_col(b) : dp_col(b);
+          const uint32_t sb = rb + st * 32768;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const int gk = cc * 8 + kk;
+            umma_ss(tmem + dcol, sdesc_sw128(abase + (gk >> 2) * 16384 + (gk & 3) * 32, 16, 1024),
+                    sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), kId,
+                    (cc | kk) != 0);
+          }
+          umma_commit(&misc->ring_empty[st]);
+        }
+        umma_commit(&misc->s_full[b]);
+      }
+      umma_commit(&misc->drain);
+      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- math warps: P / dS tiles to HBM ----------------
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int r = tid;  // row in the query tile
+    const int q_idx = qt * kTileM + r;
+    const bool row_valid = q_idx < si.len_q;
+    const int q_abs = q_idx + q_off;
+    const float lse2_r = row_valid ? p.lse2[head * p.ws_head_stride + tok_base + q_idx] : -INFINITY;
+    const float delta_r = row_valid ? p.delta[head * p.ws_head_stride + tok_base + q_idx] : 0.f;
+    const int qdoc = (row_valid && p.mask.doc) ? p.mask.doc[si.meta_base + q_abs] : 0;
+    const int qa0 = qt * kTileM + q_off;
+    const int qa1 = min((qt + 1) * kTileM, si.len_q) - 1 + q_off;
+    bool ok = true;
+    for (int j = 0; j < work; ++j) {
+      const int b = j & 1;
+      const int k0 = (kt_lo + j) * kTileN;
+      const int cls = p.mask.doc ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
+      if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) continue;
+      tc_fence_after();
+      uint8_t* ptile = Cfg::kS || MODE == kScoreDs ? scratch_tile(p.p_tiles, p, head, t_off, j) : nullptr;
+      uint8_t* dtile = Cfg::kDP ? scratch_tile(p.ds_tiles, p, head, t_off, j) : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32], dr[32];
+        if (Cfg::kS && Cfg::kDP) {
+          tmem_ld32(lane_base + s_col(b) + c * 32, sr);
+          tmem_ld32(lane_base + dp_col(b) + c * 32, dr);
+          tmem_wait_ld();
+          reg_fence32(sr);
+          reg_fence32(dr);
+        } else if (Cfg::kS) {
+          tmem_ld32(lane_base + s_col(b) + c * 32, sr);
+          tmem_wait_ld();
+          reg_fence32(sr);
+        } else {
+          tmem_ld32(lane_base + dp_col(b) + c * 32, dr);
+          tmem_wait_ld();
+          reg_fence32(dr);
+        }
+        if (c == 3) {  // every TMEM value of this buffer is now in registers
+          tc_fence_before();
+          mbar_arrive(&misc->buf_free[b]);
+        }
+        float pv[32];
+        if (MODE == kScoreDs) {
+          // P as written by the P-only pass (exact zeros where masked)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint4 w = *reinterpret_cast<const uint4*>(ptile + tile_chunk_offset(r, c * 4 + u));
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[e]));
+              pv[u * 8 + 2 * e] = f.x;
+              pv[u * 8 + 2 * e + 1] = f.y;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int k = k0 + c * 32 + i;
+            bool keep = row_valid && lse2_r != -INFINITY && k < si.len_k;
+            if (cls != 1 && keep) {
+              const int kdoc = p.mask.doc ? p.mask.doc[si.meta_base + k] : 0;
+              keep = mask_allows(p.mask.window, q_abs, k, -1, qdoc, -1, kdoc);
+            }
+            pv[i] = keep ? ex2(fmaf(__uint_as_float(sr[i]), kLog2e, -lse2_r)) : 0.f;
+          }
+        }
+        if (MODE != kScoreDs) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 w;
+            w.x = pack_bf16x2(pv[u * 8 + 0], pv[u * 8 + 1]);
+            w.y = pack_bf16x2(pv[u * 8 + 2], pv[u * 8 + 3]);
+            w.z = pack_bf16x2(pv[u * 8 + 4], pv[u * 8 + 5]);
+            w.w = pack_bf16x2(pv[u * 8 + 6], pv[u * 8 + 7]);
+            *reinterpret_cast<uint4*>(ptile + tile_chunk_offset(r, c * 4 + u)) = w;
+          }
+        }
+        if (Cfg::kDP) {
+          float dv[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            dv[i] = pv[i] != 0.f ? pv[i] * (__uint_as_float(dr[i]) - delta_r) : 0.f;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 w;
+            w.x = pack_bf16x2(dv[u * 8 + 0], dv[u * 8 + 1]);
+            w.y = pack_bf16x2(dv[u * 8 + 2], dv[u * 8 + 3]);
+            w.z = pack_bf16x2(dv[u * 8 + 4], dv[u * 8 + 5]);
+            w.w = pack_bf16x2(dv[u * 8 + 6], dv[u * 8 + 7]);
+            *reinterpret_cast<uint4*>(dtile + tile_chunk_offset(r, c * 4 + u)) = w;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// =====================================================================================
+// tile GEMM kernel: dV = P^T dO, dK = dS^T Q (KV-major) and dQ = dS K (Q-major)
+// =====================================================================================
+enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2 };
+
+template <int D>
+struct GemmCfg {
+  static constexpr int kABytes = 16384;             // 128 rows x 64 deep
+  static constexpr int kBBytes = 64 * D * 2;        // 64 deep x D
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = D == 512 ? 2 : 4;
+};
+
+struct GemmMisc {
+  uint64_t full[4];
+  uint64_t empty[4];
+  uint64_t acc_full;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// One k-step of 64 (half a scratch tile): where A and B come from.
+struct GemmStep {
+  const uint8_t* a;  // scratch tile base
+  int half;          // 0 / 1: which 64 of the tile's 128 contraction rows
+  int b_head;        // TMA head coordinate for B
+  int b_row;         // TMA token coordinate for B (first of 64 rows)
+};
+
+template <int D, int WHICH>
+__global__ void __launch_bounds__(192, 1)
+    bwd_tile_gemm_kernel(const __grid_constant__ CUtensorMap tmB, const MatParams p) {
+  using Cfg = GemmCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_addr(smem) & 1023u) != 0) {
+    if (p.err) atomicCAS(p.err, 0, 5);
+    return;
+  }
+  GemmMisc* misc = reinterpret_cast<GemmMisc*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool packed = p.layout.packed();
+  const int G = p.group;
+
+  // ---- this CTA's output tile ----
+  int seq, tile, head;  // tile: key tile (dV/dK) or query tile (dQ) within the sequence
+  int qg = 0;           // dQ: global query-tile index
+  if (WHICH == kGemmDq) {
+    qg = blockIdx.x;
+    head = blockIdx.y;
+    if (packed ? qg >= *p.n_q_tiles : qg >= p.layout.batch * p.n_qt_fixed) return;
+    seq = p.ranges[qg].w;
+    tile = packed ? p.q_tiles[qg].y : qg % p.n_qt_fixed;
+  } else {
+    head = blockIdx.y;  // KV head
+    if (packed) {
+      if (static_cast<int>(blockIdx.x) >= *p.n_k_tiles) return;
+      const int2 t = p.k_tiles[blockIdx.x];
+      seq = t.x;
+      tile = t.y;
+    } else {
+      const int nkt = (p.layout.seqlen_k + kTileN - 1) / kTileN;
+      seq = blockIdx.x / nkt;
+      tile = blockIdx.x % nkt;
+    }
+  }
+  const SeqInfo si = p.layout.seq(seq);
+
+  // Enumerate the k-steps (two per scratch tile) in a fixed order shared by the
+  // producer and the MMA thread.
+  const int n_qt_seq = (si.len_q + kTileM - 1) / kTileM;
+  const int first_qg = packed ? (n_qt_seq > 0 ? p.seg_first_qtile[seq] : 0) : seq * p.n_qt_fixed;
+  auto for_each_tile = [&](auto&& fn) {
+    if (WHICH == kGemmDq) {
+      const int4 rg = p.ranges[qg];
+      const int kv_head = head / G;
+      if (rg.z + rg.y > p.head_cap_tiles) return;  // planner flagged an overflow
+      for (int j = 0; j < rg.y; ++j)
+        if (!fn(scratch_tile(p.ds_tiles, p, head, rg.z, j), kv_head,
+                si.k_base + (rg.x + j) * kTileN))
+          return;
+    } else {
+      uint8_t* base = WHICH == kGemmDv ? p.p_tiles : p.ds_tiles;
+      for (int gi = 0; gi < G; ++gi) {
+        const int qh = head * G + gi;
+        for (int qt = 0; qt < n_qt_seq; ++qt) {
+          const int4 rg = p.ranges[first_qg + qt];
+          if (tile < rg.x || tile >= rg.x + rg.y) continue;
+          if (rg.z + rg.y > p.head_cap_tiles) continue;  // planner flagged an overflow
+          if (!fn(scratch_tile(base, p, qh, rg.z, tile - rg.x), qh, si.q_base + qt * kTileM))
+            return;
+        }
+      }
+    }
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&misc->full[s], 1);
+      mbar_init(&misc->empty[s], 1);
+    }
+    mbar_init(&misc->acc_full, 1);
+    mbar_init(&misc->drain, 1);
+    misc->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(&misc->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc->tmem_base;
+  const CtaAbort ab{&misc->abort, p.err};
+
+  int n_steps = 0;
+  for_each_tile([&](const uint8_t*, int, int) {
+    n_steps += 2;
+    return true;
+  });
+
+  if (warp == 4) {
+    if (lane == 0 && n_steps > 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for_each_tile([&](const uint8_t* t, int b_head, int b_row) {
+        for (int h = 0; h < 2 && ok; ++h) {
+          const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+          ++it;
+          if (!(ok = mbar_wait(&misc->empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
+          uint8_t* dst = smem + st * Cfg::kStageBytes;
+          mbar_expect_tx(&misc->full[st], Cfg::kStageBytes);
+          if (WHICH == kGemmDq) {
+            bulk_load(dst, t + h * 16384, 16384, &misc->full[st]);
+          } else {
+            bulk_load(dst, t + h * 8192, 8192, &misc->full[st]);
+            bulk_load(dst + 8192, t + 16384 + h * 8192, 8192, &misc->full[st]);
+          }
+          for (int blk = 0; blk < D / 64; ++blk)
+            tma_load_4d(dst + Cfg::kABytes + blk * 8192, &tmB, &misc->full[st], blk * 64, b_head,
+                        b_row + h * 64, si.b_coord);
+        }
+        return ok;
+      });
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0 && n_steps > 0) {
+      constexpr uint32_t kId = idesc_bf16(128, 256, WHICH != kGemmDq, true);
+      const uint32_t sb0 = smem_addr(smem);
+      uint32_t it = 0;
+      bool ok = true;
+      for_each_tile([&](const uint8_t*, int, int) {
+        for (int h = 0; h < 2 && ok; ++h) {
+          const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+          const uint32_t first = it == 0;
+          ++it;
+          if (!(ok = mbar_wait(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
+          tc_fence_after();
+          const uint32_t a = sb0 + st * Cfg::kStageBytes;
+          const uint32_t bb = a + Cfg::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t adesc = WHICH == kGemmDq ? sdesc_sw128(a + kk * 32, 16, 1024)
+                                                    : sdesc_sw128(a + kk * 2048, 8192, 1024);
+#pragma unroll
+            for (int nh = 0; nh < D / 256; ++nh)
+              umma_ss(tmem + nh * 256, adesc, sdesc_sw128(bb + nh * 32768 + kk * 2048, 8192, 1024),
+                      kId, !(first && kk == 0));
+          }
+          umma_commit(&misc->empty[st]);
+        }
+        return ok;
+      });
+      umma_commit(&misc->acc_full);
+      umma_commit(&misc->drain);
+      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: TMEM -> bf16 rows ----------------
+    bool ok = true;
+    if (n_steps > 0) ok = mbar_wait(&misc->acc_full, 0, ab, kDevTimeoutMma);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    const bool have = ok && n_steps > 0;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int row = tile * 128 + tid;
+    const bool row_valid = WHICH == kGemmDq ? row < si.len_q : row < si.len_k;
+    __nv_bfloat16* dst;
+    if (WHICH == kGemmDq)
+      dst = p.dq + static_cast<int64_t>(si.b_coord) * p.dq_stride[0] +
+            static_cast<int64_t>(si.q_base + row) * p.dq_stride[1] + static_cast<int64_t>(head) * p.dq_stride[2];
+    else if (WHICH == kGemmDv)
+      dst = p.dv + static_cast<int64_t>(si.b_coord) * p.dv_stride[0] +
+            static_cast<int64_t>(si.k_base + row) * p.dv_stride[1] + static_cast<int64_t>(head) * p.dv_stride[2];
+    else
+      dst = p.dk + static_cast<int64_t>(si.b_coord) * p.dk_stride[0] +
+            static_cast<int64_t>(si.k_base + row) * p.dk_stride[1] + static_cast<int64_t>(head) * p.dk_stride[2];
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t r[32];
+      if (have) {
+        tmem_ld32(lane_base + c * 32, r);
+        tmem_wait_ld();
+        reg_fence32(r);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = 0u;
+      }
+      if (row_valid) {
+        uint4* out = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          out[i] = make_uint4(
+              pack_bf16x2(__uint_as_float(r[8 * i + 0]), __uint_as_float(r[8 * i + 1])),
+              pack_bf16x2(__uint_as_float(r[8 * i + 2]), __uint_as_float(r[8 * i + 3])),
+              pack_bf16x2(__uint_as_float(r[8 * i + 4]), __uint_as_float(r[8 * i + 5])),
+              pack_bf16x2(__uint_as_float(r[8 * i + 6]), __uint_as_float(r[8 * i + 7])));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// =====================================================================================
+// launchers
+// =====================================================================================
+int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream) {
+  plan_qtile_ranges_kernel<<<1, 1024, 0, stream>>>(p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int D, int MODE>
+static int launch_score_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                             const CUtensorMap& tdo, const MatParams& p, int grid_x,
+                             cudaStream_t stream) {
+  using Cfg = ScoreCfg<D, MODE>;
+  const int smem = Cfg::kQBytes + Cfg::kDoBytes + Cfg::kStages * 32768 + sizeof(ScoreMisc);
+  cudaError_t e = cudaFuncSetAttribute(bwd_score_kernel<D, MODE>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  dim3 grid(grid_x, p.num_q_heads);
+  bwd_score_kernel<D, MODE><<<grid, 192, smem, stream>>>(tq, tk, tv, tdo, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& tk,
+                     const CUtensorMap& tv, const CUtensorMap& tdo, const MatParams& p, int grid_x,
+                     cudaStream_t stream) {
+  if (d == 256) return launch_score_impl<256, kScorePdS>(tq, tk, tv, tdo, p, grid_x, stream);
+  if (pass == 0) return launch_score_impl<512, kScoreP>(tq, tk, tv, tdo, p, grid_x, stream);
+  return launch_score_impl<512, kScoreDs>(tq, tk, tv, tdo, p, grid_x, stream);
+}
+
+template <int D, int WHICH>
+static int launch_gemm_impl(const CUtensorMap& tb, const MatParams& p, int grid_x, int grid_y,
+                            cudaStream_t stream) {
+  using Cfg = GemmCfg<D>;
+  const int smem = Cfg::kStages * Cfg::kStageBytes + sizeof(GemmMisc);
+  cudaError_t e = cudaFuncSetAttribute(bwd_tile_gemm_kernel<D, WHICH>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  dim3 grid(grid_x, grid_y);
+  bwd_tile_gemm_kernel<D, WHICH><<<grid, 192, smem, stream>>>(tb, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const MatParams& p, int grid_x,
+                         int grid_y, cudaStream_t stream) {
+  if (d == 256) {
+    if (which == kGemmDv) return launch_gemm_impl<256, kGemmDv>(tb, p, grid_x, grid_y, stream);
+    if (which == kGemmDk) return launch_gemm_impl<256, kGemmDk>(tb, p, grid_x, grid_y, stream);
+    return launch_gemm_impl<256, kGemmDq>(tb, p, grid_x, grid_y, stream);
+  }
+  if (which == kGemmDv) return launch_gemm_impl<512, kGemmDv>(tb, p, grid_x, grid_y, stream);
+  if (which == kGemmDk) return launch_gemm_impl<512, kGemmDk>(tb, p, grid_x, grid_y, stream);
+  return launch_gemm_impl<512, kGemmDq>(tb, p, grid_x, grid_y, stream);
+}
+
+}  // namespace g4

@@ -7,6 +7,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -37,9 +38,22 @@ int cuda_fail(cudaError_t e, const char* what) {
 // ---------------------------------------------------------------------------------------
 // launch accounting / opt-in event timing
 // ---------------------------------------------------------------------------------------
-enum KernelId { kKFwd = 0, kKBwdPre, kKBwdDq, kKBwdDkv, kKPlan, kKMask, kKCount };
+enum KernelId {
+  kKFwd = 0,
+  kKBwdPre,
+  kKBwdDq,
+  kKBwdDkv,
+  kKPlan,
+  kKMask,
+  kKScore,
+  kKGemmDv,
+  kKGemmDk,
+  kKGemmDq,
+  kKCount
+};
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
-                                           "plan", "mask"};
+                                           "plan",     "mask",           "bwd_score",
+                                           "bwd_gemm_dv", "bwd_gemm_dk", "bwd_gemm_dq"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -169,15 +183,49 @@ struct Workspace {
   size_t pair_first = 0;   // int[meta_len] (backward)
   size_t delta = 0;        // float[Hq * tokens_q]
   size_t lse2 = 0;         // float[Hq * tokens_q]
+  // materialised-P/dS backward only
+  size_t seg_first = 0;    // int[B] (packed)
+  size_t ranges = 0;       // int4[n_qt_total]
+  size_t p_tiles = 0;      // Hq * head_cap tiles of 32 KB
+  size_t ds_tiles = 0;
+  bool materialized = false;
+  int n_qt_total = 0;
+  int64_t head_cap_tiles = 0;
   size_t total = 0;
   int max_q_tiles = 0;
   int max_k_tiles = 0;
   int64_t tokens_q = 0;
 };
 
+// Upper bound of scratch tiles per query head for the materialised backward:
+// exact band sizes for fixed layouts, a per-tile bound for packed layouts.
+int64_t mat_head_cap_tiles(const g4_attn_args* a, int n_qt_total) {
+  const bool packed = a->cu_seqlens_q != nullptr;
+  const int W = a->window;
+  if (packed) {
+    const int64_t kmax = (a->max_seqlen_k + g4::kTileN - 1) / g4::kTileN;
+    int64_t per = kmax;
+    if (W > 0) per = std::min<int64_t>(per, (W + 126) / g4::kTileN + 2);
+    return per * n_qt_total;
+  }
+  const int n_qt = (a->seqlen_q + g4::kTileM - 1) / g4::kTileM;
+  const int q_off = a->seqlen_k - a->seqlen_q;
+  int64_t total = 0;
+  for (int qt = 0; qt < n_qt; ++qt) {
+    const int qa0 = qt * g4::kTileM + q_off;
+    const int qa1 = std::min((qt + 1) * g4::kTileM, a->seqlen_q) - 1 + q_off;
+    const int lo = W > 0 ? std::max(0, qa0 - W + 1) : 0;
+    const int hi = std::min(qa1, a->seqlen_k - 1);
+    if (hi >= lo) total += hi / g4::kTileN - lo / g4::kTileN + 1;
+  }
+  return total * a->batch;
+}
+
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-Workspace plan_workspace(const g4_attn_args* a, bool backward) {
+// backward == 2 requests the materialised-P/dS layout (ignored when the call is
+// not eligible: vision metadata needs data-dependent key ranges).
+Workspace plan_workspace(const g4_attn_args* a, int backward) {
   Workspace w;
   const bool packed = a->cu_seqlens_q != nullptr;
   size_t off = 256;
@@ -206,6 +254,23 @@ Workspace plan_workspace(const g4_attn_args* a, bool backward) {
     off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
     w.lse2 = off;
     off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
+    if (backward == 2 && !(a->vision_ids && a->window > 0)) {
+      w.materialized = true;
+      w.n_qt_total = packed ? w.max_q_tiles
+                            : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
+      if (packed) {
+        w.seg_first = off;
+        off = align256(off + sizeof(int) * a->batch);
+      }
+      w.ranges = off;
+      off = align256(off + sizeof(int4) * w.n_qt_total);
+      w.head_cap_tiles = mat_head_cap_tiles(a, w.n_qt_total);
+      const size_t tiles = size_t(a->num_q_heads) * size_t(w.head_cap_tiles) * 32768;
+      w.p_tiles = off;
+      off = align256(off + tiles);
+      w.ds_tiles = off;
+      off = align256(off + tiles);
+    }
   }
   w.total = off;
   return w;
@@ -239,12 +304,13 @@ int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream
   if (a->cu_seqlens_q) {
     LaunchScope ls(kKPlan, st);
     int rc = g4::launch_plan_tiles(a->cu_seqlens_q, a->batch, g4::kTileM,
-                                   ws_ptr<int2>(a, w.q_tiles), hdr + 1, st);
+                                   ws_ptr<int2>(a, w.q_tiles), hdr + 1,
+                                   w.seg_first ? ws_ptr<int>(a, w.seg_first) : nullptr, st);
     if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "q tile planning");
     if (backward) {
       LaunchScope ls2(kKPlan, st);
       rc = g4::launch_plan_tiles(a->cu_seqlens_k, a->batch, g4::kTileN,
-                                 ws_ptr<int2>(a, w.k_tiles), hdr + 2, st);
+                                 ws_ptr<int2>(a, w.k_tiles), hdr + 2, nullptr, st);
       if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "k tile planning");
     }
   }
@@ -305,7 +371,12 @@ size_t g4_attn_fwd_workspace_bytes(const g4_attn_args* args) {
 
 size_t g4_attn_bwd_workspace_bytes(const g4_attn_args* args) {
   if (!args) return 0;
-  return plan_workspace(args, true).total;
+  return plan_workspace(args, 2).total;
+}
+
+size_t g4_attn_bwd_min_workspace_bytes(const g4_attn_args* args) {
+  if (!args) return 0;
+  return plan_workspace(args, 1).total;
 }
 
 int g4_attn_fwd(const g4_attn_args* a, void* stream) {
@@ -316,7 +387,7 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
   if (!packed && (a->lse_stride[0] <= 0 || a->lse_stride[1] <= 0))
     return fail(G4_ERR_INVALID, "lse strides must be positive");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const Workspace w = plan_workspace(a, false);
+  const Workspace w = plan_workspace(a, 0);
   g4::FwdParams p;
   memset(&p, 0, sizeof(p));
   if ((rc = prepare(a, w, false, st, &p.mask))) return rc;
@@ -370,7 +441,11 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
   if (!packed && (a->lse_stride[0] <= 0 || a->lse_stride[1] <= 0))
     return fail(G4_ERR_INVALID, "lse strides must be positive");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const Workspace w = plan_workspace(a, true);
+  // Materialised P/dS when eligible and the workspace holds the scratch,
+  // otherwise the recompute kernels (small workspaces, vision metadata).
+  const Workspace wm = plan_workspace(a, 2);
+  const Workspace w =
+      (wm.materialized && a->workspace && a->workspace_bytes >= wm.total) ? wm : plan_workspace(a, 1);
   g4::BwdParams p;
   memset(&p, 0, sizeof(p));
   if ((rc = prepare(a, w, true, st, &p.mask))) return rc;
@@ -429,6 +504,69 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     return rc;
   const int gq = packed ? w.max_q_tiles : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
   const int gk = packed ? w.max_k_tiles : a->batch * ((a->seqlen_k + g4::kTileN - 1) / g4::kTileN);
+  if (w.materialized) {
+    g4::MatParams m;
+    memset(&m, 0, sizeof(m));
+    m.layout = p.layout;
+    m.mask = p.mask;
+    m.group = p.group;
+    m.num_q_heads = a->num_q_heads;
+    m.n_qt_fixed = packed ? 0 : (a->seqlen_q + g4::kTileM - 1) / g4::kTileM;
+    m.q_tiles = p.q_tiles;
+    m.n_q_tiles = p.n_q_tiles;
+    m.k_tiles = p.k_tiles;
+    m.n_k_tiles = p.n_k_tiles;
+    m.seg_first_qtile = packed ? ws_ptr<int>(a, w.seg_first) : nullptr;
+    m.ranges = ws_ptr<int4>(a, w.ranges);
+    m.head_cap_tiles = w.head_cap_tiles;
+    m.p_tiles = ws_ptr<uint8_t>(a, w.p_tiles);
+    m.ds_tiles = ws_ptr<uint8_t>(a, w.ds_tiles);
+    m.lse2 = p.lse2;
+    m.delta = p.delta;
+    m.ws_head_stride = p.ws_head_stride;
+    m.dq = p.dq;
+    m.dk = p.dk;
+    m.dv = p.dv;
+    for (int i = 0; i < 3; ++i) {
+      m.dq_stride[i] = p.dq_stride[i];
+      m.dk_stride[i] = p.dk_stride[i];
+      m.dv_stride[i] = p.dv_stride[i];
+    }
+    m.err = p.err;
+    CUtensorMap tq64, tdo64;
+    if ((rc = make_map(&tq64, a->q, D, a->num_q_heads, a->seqlen_q, bq, a->q_stride[2],
+                       a->q_stride[1], a->q_stride[0], 64)))
+      return rc;
+    if ((rc = make_map(&tdo64, a->dout, a->head_dim_v, a->num_q_heads, a->seqlen_q, bq,
+                       a->do_stride[2], a->do_stride[1], a->do_stride[0], 64)))
+      return rc;
+    {
+      LaunchScope ls(kKPlan, st);
+      e = g4::launch_plan_qtile_ranges(m, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "query-tile range planning");
+    }
+    for (int pass = 0; pass < (D == 512 ? 2 : 1); ++pass) {
+      LaunchScope ls(kKScore, st);
+      e = g4::launch_bwd_score(D, pass, tq, tk, tv, tdo, m, w.n_qt_total, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "score launch");
+    }
+    {
+      LaunchScope ls(kKGemmDv, st);
+      e = g4::launch_bwd_tile_gemm(D, 0, tdo64, m, gk, a->num_kv_heads, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV launch");
+    }
+    {
+      LaunchScope ls(kKGemmDk, st);
+      e = g4::launch_bwd_tile_gemm(D, 1, tq64, m, gk, a->num_kv_heads, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK launch");
+    }
+    {
+      LaunchScope ls(kKGemmDq, st);
+      e = g4::launch_bwd_tile_gemm(D, 2, tk64, m, w.n_qt_total, a->num_q_heads, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "dQ launch");
+    }
+    return G4_OK;
+  }
   {
     LaunchScope ls(kKBwdDq, st);
     e = D == 256 ? g4::launch_bwd_dq<256>(tq, tk, tk64, tv, tdo, p, gq, st)
@@ -447,7 +585,7 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
 int g4_attn_bwd_noalloc(const g4_attn_args* a, void* stream) {
   g_last_error.clear();
   if (!a) return fail(G4_ERR_INVALID, "null argument block");
-  const size_t need = plan_workspace(a, true).total;
+  const size_t need = plan_workspace(a, 1).total;
   if (need > G4_NOALLOC_SCRATCH_BYTES)
     return fail(G4_ERR_WORKSPACE,
                 "this backward needs %zu bytes of scratch; the allocation-free entry point has "

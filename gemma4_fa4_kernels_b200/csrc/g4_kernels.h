@@ -51,6 +51,43 @@ struct BwdParams {
   int* err;
 };
 
+// Backward with materialised P / dS scratch tiles (attn_bwd_mat.cu).
+struct MatParams {
+  SeqLayout layout;
+  MaskSpec mask;                   // window and documents only (no vision)
+  int group;
+  int num_q_heads;
+  int n_qt_fixed;                  // fixed layout: query tiles per sequence
+  const int2* q_tiles;             // packed: (segment, q tile) list, else null
+  const int* n_q_tiles;
+  const int2* k_tiles;
+  const int* n_k_tiles;
+  const int* seg_first_qtile;      // packed: list index of each segment's first q tile
+  int4* ranges;                    // per query tile: kt_lo, n_kt, scratch offset, sequence
+  int64_t head_cap_tiles;          // scratch tiles reserved per query head
+  uint8_t* p_tiles;
+  uint8_t* ds_tiles;
+  const float* lse2;
+  const float* delta;
+  int64_t ws_head_stride;
+  __nv_bfloat16* dq;
+  int64_t dq_stride[3];
+  __nv_bfloat16* dk;
+  int64_t dk_stride[3];
+  __nv_bfloat16* dv;
+  int64_t dv_stride[3];
+  int* err;
+};
+
+int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream);
+// pass: d512 runs pass 0 (P) then pass 1 (dS); d256 computes both in pass 0.
+int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& tk,
+                     const CUtensorMap& tv, const CUtensorMap& tdo, const MatParams& p, int grid_x,
+                     cudaStream_t stream);
+// which: 0 = dV (B = dO), 1 = dK (B = Q), 2 = dQ (B = K); maps use 64-row boxes.
+int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const MatParams& p, int grid_x,
+                         int grid_y, cudaStream_t stream);
+
 template <int DQK>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                const FwdParams& p, int grid_x, int num_q_heads, int slabs, cudaStream_t stream);
@@ -72,7 +109,7 @@ int launch_bwd_dkv(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
 
 // planning kernels (plan.cu)
 int launch_plan_tiles(const int* cu, int nseg, int tile, int2* tiles, int* n_tiles,
-                      cudaStream_t stream);
+                      int* seg_first, cudaStream_t stream);
 int launch_pair_last(const SeqLayout& layout, const int* vis, const int* doc, int* pair_last,
                      int* pair_first, int nseq, cudaStream_t stream);
 

@@ -22,7 +22,7 @@
 namespace g4 {
 
 __global__ void plan_tiles_kernel(const int* __restrict__ cu, int nseg, int tile, int2* tiles,
-                                  int* n_tiles) {
+                                  int* n_tiles, int* seg_first) {
   __shared__ int scan[1024];
   __shared__ int carry;
   const int tid = threadIdx.x;
@@ -42,6 +42,7 @@ __global__ void plan_tiles_kernel(const int* __restrict__ cu, int nseg, int tile
     }
     const int start = carry + scan[tid] - cnt;
     for (int t = 0; t < cnt; ++t) tiles[start + t] = make_int2(s, t);
+    if (seg_first && s < nseg) seg_first[s] = start;
     __syncthreads();
     if (tid == 1023) carry += scan[1023];
     __syncthreads();
@@ -50,8 +51,8 @@ __global__ void plan_tiles_kernel(const int* __restrict__ cu, int nseg, int tile
 }
 
 int launch_plan_tiles(const int* cu, int nseg, int tile, int2* tiles, int* n_tiles,
-                      cudaStream_t stream) {
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(cu, nseg, tile, tiles, n_tiles);
+                      int* seg_first, cudaStream_t stream) {
+  plan_tiles_kernel<<<1, 1024, 0, stream>>>(cu, nseg, tile, tiles, n_tiles, seg_first);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -79,6 +79,17 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
+# The materialised-P/dS backward is used when its scratch fits this budget
+# (the smaller of 24 GiB and half the free device memory); otherwise the
+# recompute kernels run with a small workspace.
+_SCRATCH_CAP = 24 * 1024**3
+
+
+def _scratch_budget(device) -> int:
+    free, _total = torch.cuda.mem_get_info(device)
+    return min(_SCRATCH_CAP, free // 2)
+
+
 def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -108,8 +119,11 @@ def attn_fwd(q, k, v, *, window=0, vision_ids=None, document_ids=None, cu_seqlen
 
 def attn_bwd(q, k, v, out, lse, dout, *, dlse=None, window=0, vision_ids=None,
              document_ids=None, cu_seqlens_q=None, cu_seqlens_k=None, max_seqlen_q=None,
-             max_seqlen_k=None, dq=None, dk=None, dv=None):
-    """Backward through ``g4_attn_bwd``; returns ``(dq, dk, dv)``."""
+             max_seqlen_k=None, dq=None, dk=None, dv=None, algorithm="auto"):
+    """Backward through ``g4_attn_bwd``; returns ``(dq, dk, dv)``.
+
+    ``algorithm``: "auto" materialises P/dS when the scratch fits the budget,
+    "recompute" always passes the minimum workspace (recompute kernels)."""
     lib = _lib.load()
     packed = cu_seqlens_q is not None
     dev = q.device
@@ -133,7 +147,15 @@ def attn_bwd(q, k, v, out, lse, dout, *, dlse=None, window=0, vision_ids=None,
     a.dq_stride = _strides3(dq, packed)
     a.dk_stride = _strides3(dk, packed)
     a.dv_stride = _strides3(dv, packed)
-    ws = _workspace(lib.g4_attn_bwd_workspace_bytes(ctypes.byref(a)), dev)
+    full = lib.g4_attn_bwd_workspace_bytes(ctypes.byref(a))
+    small = lib.g4_attn_bwd_min_workspace_bytes(ctypes.byref(a))
+    if algorithm == "recompute" or full > _scratch_budget(dev):
+        nbytes = small
+    elif algorithm in ("auto", "materialized"):
+        nbytes = full
+    else:
+        raise ValueError(f"unknown backward algorithm {algorithm!r}")
+    ws = _workspace(nbytes, dev)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _raise_for(lib.g4_attn_bwd(ctypes.byref(a), _stream(dev)), "g4_attn_bwd")
     return dq, dk, dv

@@ -1,0 +1,55 @@
+"""Run a few forward+backward steps of one benchmark configuration, for profilers.
+
+    python -m gemma4_fa4_kernels_b200.profile_step --config c1 --steps 1
+
+Configs: c0 (local d256 W1024, S=2048, 32Q/16KV) and c1 (global d512 causal,
+S=4096, 32Q/4KV), B=1, BF16, inputs as in bench.py.  Inputs exceed the 126 MB
+L2 for c1.  Prints nothing but the per-step wall time; meant to be wrapped by
+ncu with -k/-c filters.
+"""
+
+from __future__ import annotations
+
+import argparse
+import time
+
+import torch
+
+from . import ops
+
+CONFIGS = {
+    "c0": dict(seq=2048, hq=32, hkv=16, d=256, window=1024),
+    "c1": dict(seq=4096, hq=32, hkv=4, d=512, window=0),
+}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
+    ap.add_argument("--steps", type=int, default=1)
+    ap.add_argument("--seq", type=int, default=None, help="override the sequence length")
+    args = ap.parse_args()
+    c = dict(CONFIGS[args.config])
+    if args.seq:
+        c["seq"] = args.seq
+    g = torch.Generator().manual_seed(0)
+    dev = torch.device("cuda", 0)
+
+    def rms(x):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+
+    s, hq, hkv, d = c["seq"], c["hq"], c["hkv"], c["d"]
+    q = rms(torch.randn(1, s, hq, d, generator=g)).to(torch.bfloat16).to(dev)
+    k = rms(torch.randn(1, s, hkv, d, generator=g)).to(torch.bfloat16).to(dev)
+    v = rms(torch.randn(1, s, hkv, d, generator=g)).to(torch.bfloat16).to(dev)
+    do = torch.randn(1, s, hq, d, generator=g).to(torch.bfloat16).to(dev)
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        out, lse = ops.attn_fwd(q, k, v, window=c["window"])
+        ops.attn_bwd(q, k, v, out, lse, do, window=c["window"])
+        torch.cuda.synchronize()
+        print(f"step {time.perf_counter() - t0:.4f} s", flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -111,8 +111,16 @@ size_t g4_attn_fwd_workspace_bytes(const g4_attn_args* args);
  */
 int g4_attn_fwd(const g4_attn_args* args, void* stream);
 
-/* Workspace bytes g4_attn_bwd needs for these arguments (no device access). */
+/*
+ * Workspace bytes for g4_attn_bwd (no device access).  The full size lets the
+ * backward materialise P and dS once as bf16 scratch tiles in HBM (every
+ * backward matmul done exactly once; about 64 KB per query head and visible
+ * 128x128 tile); the minimum size runs kernels that recompute S and dP
+ * instead.  g4_attn_bwd picks the materialised path whenever it is eligible
+ * (no vision metadata) and workspace_bytes is at least the full size.
+ */
 size_t g4_attn_bwd_workspace_bytes(const g4_attn_args* args);
+size_t g4_attn_bwd_min_workspace_bytes(const g4_attn_args* args);
 
 /*
  * Attention backward: dQ, dK, dV from (Q, K, V, O, LSE, dO[, dLSE]).
@@ -165,8 +173,10 @@ int g4_build_mask(uint8_t* out, int32_t batch, int32_t q_len, int32_t kv_len, in
 /*
  * Launch accounting and opt-in timing (benchmark/profiling support; no
  * reference counterpart -- the reference times whole Python calls).
- * Kernel ids: 0 forward, 1 backward preprocess, 2 backward dQ, 3 backward
- * dK/dV, 4 planning (tile lists, vision pairs), 5 mask builder.
+ * Kernel ids: 0 forward, 1 backward preprocess, 2 backward dQ (recompute),
+ * 3 backward dK/dV (recompute), 4 planning (tile lists, vision pairs, tile
+ * ranges), 5 mask builder, 6 backward P/dS scores, 7-9 backward dV / dK / dQ
+ * tile GEMMs (materialised path).
  *  - g4_launch_count: launches of `kernel_id` issued by this process so far.
  *  - g4_profile_enable(1): every later launch is bracketed by CUDA events on
  *    its own stream; g4_profile_read synchronises those events and returns the

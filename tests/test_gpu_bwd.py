@@ -132,3 +132,19 @@ def test_backward_is_deterministic():
     torch.cuda.synchronize()
     for a, b in zip(g1, g2):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("shape", [(1, 300, 4, 2, 256, 1024), (1, 260, 8, 1, 512, 0)],
+                         ids=["local_d256", "global_d512"])
+def test_recompute_and_materialized_backward_agree_with_oracle(shape):
+    b, s, hq, hkv, d, window = shape
+    q, k, v, dout = make_inputs((b, s, hq, d), (b, s, hkv, d), (b, s, hkv, d), seed=71)
+    out, lse = ops.attn_fwd(q, k, v, window=window)
+    rq, rk, rv = oracle.attention_bwd(bshd_to_bhsd_np(q), bshd_to_bhsd_np(k), bshd_to_bhsd_np(v),
+                                      bshd_to_bhsd_np(dout), sliding_window=window or None,
+                                      allow_vision_bidirectional=window > 0)
+    for algo in ("recompute", "materialized"):
+        dq, dk, dv = ops.attn_bwd(q, k, v, out, lse, dout, window=window, algorithm=algo)
+        torch.cuda.synchronize()
+        for name, got, ref in (("dq", dq, rq), ("dk", dk, rk), ("dv", dv, rv)):
+            assert_close_to_oracle(f"{algo} {name}", bshd_to_bhsd_np(got), ref)
