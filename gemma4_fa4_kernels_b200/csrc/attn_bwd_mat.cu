@@ -128,8 +128,11 @@ struct ScoreMisc {
   int abort;
 };
 
+constexpr int kScoreThreads = 320;  // 8 math warps + producer + MMA
+constexpr int kScoreMathThreads = 256;
+
 template <int D, int MODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kScoreThreads, 1)
     bwd_score_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmDO, const MatParams p) {
@@ -145,12 +148,12 @@ __global__ void __launch_bounds__(192, 1)
   ScoreMisc* misc = reinterpret_cast<ScoreMisc*>(ring + Cfg::kStages * 32768);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = blockIdx.x;
   const int head = blockIdx.y;
   const int kv_head = head / p.group;
   const bool packed = p.layout.packed();
-  if (packed && g >= *p.n_q_tiles) return;
-  if (!packed && g >= p.layout.batch * p.n_qt_fixed) return;
+  const int n_tiles = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
+  if (static_cast<int>(blockIdx.x) >= n_tiles) return;
+  const int g = n_tiles - 1 - static_cast<int>(blockIdx.x);  // longest causal rows first
   const int4 rg = p.ranges[g];
   const int kt_lo = rg.x, n_kt = rg.y, t_off = rg.z, seq = rg.w;
   const int qt = packed ? p.q_tiles[g].y : g % p.n_qt_fixed;
@@ -167,13 +170,13 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&misc->s_full[b], 1);
-      mbar_init(&misc->buf_free[b], kTileM);
+      mbar_init(&misc->buf_free[b], kScoreMathThreads);
     }
     mbar_init(&misc->drain, 1);
     misc->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(&misc->tmem_base, 512);
     tmem_relinquish();
   }
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(192, 1)
   auto s_col = [](int b) { return static_cast<uint32_t>(b * 256); };
   auto dp_col = [](int b) { return static_cast<uint32_t>(b * 256 + 128); };
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0 && work > 0) {
       mbar_expect_tx(&misc->res_full, Cfg::kQBytes + Cfg::kDoBytes);
       const int qrow = si.q_base + qt * kTileM;
@@ -215,7 +218,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0 && work > 0) {
       constexpr uint32_t kId = idesc_bf16(128, 128, false, false);
       const uint32_t qb = smem_addr(q_s), db = smem_addr(do_s), rb = smem_addr(ring);
@@ -253,8 +256,10 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ---------------- math warps: P / dS tiles to HBM ----------------
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const int r = tid;  // row in the query tile
+    // warp w reads TMEM lanes 32*(w%4).. (its rows) and columns [64*(w/4), +64)
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int r = (warp & 3) * 32 + lane;  // row in the query tile
+    const int c_begin = (warp >> 2) * 2;   // first of this warp's two 32-column chunks
     const int q_idx = qt * kTileM + r;
     const bool row_valid = q_idx < si.len_q;
     const int q_abs = q_idx + q_off;
@@ -275,7 +280,7 @@ __global__ void __launch_bounds__(192, 1)
       uint8_t* ptile = Cfg::kS || MODE == kScoreDs ? scratch_tile(p.p_tiles, p, head, t_off, j) : nullptr;
       uint8_t* dtile = Cfg::kDP ? scratch_tile(p.ds_tiles, p, head, t_off, j) : nullptr;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = c_begin; c < c_begin + 2; ++c) {
         uint32_t sr[32], dr[32];
         if (Cfg::kS && Cfg::kDP) {
           tmem_ld32(lane_base + s_col(b) + c * 32, sr);
@@ -292,7 +297,7 @@ __global__ void __launch_bounds__(192, 1)
           tmem_wait_ld();
           reg_fence32(dr);
         }
-        if (c == 3) {  // every TMEM value of this buffer is now in registers
+        if (c == c_begin + 1) {  // this warp's TMEM values are all in registers
           tc_fence_before();
           mbar_arrive(&misc->buf_free[b]);
         }
@@ -354,7 +359,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -365,12 +370,16 @@ __global__ void __launch_bounds__(192, 1)
 // =====================================================================================
 enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2 };
 
-template <int D>
+// dQ CTAs produce all D output columns (A loaded once); dV / dK CTAs produce
+// one 256-column half each, which doubles the KV-major grid for load balance.
+template <int D, int WHICH>
 struct GemmCfg {
+  static constexpr int kNB = WHICH == 2 ? D : 256;  // output columns per CTA
+  static constexpr int kHalves = D / kNB;
   static constexpr int kABytes = 16384;             // 128 rows x 64 deep
-  static constexpr int kBBytes = 64 * D * 2;        // 64 deep x D
+  static constexpr int kBBytes = 64 * kNB * 2;      // 64 deep x kNB
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = D == 512 ? 2 : 4;
+  static constexpr int kStages = kStageBytes > 64 * 1024 ? 2 : 4;
 };
 
 struct GemmMisc {
@@ -393,7 +402,7 @@ struct GemmStep {
 template <int D, int WHICH>
 __global__ void __launch_bounds__(192, 1)
     bwd_tile_gemm_kernel(const __grid_constant__ CUtensorMap tmB, const MatParams p) {
-  using Cfg = GemmCfg<D>;
+  using Cfg = GemmCfg<D, WHICH>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if ((smem_addr(smem) & 1023u) != 0) {
     if (p.err) atomicCAS(p.err, 0, 5);
@@ -404,26 +413,34 @@ __global__ void __launch_bounds__(192, 1)
   const bool packed = p.layout.packed();
   const int G = p.group;
 
-  // ---- this CTA's output tile ----
+  // ---- this CTA's output tile (heaviest causal work scheduled first) ----
   int seq, tile, head;  // tile: key tile (dV/dK) or query tile (dQ) within the sequence
   int qg = 0;           // dQ: global query-tile index
+  int half = 0;         // dV/dK: which 256-column half
   if (WHICH == kGemmDq) {
-    qg = blockIdx.x;
+    const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
+    if (static_cast<int>(blockIdx.x) >= n) return;
+    qg = n - 1 - static_cast<int>(blockIdx.x);
     head = blockIdx.y;
-    if (packed ? qg >= *p.n_q_tiles : qg >= p.layout.batch * p.n_qt_fixed) return;
     seq = p.ranges[qg].w;
     tile = packed ? p.q_tiles[qg].y : qg % p.n_qt_fixed;
   } else {
-    head = blockIdx.y;  // KV head
+    const int hkv = p.num_q_heads / G;
+    const int per_item = hkv * Cfg::kHalves;
+    const int item = blockIdx.x / per_item;
+    const int rest = blockIdx.x % per_item;
+    head = rest / Cfg::kHalves;  // KV head
+    half = rest % Cfg::kHalves;
     if (packed) {
-      if (static_cast<int>(blockIdx.x) >= *p.n_k_tiles) return;
-      const int2 t = p.k_tiles[blockIdx.x];
+      if (item >= *p.n_k_tiles) return;
+      const int2 t = p.k_tiles[item];
       seq = t.x;
       tile = t.y;
     } else {
       const int nkt = (p.layout.seqlen_k + kTileN - 1) / kTileN;
-      seq = blockIdx.x / nkt;
-      tile = blockIdx.x % nkt;
+      if (item >= nkt * p.layout.batch) return;
+      tile = item / p.layout.batch;  // key tile 0 (most causal work) of every sequence first
+      seq = item % p.layout.batch;
     }
   }
   const SeqInfo si = p.layout.seq(seq);
@@ -499,9 +516,9 @@ __global__ void __launch_bounds__(192, 1)
             bulk_load(dst, t + h * 8192, 8192, &misc->full[st]);
             bulk_load(dst + 8192, t + 16384 + h * 8192, 8192, &misc->full[st]);
           }
-          for (int blk = 0; blk < D / 64; ++blk)
-            tma_load_4d(dst + Cfg::kABytes + blk * 8192, &tmB, &misc->full[st], blk * 64, b_head,
-                        b_row + h * 64, si.b_coord);
+          for (int blk = 0; blk < Cfg::kNB / 64; ++blk)
+            tma_load_4d(dst + Cfg::kABytes + blk * 8192, &tmB, &misc->full[st],
+                        half * 256 + blk * 64, b_head, b_row + h * 64, si.b_coord);
         }
         return ok;
       });
@@ -527,7 +544,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t adesc = WHICH == kGemmDq ? sdesc_sw128(a + kk * 32, 16, 1024)
                                                     : sdesc_sw128(a + kk * 2048, 8192, 1024);
 #pragma unroll
-            for (int nh = 0; nh < D / 256; ++nh)
+            for (int nh = 0; nh < Cfg::kNB / 256; ++nh)
               umma_ss(tmem + nh * 256, adesc, sdesc_sw128(bb + nh * 32768 + kk * 2048, 8192, 1024),
                       kId, !(first && kk == 0));
           }
@@ -560,8 +577,9 @@ __global__ void __launch_bounds__(192, 1)
     else
       dst = p.dk + static_cast<int64_t>(si.b_coord) * p.dk_stride[0] +
             static_cast<int64_t>(si.k_base + row) * p.dk_stride[1] + static_cast<int64_t>(head) * p.dk_stride[2];
+    dst += half * 256;
 #pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
+    for (int c = 0; c < Cfg::kNB / 32; ++c) {
       uint32_t r[32];
       if (have) {
         tmem_ld32(lane_base + c * 32, r);
@@ -610,7 +628,7 @@ static int launch_score_impl(const CUtensorMap& tq, const CUtensorMap& tk, const
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
   dim3 grid(grid_x, p.num_q_heads);
-  bwd_score_kernel<D, MODE><<<grid, 192, smem, stream>>>(tq, tk, tv, tdo, p);
+  bwd_score_kernel<D, MODE><<<grid, kScoreThreads, smem, stream>>>(tq, tk, tv, tdo, p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -625,7 +643,11 @@ int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& 
 template <int D, int WHICH>
 static int launch_gemm_impl(const CUtensorMap& tb, const MatParams& p, int grid_x, int grid_y,
                             cudaStream_t stream) {
-  using Cfg = GemmCfg<D>;
+  using Cfg = GemmCfg<D, WHICH>;
+  if (WHICH != kGemmDq) {  // KV-major: (key tile, KV head, half) all along x
+    grid_x *= grid_y * Cfg::kHalves;
+    grid_y = 1;
+  }
   const int smem = Cfg::kStages * Cfg::kStageBytes + sizeof(GemmMisc);
   cudaError_t e = cudaFuncSetAttribute(bwd_tile_gemm_kernel<D, WHICH>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

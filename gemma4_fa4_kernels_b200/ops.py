@@ -80,14 +80,20 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
 
 
 # The materialised-P/dS backward is used when its scratch fits this budget
-# (the smaller of 24 GiB and half the free device memory); otherwise the
-# recompute kernels run with a small workspace.
+# (the smaller of 24 GiB and a quarter of the device's memory); otherwise the
+# recompute kernels run with a small workspace.  The budget is fixed per
+# device: querying free memory on every call costs more than a whole
+# backward at the benchmark sizes.
 _SCRATCH_CAP = 24 * 1024**3
+_budget_cache: dict[int, int] = {}
 
 
 def _scratch_budget(device) -> int:
-    free, _total = torch.cuda.mem_get_info(device)
-    return min(_SCRATCH_CAP, free // 2)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _budget_cache:
+        total = torch.cuda.get_device_properties(idx).total_memory
+        _budget_cache[idx] = min(_SCRATCH_CAP, total // 4)
+    return _budget_cache[idx]
 
 
 def _stream(device) -> int:
@@ -155,7 +161,12 @@ def attn_bwd(q, k, v, out, lse, dout, *, dlse=None, window=0, vision_ids=None,
         nbytes = full
     else:
         raise ValueError(f"unknown backward algorithm {algorithm!r}")
-    ws = _workspace(nbytes, dev)
+    try:
+        ws = _workspace(nbytes, dev)
+    except torch.cuda.OutOfMemoryError:
+        if nbytes == small:
+            raise
+        ws = _workspace(small, dev)  # no room for the scratch: recompute kernels
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _raise_for(lib.g4_attn_bwd(ctypes.byref(a), _stream(dev)), "g4_attn_bwd")
     return dq, dk, dv
