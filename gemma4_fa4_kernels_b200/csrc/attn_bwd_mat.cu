@@ -115,14 +115,28 @@ struct ScoreCfg {
   static constexpr int kDoBytes = kDP ? D * kTileM * 2 : 0;
   static constexpr int kStages = 3;
   static constexpr int kChunksPerTile = (kS ? D / 128 : 0) + (kDP ? D / 128 : 0);
+  // d512 single-product passes keep their resident operand (Q or dO) in TMEM
+  // and issue TS MMAs: only B is read from shared memory, which halves the
+  // shared-memory read traffic of the 128x128x512 products.  The freed shared
+  // memory then holds a ring of P tiles for the dS pass.
+  static constexpr bool kTS = D == 512 && MODE != kScorePdS;
+  // TS variant: once the resident operand sits in TMEM its 128 KB of shared
+  // memory extends the operand ring (more bytes in flight per SM): the P pass
+  // gets 3 + 4 K stages; the dS pass 3 + 2 V stages and 2 P stages.
+  static constexpr int kExtraStages = kTS ? (MODE == kScoreP ? 4 : 2) : 0;
+  static constexpr int kRingStages = kStages + kExtraStages;
+  static constexpr int kPStages = 2;
 };
 
 struct ScoreMisc {
   uint64_t res_full;
-  uint64_t ring_full[4];
-  uint64_t ring_empty[4];
+  uint64_t a_ready;       // resident operand copied into TMEM (TS variant)
+  uint64_t ring_full[8];
+  uint64_t ring_empty[8];
   uint64_t s_full[2];
   uint64_t buf_free[2];
+  uint64_t p_full[4];     // P tiles in shared memory (dS pass, TS variant)
+  uint64_t p_empty[4];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -164,7 +178,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
 
   if (tid == 0) {
     mbar_init(&misc->res_full, 1);
-    for (int s = 0; s < Cfg::kStages; ++s) {
+    for (int s = 0; s < Cfg::kRingStages; ++s) {
       mbar_init(&misc->ring_full[s], 1);
       mbar_init(&misc->ring_empty[s], 1);
     }
@@ -172,6 +186,11 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       mbar_init(&misc->s_full[b], 1);
       mbar_init(&misc->buf_free[b], kScoreMathThreads);
     }
+    for (int s2 = 0; s2 < 4; ++s2) {
+      mbar_init(&misc->p_full[s2], 1);
+      mbar_init(&misc->p_empty[s2], kScoreMathThreads);
+    }
+    mbar_init(&misc->a_ready, kScoreMathThreads);
     mbar_init(&misc->drain, 1);
     misc->abort = 0;
     fence_mbar_init();
@@ -186,9 +205,19 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   const uint32_t tmem = misc->tmem_base;
   const CtaAbort ab{&misc->abort, p.err};
   const int work = cap_ok ? n_kt : 0;
-  // TMEM per buffer b: S at b*256, dP at b*256+128 (P-only / dS-only modes use one of them)
-  auto s_col = [](int b) { return static_cast<uint32_t>(b * 256); };
-  auto dp_col = [](int b) { return static_cast<uint32_t>(b * 256 + 128); };
+  // TMEM: PdS mode: buffer b holds S at b*256 and dP at b*256+128.  TS
+  // variant: buffer b at b*128, the resident A operand (bf16 pairs) at 256.
+  auto s_col = [](int b) { return static_cast<uint32_t>(Cfg::kTS ? b * 128 : b * 256); };
+  auto dp_col = [](int b) { return static_cast<uint32_t>(Cfg::kTS ? b * 128 : b * 256 + 128); };
+  uint8_t* res_area = Cfg::kS ? q_s : do_s;
+  // ring stage s: the first kStages in the ring area, the rest in the
+  // resident area (usable once the resident operand has moved to TMEM)
+  auto stage_ptr = [&](uint32_t st) -> uint8_t* {
+    return st < static_cast<uint32_t>(Cfg::kStages) ? ring + st * 32768
+                                                     : res_area + (st - Cfg::kStages) * 32768;
+  };
+  // TS dS pass: P ring after the extra V stages in the resident area
+  uint8_t* pring = res_area + Cfg::kExtraStages * 32768;
 
   if (warp == 8) {
     if (lane == 0 && work > 0) {
@@ -202,17 +231,35 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           tma_load_4d(do_s + blk * 16384, &tmDO, &misc->res_full, blk * 64, head, qrow, si.b_coord);
       uint32_t it = 0;
       bool ok = true;
+      bool res_free = !Cfg::kTS;
+      if (Cfg::kTS && MODE == kScoreDs) {  // the P ring reuses the resident area
+        ok = mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer);
+        res_free = true;
+      }
       for (int j = 0; j < work && ok; ++j) {
         const int krow = si.k_base + (kt_lo + j) * kTileN;
+        if (Cfg::kTS && MODE == kScoreDs) {
+          const int sp = j % Cfg::kPStages;
+          if (!(ok = mbar_wait(&misc->p_empty[sp], ((j / Cfg::kPStages) & 1) ^ 1, ab,
+                               kDevTimeoutPeer)))
+            break;
+          mbar_expect_tx(&misc->p_full[sp], 32768);
+          bulk_load(pring + sp * 32768, scratch_tile(p.p_tiles, p, head, t_off, j), 32768,
+                    &misc->p_full[sp]);
+        }
         for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
-          const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+          const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
+          if (st >= static_cast<uint32_t>(Cfg::kStages) && !res_free) {
+            if (!(ok = mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer))) break;
+            res_free = true;
+          }
           if (!(ok = mbar_wait(&misc->ring_empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
           mbar_expect_tx(&misc->ring_full[st], 32768);
           const bool is_k = Cfg::kS && c < D / 128;
           const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
           for (int h = 0; h < 2; ++h)
-            tma_load_4d(ring + st * 32768 + h * 16384, is_k ? &tmK : &tmV, &misc->ring_full[st],
+            tma_load_4d(stage_ptr(st) + h * 16384, is_k ? &tmK : &tmV, &misc->ring_full[st],
                         (2 * cc + h) * 64, kv_head, krow, si.b_coord);
         }
       }
@@ -223,14 +270,15 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       constexpr uint32_t kId = idesc_bf16(128, 128, false, false);
       const uint32_t qb = smem_addr(q_s), db = smem_addr(do_s), rb = smem_addr(ring);
       uint32_t it = 0;
-      bool ok = mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
+      bool ok = Cfg::kTS ? mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer)
+                         : mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
       for (int j = 0; j < work && ok; ++j) {
         const int b = j & 1;
         if (j >= 2 && !(ok = mbar_wait(&misc->buf_free[b], ((j - 2) >> 1) & 1, ab, kDevTimeoutPeer)))
           break;
         tc_fence_after();
         for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
-          const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+          const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
           if (!(ok = mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma))) break;
           tc_fence_after();
@@ -238,13 +286,16 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
           const uint32_t abase = is_k ? qb : db;
           const uint32_t dcol = is_k ? s_col(b) : dp_col(b);
-          const uint32_t sb = rb + st * 32768;
+          const uint32_t sb = smem_addr(stage_ptr(st));
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const int gk = cc * 8 + kk;
-            umma_ss(tmem + dcol, sdesc_sw128(abase + (gk >> 2) * 16384 + (gk & 3) * 32, 16, 1024),
-                    sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), kId,
-                    (cc | kk) != 0);
+            const uint64_t bdesc = sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+            if (Cfg::kTS)
+              umma_ts(tmem + dcol, tmem + 256 + gk * 8, bdesc, kId, (cc | kk) != 0);
+            else
+              umma_ss(tmem + dcol, sdesc_sw128(abase + (gk >> 2) * 16384 + (gk & 3) * 32, 16, 1024),
+                      bdesc, kId, (cc | kk) != 0);
           }
           umma_commit(&misc->ring_empty[st]);
         }
@@ -265,18 +316,52 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     const int q_abs = q_idx + q_off;
     const float lse2_r = row_valid ? p.lse2[head * p.ws_head_stride + tok_base + q_idx] : -INFINITY;
     const float delta_r = row_valid ? p.delta[head * p.ws_head_stride + tok_base + q_idx] : 0.f;
+    const bool row_ok = row_valid && lse2_r != -INFINITY;
     const int qdoc = (row_valid && p.mask.doc) ? p.mask.doc[si.meta_base + q_abs] : 0;
     const int qa0 = qt * kTileM + q_off;
     const int qa1 = min((qt + 1) * kTileM, si.len_q) - 1 + q_off;
     bool ok = true;
+    if (Cfg::kTS && work > 0) {
+      // resident Q / dO (128-B swizzled rows) -> TMEM lane r, bf16 pairs from
+      // column 256; this warp copies K elements [256*(w/4), +256) of its rows.
+      ok = mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        const uint8_t* src = Cfg::kS ? q_s : do_s;
+        const int h = warp >> 2;
+#pragma unroll 1
+        for (int blk = 0; blk < 4; ++blk) {  // 64 K elements = 32 columns per block
+          uint32_t v[32];
+          const int dblk = h * 4 + blk;
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const uint4 w = *reinterpret_cast<const uint4*>(src + dblk * 16384 + r * 128 +
+                                                            ((ch ^ (r & 7)) << 4));
+            v[4 * ch + 0] = w.x;
+            v[4 * ch + 1] = w.y;
+            v[4 * ch + 2] = w.z;
+            v[4 * ch + 3] = w.w;
+          }
+          tmem_st32(lane_base + 256 + dblk * 32, v);
+        }
+        tmem_wait_st();
+      }
+      fence_proxy_async_smem();  // the area is refilled by bulk copies next
+      tc_fence_before();
+      mbar_arrive(&misc->a_ready);
+    }
     for (int j = 0; j < work; ++j) {
       const int b = j & 1;
       const int k0 = (kt_lo + j) * kTileN;
       const int cls = p.mask.doc ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
       if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
+      if (ok && Cfg::kTS && MODE == kScoreDs)
+        ok = mbar_wait(&misc->p_full[j % Cfg::kPStages], (j / Cfg::kPStages) & 1, ab,
+                       kDevTimeoutTma);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) continue;
       tc_fence_after();
+      const uint8_t* psm = pring + (j % Cfg::kPStages) * 32768;
       uint8_t* ptile = Cfg::kS || MODE == kScoreDs ? scratch_tile(p.p_tiles, p, head, t_off, j) : nullptr;
       uint8_t* dtile = Cfg::kDP ? scratch_tile(p.ds_tiles, p, head, t_off, j) : nullptr;
 #pragma unroll 1
@@ -306,7 +391,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           // P as written by the P-only pass (exact zeros where masked)
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const uint4 w = *reinterpret_cast<const uint4*>(ptile + tile_chunk_offset(r, c * 4 + u));
+            const uint4 w = Cfg::kTS
+                                ? *reinterpret_cast<const uint4*>(psm + tile_chunk_offset(r, c * 4 + u))
+                                : *reinterpret_cast<const uint4*>(ptile + tile_chunk_offset(r, c * 4 + u));
             const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -316,15 +403,24 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             }
           }
         } else {
+          const int kc = k0 + c * 32;
+          // Fast path (warp-uniform in practice): the whole 32-key chunk is
+          // inside the mask for a row with a finite LSE.
+          if (cls == 1 && row_ok && kc + 32 <= si.len_k) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int k = k0 + c * 32 + i;
-            bool keep = row_valid && lse2_r != -INFINITY && k < si.len_k;
-            if (cls != 1 && keep) {
-              const int kdoc = p.mask.doc ? p.mask.doc[si.meta_base + k] : 0;
-              keep = mask_allows(p.mask.window, q_abs, k, -1, qdoc, -1, kdoc);
+            for (int i = 0; i < 32; ++i) pv[i] = ex2(fmaf(__uint_as_float(sr[i]), kLog2e, -lse2_r));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int k = kc + i;
+              bool keep = row_ok && k < si.len_k;
+              if (cls != 1) {
+                const int kdoc = (p.mask.doc && k < si.len_k) ? p.mask.doc[si.meta_base + k] : 0;
+                keep = keep && mask_allows(p.mask.window, q_abs, k, -1, qdoc, -1, kdoc);
+              }
+              const float e = ex2(fmaf(__uint_as_float(sr[i]), kLog2e, row_ok ? -lse2_r : 0.f));
+              pv[i] = keep ? e : 0.f;
             }
-            pv[i] = keep ? ex2(fmaf(__uint_as_float(sr[i]), kLog2e, -lse2_r)) : 0.f;
           }
         }
         if (MODE != kScoreDs) {
@@ -339,10 +435,11 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           }
         }
         if (Cfg::kDP) {
+          // dS = P (dP - delta); P is exactly 0 outside the mask and dP is
+          // finite for finite inputs, so no guard is needed.
           float dv[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            dv[i] = pv[i] != 0.f ? pv[i] * (__uint_as_float(dr[i]) - delta_r) : 0.f;
+          for (int i = 0; i < 32; ++i) dv[i] = pv[i] * (__uint_as_float(dr[i]) - delta_r);
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 w;
@@ -353,6 +450,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             *reinterpret_cast<uint4*>(dtile + tile_chunk_offset(r, c * 4 + u)) = w;
           }
         }
+      }
+      if (Cfg::kTS && MODE == kScoreDs) {
+        fence_proxy_async_smem();
+        mbar_arrive(&misc->p_empty[j % Cfg::kPStages]);
       }
     }
   }

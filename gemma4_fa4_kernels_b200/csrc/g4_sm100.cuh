@@ -115,6 +115,13 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Order this thread's generic shared-memory accesses before later async-proxy
+// (TMA / bulk copy) accesses to the same bytes, e.g. before a buffer that was
+// read with ordinary loads is handed back to a bulk-copy producer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Untiled bulk copy global -> shared (both addresses 16-B aligned, size a
 // multiple of 16 bytes), completing on an mbarrier transaction count.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
