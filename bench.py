@@ -68,7 +68,9 @@ def flops_of(cfg) -> dict:
             # materialised path: the score kernels compute S and dP once; each
             # tile GEMM does one of dV, dK, dQ
             "bwd_score": 2.0 * h * p * (2 * d), "bwd_gemm_dv": 2.0 * h * p * d,
-            "bwd_gemm_dk": 2.0 * h * p * d, "bwd_gemm_dq": 2.0 * h * p * d}
+            "bwd_gemm_dk": 2.0 * h * p * d, "bwd_gemm_dq": 2.0 * h * p * d,
+            # two-pass forward: S once, then O = P V
+            "fwd_score": 2.0 * h * p * d, "fwd_pv": 2.0 * h * p * d}
 
 
 def make_inputs(cfg, seed, device, dtype=torch.bfloat16):

@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "g4_abi_version",
     "g4_last_error",
     "g4_attn_fwd_workspace_bytes",
+    "g4_attn_fwd_min_workspace_bytes",
     "g4_attn_fwd",
     "g4_attn_bwd_workspace_bytes",
     "g4_attn_bwd_min_workspace_bytes",
@@ -114,8 +115,8 @@ def load() -> ctypes.CDLL:
         P = ctypes.POINTER(G4AttnArgs)
         lib.g4_abi_version.restype = ctypes.c_int
         lib.g4_last_error.restype = ctypes.c_char_p
-        for name in ("g4_attn_fwd_workspace_bytes", "g4_attn_bwd_workspace_bytes",
-                     "g4_attn_bwd_min_workspace_bytes"):
+        for name in ("g4_attn_fwd_workspace_bytes", "g4_attn_fwd_min_workspace_bytes",
+                     "g4_attn_bwd_workspace_bytes", "g4_attn_bwd_min_workspace_bytes"):
             fn = getattr(lib, name)
             fn.argtypes = [P]
             fn.restype = ctypes.c_size_t

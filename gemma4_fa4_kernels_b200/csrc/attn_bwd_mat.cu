@@ -105,12 +105,12 @@ __global__ void plan_qtile_ranges_kernel(const MatParams p) {
 // =====================================================================================
 // score kernel
 // =====================================================================================
-enum ScoreMode : int { kScorePdS = 0, kScoreP = 1, kScoreDs = 2 };
+enum ScoreMode : int { kScorePdS = 0, kScoreP = 1, kScoreDs = 2, kScoreFwd = 3 };
 
 template <int D, int MODE>
 struct ScoreCfg {
-  static constexpr bool kS = MODE != kScoreDs;   // computes S (needs Q, K)
-  static constexpr bool kDP = MODE != kScoreP;   // computes dP (needs dO, V)
+  static constexpr bool kS = MODE != kScoreDs;                        // S (needs Q, K)
+  static constexpr bool kDP = MODE == kScorePdS || MODE == kScoreDs;   // dP (needs dO, V)
   static constexpr int kQBytes = kS ? D * kTileM * 2 : 0;
   static constexpr int kDoBytes = kDP ? D * kTileM * 2 : 0;
   static constexpr int kStages = 3;
@@ -123,7 +123,8 @@ struct ScoreCfg {
   // TS variant: once the resident operand sits in TMEM its 128 KB of shared
   // memory extends the operand ring (more bytes in flight per SM): the P pass
   // gets 3 + 4 K stages; the dS pass 3 + 2 V stages and 2 P stages.
-  static constexpr int kExtraStages = kTS ? (MODE == kScoreP ? 4 : 2) : 0;
+  // (the forward pass keeps 32 KB of that area for its row-statistics exchange)
+  static constexpr int kExtraStages = kTS ? (MODE == kScoreDs ? 2 : (MODE == kScoreFwd ? 3 : 4)) : 0;
   static constexpr int kRingStages = kStages + kExtraStages;
   static constexpr int kPStages = 2;
 };
@@ -314,8 +315,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     const int q_idx = qt * kTileM + r;
     const bool row_valid = q_idx < si.len_q;
     const int q_abs = q_idx + q_off;
-    const float lse2_r = row_valid ? p.lse2[head * p.ws_head_stride + tok_base + q_idx] : -INFINITY;
-    const float delta_r = row_valid ? p.delta[head * p.ws_head_stride + tok_base + q_idx] : 0.f;
+    const float lse2_r =
+        (row_valid && p.lse2) ? p.lse2[head * p.ws_head_stride + tok_base + q_idx] : -INFINITY;
+    const float delta_r =
+        (row_valid && p.delta) ? p.delta[head * p.ws_head_stride + tok_base + q_idx] : 0.f;
     const bool row_ok = row_valid && lse2_r != -INFINITY;
     const int qdoc = (row_valid && p.mask.doc) ? p.mask.doc[si.meta_base + q_abs] : 0;
     const int qa0 = qt * kTileM + q_off;
@@ -350,6 +353,104 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       tc_fence_before();
       mbar_arrive(&misc->a_ready);
     }
+    if constexpr (MODE == kScoreFwd) {
+      // ---- forward pass 1: online softmax over the key tiles ----
+      // Rows are shared by warps w and w+4 (64 columns each); the tile row max
+      // and the final row sum are combined through shared memory, and both
+      // halves take identical rescale decisions from identical inputs.
+      const int half = warp >> 2;
+      // [2 parity][2 half][128] in the resident area past the extra stages (free
+      // once Q is in TMEM; every math thread passed that point before use)
+      float* pmax = reinterpret_cast<float*>(res_area + Cfg::kExtraStages * 32768);
+      float* lsum = pmax + 512;                         // [2 half][128]
+      const int64_t tile_base = static_cast<int64_t>(head) * p.head_cap_tiles + t_off;
+      for (int j = tid; j < work; j += kScoreMathThreads) p.fwd_flags[tile_base + j] = 0;
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      float m_run = -INFINITY, l_half = 0.f;
+      for (int j = 0; j < work; ++j) {
+        const int b = j & 1;
+        const int k0 = (kt_lo + j) * kTileN;
+        const int cls = p.mask.doc ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
+        if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
+        ok = __all_sync(0xffffffffu, ok);
+        float sv[64];
+        if (ok) {
+          tc_fence_after();
+          uint32_t r0[32], r1[32];
+          tmem_ld32(lane_base + s_col(b) + c_begin * 32, r0);
+          tmem_ld32(lane_base + s_col(b) + c_begin * 32 + 32, r1);
+          tmem_wait_ld();
+          reg_fence32(r0);
+          reg_fence32(r1);
+          tc_fence_before();
+          mbar_arrive(&misc->buf_free[b]);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            sv[i] = __uint_as_float(r0[i]);
+            sv[32 + i] = __uint_as_float(r1[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) sv[i] = -INFINITY;
+        }
+        const int kc = k0 + c_begin * 32;
+        if (!(cls == 1 && kc + 64 <= si.len_k)) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const int k = kc + i;
+            bool keep = k < si.len_k;
+            if (cls != 1 && keep) {
+              const int kdoc = p.mask.doc ? p.mask.doc[si.meta_base + k] : 0;
+              keep = mask_allows(p.mask.window, q_abs, k, -1, qdoc, -1, kdoc);
+            }
+            if (!keep) sv[i] = -INFINITY;
+          }
+        }
+        float mt = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mt = fmaxf(mt, sv[i]);
+        pmax[(j & 1) * 256 + half * 128 + r] = mt * kLog2e;
+        asm volatile("bar.sync 2, 256;" ::: "memory");
+        mt = fmaxf(pmax[(j & 1) * 256 + r], pmax[(j & 1) * 256 + 128 + r]);
+        float alpha = 1.f;
+        if (mt > m_run + 8.f) {  // lazy rescale; also the first finite tile
+          alpha = m_run == -INFINITY ? 0.f : ex2(m_run - mt);
+          m_run = mt;
+        }
+        const float m_sub = m_run == -INFINITY ? 0.f : m_run;
+        float rowsum = 0.f;
+        uint8_t* ptile = scratch_tile(p.p_tiles, p, head, t_off, j);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          float pe[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            pe[e] = ex2(fmaf(sv[u * 8 + e], kLog2e, -m_sub));
+            rowsum += pe[e];
+          }
+          uint4 w;
+          w.x = pack_bf16x2(pe[0], pe[1]);
+          w.y = pack_bf16x2(pe[2], pe[3]);
+          w.z = pack_bf16x2(pe[4], pe[5]);
+          w.w = pack_bf16x2(pe[6], pe[7]);
+          *reinterpret_cast<uint4*>(ptile + tile_chunk_offset(r, c_begin * 4 + u)) = w;
+        }
+        l_half = l_half * alpha + rowsum;
+        if (half == 0) {
+          p.fwd_alpha[(tile_base + j) * 128 + r] = alpha;
+          if (j > 0 && alpha != 1.f && row_valid) atomicOr(&p.fwd_flags[tile_base + j], 1);
+        }
+      }
+      lsum[half * 128 + r] = l_half;
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      if (half == 0 && row_valid) {
+        const float l = lsum[r] + lsum[128 + r];
+        const float lse = l > 0.f ? (m_run + __log2f(l)) * kLn2 : -INFINITY;
+        p.lse_out[static_cast<int64_t>(si.b_coord) * p.lse_stride[0] +
+                  static_cast<int64_t>(head) * p.lse_stride[1] + si.q_base + q_idx] = lse;
+        p.fwd_inv_l[head * p.ws_head_stride + tok_base + q_idx] = l > 0.f ? 1.f / l : 0.f;
+      }
+    } else
     for (int j = 0; j < work; ++j) {
       const int b = j & 1;
       const int k0 = (kt_lo + j) * kTileN;
@@ -469,13 +570,14 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
 // =====================================================================================
 // tile GEMM kernel: dV = P^T dO, dK = dS^T Q (KV-major) and dQ = dS K (Q-major)
 // =====================================================================================
-enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2 };
+enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2, kGemmO = 3 };
 
 // dQ CTAs produce all D output columns (A loaded once); dV / dK CTAs produce
 // one 256-column half each, which doubles the KV-major grid for load balance.
 template <int D, int WHICH>
 struct GemmCfg {
-  static constexpr int kNB = WHICH == 2 ? D : 256;  // output columns per CTA
+  static constexpr bool kQMajor = WHICH >= 2;       // dQ and the forward O
+  static constexpr int kNB = kQMajor ? D : 256;     // output columns per CTA
   static constexpr int kHalves = D / kNB;
   static constexpr int kABytes = 16384;             // 128 rows x 64 deep
   static constexpr int kBBytes = 64 * kNB * 2;      // 64 deep x kNB
@@ -487,6 +589,8 @@ struct GemmMisc {
   uint64_t full[4];
   uint64_t empty[4];
   uint64_t acc_full;
+  uint64_t o_done;   // forward: MMAs before a rescale point completed
+  uint64_t o_ready;  // forward: O rows rescaled
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -518,7 +622,7 @@ __global__ void __launch_bounds__(192, 1)
   int seq, tile, head;  // tile: key tile (dV/dK) or query tile (dQ) within the sequence
   int qg = 0;           // dQ: global query-tile index
   int half = 0;         // dV/dK: which 256-column half
-  if (WHICH == kGemmDq) {
+  if (Cfg::kQMajor) {
     const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
     if (static_cast<int>(blockIdx.x) >= n) return;
     qg = n - 1 - static_cast<int>(blockIdx.x);
@@ -551,13 +655,13 @@ __global__ void __launch_bounds__(192, 1)
   const int n_qt_seq = (si.len_q + kTileM - 1) / kTileM;
   const int first_qg = packed ? (n_qt_seq > 0 ? p.seg_first_qtile[seq] : 0) : seq * p.n_qt_fixed;
   auto for_each_tile = [&](auto&& fn) {
-    if (WHICH == kGemmDq) {
+    if (Cfg::kQMajor) {
       const int4 rg = p.ranges[qg];
       const int kv_head = head / G;
       if (rg.z + rg.y > p.head_cap_tiles) return;  // planner flagged an overflow
+      uint8_t* base = WHICH == kGemmO ? p.p_tiles : p.ds_tiles;
       for (int j = 0; j < rg.y; ++j)
-        if (!fn(scratch_tile(p.ds_tiles, p, head, rg.z, j), kv_head,
-                si.k_base + (rg.x + j) * kTileN))
+        if (!fn(scratch_tile(base, p, head, rg.z, j), kv_head, si.k_base + (rg.x + j) * kTileN))
           return;
     } else {
       uint8_t* base = WHICH == kGemmDv ? p.p_tiles : p.ds_tiles;
@@ -580,6 +684,8 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&misc->empty[s], 1);
     }
     mbar_init(&misc->acc_full, 1);
+    mbar_init(&misc->o_done, 1);
+    mbar_init(&misc->o_ready, 128);
     mbar_init(&misc->drain, 1);
     misc->abort = 0;
     fence_mbar_init();
@@ -611,7 +717,7 @@ __global__ void __launch_bounds__(192, 1)
           if (!(ok = mbar_wait(&misc->empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
           uint8_t* dst = smem + st * Cfg::kStageBytes;
           mbar_expect_tx(&misc->full[st], Cfg::kStageBytes);
-          if (WHICH == kGemmDq) {
+          if (Cfg::kQMajor) {
             bulk_load(dst, t + h * 16384, 16384, &misc->full[st]);
           } else {
             bulk_load(dst, t + h * 8192, 8192, &misc->full[st]);
@@ -627,11 +733,23 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else if (warp == 5) {
     if (lane == 0 && n_steps > 0) {
-      constexpr uint32_t kId = idesc_bf16(128, 256, WHICH != kGemmDq, true);
+      constexpr uint32_t kId = idesc_bf16(128, 256, !Cfg::kQMajor, true);
       const uint32_t sb0 = smem_addr(smem);
       uint32_t it = 0;
       bool ok = true;
+      int tile_j = 0, events = 0;
+      const int64_t flag_base =
+          WHICH == kGemmO ? static_cast<int64_t>(head) * p.head_cap_tiles + p.ranges[qg].z : 0;
       for_each_tile([&](const uint8_t*, int, int) {
+        // forward: before the first product of a flagged tile, let the
+        // correction warps rescale O once every earlier product completed
+        if (WHICH == kGemmO && tile_j > 0 && p.fwd_flags[flag_base + tile_j]) {
+          umma_commit(&misc->o_done);
+          if (!(ok = mbar_wait(&misc->o_ready, events & 1, ab, kDevTimeoutPeer))) return false;
+          tc_fence_after();
+          ++events;
+        }
+        ++tile_j;
         for (int h = 0; h < 2 && ok; ++h) {
           const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
           const uint32_t first = it == 0;
@@ -642,8 +760,8 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t bb = a + Cfg::kABytes;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t adesc = WHICH == kGemmDq ? sdesc_sw128(a + kk * 32, 16, 1024)
-                                                    : sdesc_sw128(a + kk * 2048, 8192, 1024);
+            const uint64_t adesc = Cfg::kQMajor ? sdesc_sw128(a + kk * 32, 16, 1024)
+                                                : sdesc_sw128(a + kk * 2048, 8192, 1024);
 #pragma unroll
             for (int nh = 0; nh < Cfg::kNB / 256; ++nh)
               umma_ss(tmem + nh * 256, adesc, sdesc_sw128(bb + nh * 32768 + kk * 2048, 8192, 1024),
@@ -661,15 +779,58 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ---------------- epilogue: TMEM -> bf16 rows ----------------
     bool ok = true;
-    if (n_steps > 0) ok = mbar_wait(&misc->acc_full, 0, ab, kDevTimeoutMma);
+    const uint32_t lane_base0 = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    if (WHICH == kGemmO && n_steps > 0) {
+      // correction: apply the forward's lazy rescale factors at flagged tiles
+      const int4 rg = p.ranges[qg];
+      const int64_t tile_base = static_cast<int64_t>(head) * p.head_cap_tiles + rg.z;
+      int events = 0;
+      for (int j = 1; j < rg.y && ok; ++j) {
+        if (!p.fwd_flags[tile_base + j]) continue;
+        ok = mbar_wait(&misc->o_done, events & 1, ab, kDevTimeoutMma);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const float a = p.fwd_alpha[(tile_base + j) * 128 + tid];
+        if (__any_sync(0xffffffffu, a != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; c += 2) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(lane_base0 + c * 32, r0);
+            tmem_ld32(lane_base0 + c * 32 + 32, r1);
+            tmem_wait_ld();
+            reg_fence32(r0);
+            reg_fence32(r1);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              r0[i] = __float_as_uint(__uint_as_float(r0[i]) * a);
+              r1[i] = __float_as_uint(__uint_as_float(r1[i]) * a);
+            }
+            tmem_st32(lane_base0 + c * 32, r0);
+            tmem_st32(lane_base0 + c * 32 + 32, r1);
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        mbar_arrive(&misc->o_ready);
+        ++events;
+      }
+    }
+    if (ok && n_steps > 0) ok = mbar_wait(&misc->acc_full, 0, ab, kDevTimeoutMma);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     const bool have = ok && n_steps > 0;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const int row = tile * 128 + tid;
-    const bool row_valid = WHICH == kGemmDq ? row < si.len_q : row < si.len_k;
+    const bool row_valid = Cfg::kQMajor ? row < si.len_q : row < si.len_k;
+    float out_scale = 1.f;
     __nv_bfloat16* dst;
-    if (WHICH == kGemmDq)
+    if (WHICH == kGemmO) {
+      const int64_t tok = (packed ? si.q_base : static_cast<int64_t>(seq) * p.layout.seqlen_q) + row;
+      out_scale = row_valid ? p.fwd_inv_l[head * p.ws_head_stride + tok] : 0.f;
+      dst = p.o + static_cast<int64_t>(si.b_coord) * p.o_stride[0] +
+            static_cast<int64_t>(si.q_base + row) * p.o_stride[1] + static_cast<int64_t>(head) * p.o_stride[2];
+    } else if (WHICH == kGemmDq)
       dst = p.dq + static_cast<int64_t>(si.b_coord) * p.dq_stride[0] +
             static_cast<int64_t>(si.q_base + row) * p.dq_stride[1] + static_cast<int64_t>(head) * p.dq_stride[2];
     else if (WHICH == kGemmDv)
@@ -694,11 +855,14 @@ __global__ void __launch_bounds__(192, 1)
         uint4* out = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          out[i] = make_uint4(
-              pack_bf16x2(__uint_as_float(r[8 * i + 0]), __uint_as_float(r[8 * i + 1])),
-              pack_bf16x2(__uint_as_float(r[8 * i + 2]), __uint_as_float(r[8 * i + 3])),
-              pack_bf16x2(__uint_as_float(r[8 * i + 4]), __uint_as_float(r[8 * i + 5])),
-              pack_bf16x2(__uint_as_float(r[8 * i + 6]), __uint_as_float(r[8 * i + 7])));
+          out[i] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * i + 0]) * out_scale,
+                                          __uint_as_float(r[8 * i + 1]) * out_scale),
+                              pack_bf16x2(__uint_as_float(r[8 * i + 2]) * out_scale,
+                                          __uint_as_float(r[8 * i + 3]) * out_scale),
+                              pack_bf16x2(__uint_as_float(r[8 * i + 4]) * out_scale,
+                                          __uint_as_float(r[8 * i + 5]) * out_scale),
+                              pack_bf16x2(__uint_as_float(r[8 * i + 6]) * out_scale,
+                                          __uint_as_float(r[8 * i + 7]) * out_scale));
       }
     }
   }
@@ -736,6 +900,7 @@ static int launch_score_impl(const CUtensorMap& tq, const CUtensorMap& tk, const
 int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& tk,
                      const CUtensorMap& tv, const CUtensorMap& tdo, const MatParams& p, int grid_x,
                      cudaStream_t stream) {
+  if (pass == 2) return launch_score_impl<512, kScoreFwd>(tq, tk, tv, tdo, p, grid_x, stream);
   if (d == 256) return launch_score_impl<256, kScorePdS>(tq, tk, tv, tdo, p, grid_x, stream);
   if (pass == 0) return launch_score_impl<512, kScoreP>(tq, tk, tv, tdo, p, grid_x, stream);
   return launch_score_impl<512, kScoreDs>(tq, tk, tv, tdo, p, grid_x, stream);
@@ -745,7 +910,7 @@ template <int D, int WHICH>
 static int launch_gemm_impl(const CUtensorMap& tb, const MatParams& p, int grid_x, int grid_y,
                             cudaStream_t stream) {
   using Cfg = GemmCfg<D, WHICH>;
-  if (WHICH != kGemmDq) {  // KV-major: (key tile, KV head, half) all along x
+  if (!Cfg::kQMajor) {  // KV-major: (key tile, KV head, half) all along x
     grid_x *= grid_y * Cfg::kHalves;
     grid_y = 1;
   }
@@ -767,6 +932,7 @@ int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const MatParam
   }
   if (which == kGemmDv) return launch_gemm_impl<512, kGemmDv>(tb, p, grid_x, grid_y, stream);
   if (which == kGemmDk) return launch_gemm_impl<512, kGemmDk>(tb, p, grid_x, grid_y, stream);
+  if (which == kGemmO) return launch_gemm_impl<512, kGemmO>(tb, p, grid_x, grid_y, stream);
   return launch_gemm_impl<512, kGemmDq>(tb, p, grid_x, grid_y, stream);
 }
 

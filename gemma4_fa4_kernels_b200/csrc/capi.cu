@@ -49,11 +49,14 @@ enum KernelId {
   kKGemmDv,
   kKGemmDk,
   kKGemmDq,
+  kKFwdScore,
+  kKFwdPv,
   kKCount
 };
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
                                            "plan",     "mask",           "bwd_score",
-                                           "bwd_gemm_dv", "bwd_gemm_dk", "bwd_gemm_dq"};
+                                           "bwd_gemm_dv", "bwd_gemm_dk", "bwd_gemm_dq",
+                                           "fwd_score",   "fwd_pv"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -188,6 +191,9 @@ struct Workspace {
   size_t ranges = 0;       // int4[n_qt_total]
   size_t p_tiles = 0;      // Hq * head_cap tiles of 32 KB
   size_t ds_tiles = 0;
+  size_t fwd_alpha = 0;    // two-pass forward: float[Hq * head_cap * 128]
+  size_t fwd_flags = 0;    // int[Hq * head_cap]
+  size_t fwd_inv_l = 0;    // float[Hq * tokens_q]
   bool materialized = false;
   int n_qt_total = 0;
   int64_t head_cap_tiles = 0;
@@ -223,11 +229,16 @@ int64_t mat_head_cap_tiles(const g4_attn_args* a, int n_qt_total) {
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// backward == 2 requests the materialised-P/dS layout (ignored when the call is
-// not eligible: vision metadata needs data-dependent key ranges).
-Workspace plan_workspace(const g4_attn_args* a, int backward) {
+// Workspace modes: 0 single-kernel forward, 1 backward with recompute kernels,
+// 2 backward with materialised P/dS tiles, 3 two-pass forward (d512, P tiles).
+// Modes 2 and 3 fall back to 1 / 0 when the call is not eligible (vision
+// metadata needs data-dependent key ranges; the two-pass forward is d512 only).
+Workspace plan_workspace(const g4_attn_args* a, int mode) {
   Workspace w;
   const bool packed = a->cu_seqlens_q != nullptr;
+  const bool vision = a->vision_ids && a->window > 0;
+  const bool two_pass_fwd = mode == 3 && !vision && a->head_dim_qk == 512;
+  const int backward = (mode == 1 || mode == 2) ? mode : 0;
   size_t off = 256;
   if (packed) {
     w.max_q_tiles = a->seqlen_q / g4::kTileM + a->batch + 1;
@@ -271,6 +282,24 @@ Workspace plan_workspace(const g4_attn_args* a, int backward) {
       w.ds_tiles = off;
       off = align256(off + tiles);
     }
+  }
+  if (two_pass_fwd) {
+    w.materialized = true;
+    w.tokens_q = packed ? a->seqlen_q : int64_t(a->batch) * a->seqlen_q;
+    w.n_qt_total = packed ? w.max_q_tiles
+                          : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
+    w.ranges = off;
+    off = align256(off + sizeof(int4) * w.n_qt_total);
+    w.head_cap_tiles = mat_head_cap_tiles(a, w.n_qt_total);
+    const size_t tiles = size_t(a->num_q_heads) * size_t(w.head_cap_tiles);
+    w.p_tiles = off;
+    off = align256(off + tiles * 32768);
+    w.fwd_alpha = off;
+    off = align256(off + tiles * 128 * sizeof(float));
+    w.fwd_flags = off;
+    off = align256(off + tiles * sizeof(int));
+    w.fwd_inv_l = off;
+    off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
   }
   w.total = off;
   return w;
@@ -366,7 +395,12 @@ const char* g4_last_error(void) { return g_last_error.c_str(); }
 
 size_t g4_attn_fwd_workspace_bytes(const g4_attn_args* args) {
   if (!args) return 0;
-  return plan_workspace(args, false).total;
+  return plan_workspace(args, 3).total;
+}
+
+size_t g4_attn_fwd_min_workspace_bytes(const g4_attn_args* args) {
+  if (!args) return 0;
+  return plan_workspace(args, 0).total;
 }
 
 size_t g4_attn_bwd_workspace_bytes(const g4_attn_args* args) {
@@ -387,7 +421,11 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
   if (!packed && (a->lse_stride[0] <= 0 || a->lse_stride[1] <= 0))
     return fail(G4_ERR_INVALID, "lse strides must be positive");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const Workspace w = plan_workspace(a, 0);
+  // Two-pass d512 forward (P tiles in HBM, no QK^T recomputation) when the
+  // workspace holds its scratch; otherwise the single-kernel forward.
+  const Workspace w3 = plan_workspace(a, 3);
+  const Workspace w =
+      (w3.materialized && a->workspace && a->workspace_bytes >= w3.total) ? w3 : plan_workspace(a, 0);
   g4::FwdParams p;
   memset(&p, 0, sizeof(p));
   if ((rc = prepare(a, w, false, st, &p.mask))) return rc;
@@ -417,6 +455,51 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
     return rc;
   const int grid_x = packed ? w.max_q_tiles
                             : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
+  if (w.materialized) {
+    g4::MatParams m;
+    memset(&m, 0, sizeof(m));
+    m.layout = p.layout;
+    m.mask = p.mask;
+    m.group = p.group;
+    m.num_q_heads = a->num_q_heads;
+    m.n_qt_fixed = packed ? 0 : (a->seqlen_q + g4::kTileM - 1) / g4::kTileM;
+    m.q_tiles = p.tiles;
+    m.n_q_tiles = p.n_tiles;
+    m.ranges = ws_ptr<int4>(a, w.ranges);
+    m.head_cap_tiles = w.head_cap_tiles;
+    m.p_tiles = ws_ptr<uint8_t>(a, w.p_tiles);
+    m.fwd_alpha = ws_ptr<float>(a, w.fwd_alpha);
+    m.fwd_flags = ws_ptr<int>(a, w.fwd_flags);
+    m.fwd_inv_l = ws_ptr<float>(a, w.fwd_inv_l);
+    m.ws_head_stride = w.tokens_q;
+    m.lse_out = a->lse;
+    m.lse_stride[0] = p.lse_stride[0];
+    m.lse_stride[1] = p.lse_stride[1];
+    m.o = p.o;
+    for (int i = 0; i < 3; ++i) m.o_stride[i] = p.o_stride[i];
+    m.err = p.err;
+    CUtensorMap tv64;
+    if ((rc = make_map(&tv64, a->v, a->head_dim_v, a->num_kv_heads, a->seqlen_k, bq,
+                       a->v_stride[2], a->v_stride[1], a->v_stride[0], 64)))
+      return rc;
+    int e;
+    {
+      LaunchScope ls(kKPlan, st);
+      e = g4::launch_plan_qtile_ranges(m, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "query-tile range planning");
+    }
+    {
+      LaunchScope ls(kKFwdScore, st);
+      e = g4::launch_bwd_score(D, 2, tq, tk, tv, tq, m, w.n_qt_total, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward score launch");
+    }
+    {
+      LaunchScope ls(kKFwdPv, st);
+      e = g4::launch_bwd_tile_gemm(D, 3, tv64, m, w.n_qt_total, a->num_q_heads, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward PV launch");
+    }
+    return G4_OK;
+  }
   const int slabs = a->head_dim_v / 256;
   LaunchScope ls(kKFwd, st);
   int e = D == 256 ? g4::launch_fwd<256>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st)

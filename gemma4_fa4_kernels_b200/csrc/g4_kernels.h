@@ -76,15 +76,27 @@ struct MatParams {
   int64_t dk_stride[3];
   __nv_bfloat16* dv;
   int64_t dv_stride[3];
+  // two-pass forward (d512): pass 1 writes P (in p_tiles, relative to the
+  // running row max), the per-row rescale factor of every tile, a per-tile
+  // "some row rescaled" flag, 1/rowsum and the LSE; pass 2 forms O = P V.
+  float* fwd_alpha;                // [head][tile][128]
+  int* fwd_flags;                  // [head][tile]
+  float* fwd_inv_l;                // [head][token]
+  float* lse_out;
+  int64_t lse_stride[2];
+  __nv_bfloat16* o;
+  int64_t o_stride[3];
   int* err;
 };
 
 int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream);
-// pass: d512 runs pass 0 (P) then pass 1 (dS); d256 computes both in pass 0.
+// pass: d512 runs pass 0 (P) then pass 1 (dS); d256 computes both in pass 0;
+// pass 2 is the forward's first pass (online softmax, d512 only).
 int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& tk,
                      const CUtensorMap& tv, const CUtensorMap& tdo, const MatParams& p, int grid_x,
                      cudaStream_t stream);
-// which: 0 = dV (B = dO), 1 = dK (B = Q), 2 = dQ (B = K); maps use 64-row boxes.
+// which: 0 = dV (B = dO), 1 = dK (B = Q), 2 = dQ (B = K), 3 = forward O = P V
+// (B = V); maps use 64-row boxes.
 int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const MatParams& p, int grid_x,
                          int grid_y, cudaStream_t stream);
 

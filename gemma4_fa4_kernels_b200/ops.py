@@ -96,14 +96,29 @@ def _scratch_budget(device) -> int:
     return _budget_cache[idx]
 
 
+def _pick_workspace(full: int, small: int, force_small: bool, device) -> torch.Tensor:
+    """Workspace for the fast (scratch-backed) path when it fits the budget and
+    the allocator, else the minimum workspace of the compact path."""
+    if force_small or full > _scratch_budget(device):
+        return _workspace(small, device)
+    try:
+        return _workspace(full, device)
+    except torch.cuda.OutOfMemoryError:
+        return _workspace(small, device)
+
+
 def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
 def attn_fwd(q, k, v, *, window=0, vision_ids=None, document_ids=None, cu_seqlens_q=None,
-             cu_seqlens_k=None, max_seqlen_q=None, max_seqlen_k=None, out=None):
+             cu_seqlens_k=None, max_seqlen_q=None, max_seqlen_k=None, out=None,
+             algorithm="auto"):
     """Forward through ``g4_attn_fwd``.  Fixed BSHD (4-D) or packed THD (3-D)
-    inputs; returns ``(out, lse)`` with LSE ``(B,Hq,Sq)`` or ``(Hq,Tq)``."""
+    inputs; returns ``(out, lse)`` with LSE ``(B,Hq,Sq)`` or ``(Hq,Tq)``.
+
+    ``algorithm``: "auto" lets global d512 run the two-pass forward when its
+    scratch fits the budget; "single" forces the single-kernel forward."""
     lib = _lib.load()
     packed = cu_seqlens_q is not None
     dev = q.device
@@ -117,7 +132,9 @@ def attn_fwd(q, k, v, *, window=0, vision_ids=None, document_ids=None, cu_seqlen
     a = _build_args(q, k, v, out, lse, window=window, vision_ids=vis, document_ids=doc,
                     cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
                     max_seqlen_q=max_seqlen_q, max_seqlen_k=max_seqlen_k)
-    ws = _workspace(lib.g4_attn_fwd_workspace_bytes(ctypes.byref(a)), dev)
+    ws = _pick_workspace(lib.g4_attn_fwd_workspace_bytes(ctypes.byref(a)),
+                         lib.g4_attn_fwd_min_workspace_bytes(ctypes.byref(a)),
+                         algorithm in ("single", "recompute"), dev)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _raise_for(lib.g4_attn_fwd(ctypes.byref(a), _stream(dev)), "g4_attn_fwd")
     return out, lse
@@ -153,20 +170,11 @@ def attn_bwd(q, k, v, out, lse, dout, *, dlse=None, window=0, vision_ids=None,
     a.dq_stride = _strides3(dq, packed)
     a.dk_stride = _strides3(dk, packed)
     a.dv_stride = _strides3(dv, packed)
-    full = lib.g4_attn_bwd_workspace_bytes(ctypes.byref(a))
-    small = lib.g4_attn_bwd_min_workspace_bytes(ctypes.byref(a))
-    if algorithm == "recompute" or full > _scratch_budget(dev):
-        nbytes = small
-    elif algorithm in ("auto", "materialized"):
-        nbytes = full
-    else:
+    if algorithm not in ("auto", "materialized", "recompute"):
         raise ValueError(f"unknown backward algorithm {algorithm!r}")
-    try:
-        ws = _workspace(nbytes, dev)
-    except torch.cuda.OutOfMemoryError:
-        if nbytes == small:
-            raise
-        ws = _workspace(small, dev)  # no room for the scratch: recompute kernels
+    ws = _pick_workspace(lib.g4_attn_bwd_workspace_bytes(ctypes.byref(a)),
+                         lib.g4_attn_bwd_min_workspace_bytes(ctypes.byref(a)),
+                         algorithm == "recompute", dev)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _raise_for(lib.g4_attn_bwd(ctypes.byref(a), _stream(dev)), "g4_attn_bwd")
     return dq, dk, dv

@@ -97,8 +97,17 @@ int g4_abi_version(void);
 /* Description of the last failure on the calling thread ("" if none). */
 const char* g4_last_error(void);
 
-/* Workspace bytes g4_attn_fwd needs for these arguments (no device access). */
+/*
+ * Workspace bytes for g4_attn_fwd (no device access).  For global d512 the
+ * full size lets the forward run in two passes (S and the online softmax
+ * once, writing bf16 P tiles to HBM scratch; then O = P V with one 512-column
+ * accumulator), avoiding the second QK^T of a split-output kernel; the
+ * minimum size runs the single-kernel forward.  g4_attn_fwd picks the
+ * two-pass path whenever it is eligible and workspace_bytes is at least the
+ * full size.
+ */
 size_t g4_attn_fwd_workspace_bytes(const g4_attn_args* args);
+size_t g4_attn_fwd_min_workspace_bytes(const g4_attn_args* args);
 
 /*
  * Attention forward: O and LSE.
@@ -176,7 +185,8 @@ int g4_build_mask(uint8_t* out, int32_t batch, int32_t q_len, int32_t kv_len, in
  * Kernel ids: 0 forward, 1 backward preprocess, 2 backward dQ (recompute),
  * 3 backward dK/dV (recompute), 4 planning (tile lists, vision pairs, tile
  * ranges), 5 mask builder, 6 backward P/dS scores, 7-9 backward dV / dK / dQ
- * tile GEMMs (materialised path).
+ * tile GEMMs (materialised path), 10 two-pass forward softmax, 11 two-pass
+ * forward O = P V.
  *  - g4_launch_count: launches of `kernel_id` issued by this process so far.
  *  - g4_profile_enable(1): every later launch is bracketed by CUDA events on
  *    its own stream; g4_profile_read synchronises those events and returns the

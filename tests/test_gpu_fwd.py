@@ -119,3 +119,33 @@ def test_forward_is_bit_deterministic_on_side_stream():
     s.synchronize()
     torch.cuda.synchronize()
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
+
+
+@pytest.mark.parametrize("shape", [(1, 700, 8, 1, 0), (2, 300, 8, 1, 0)], ids=["b1", "b2"])
+def test_global_two_pass_and_single_kernel_forward_agree_with_oracle(shape):
+    b, s, hq, hkv, window = shape
+    q, k, v = make_inputs((b, s, hq, 512), (b, s, hkv, 512), (b, s, hkv, 512), seed=91,
+                          with_dout=False)
+    ref_o, ref_lse = oracle.attention_fwd(bshd_to_bhsd_np(q), bshd_to_bhsd_np(k),
+                                          bshd_to_bhsd_np(v))
+    for algo in ("auto", "single"):
+        out, lse = ops.attn_fwd(q, k, v, window=window, algorithm=algo)
+        torch.cuda.synchronize()
+        assert rel_l2(out.float().cpu().numpy(), bhsd_to_bshd(ref_o)) <= REL_L2_TOL, algo
+        assert lse_abs_err(lse.cpu().numpy(), ref_lse) <= LSE_ABS_TOL, algo
+
+
+def test_global_two_pass_rescales_when_the_running_max_jumps():
+    # Keys whose scores grow along the sequence force several lazy rescales.
+    s = 600
+    q, k, v = make_inputs((1, s, 8, 512), (1, s, 1, 512), (1, s, 1, 512), seed=92,
+                          with_dout=False)
+    ramp = torch.linspace(0.2, 3.0, s, device="cuda").view(1, s, 1, 1)
+    k = (k.float() * ramp).to(torch.bfloat16)
+    q = (q.float() + k.float().mean(dim=1, keepdim=True).expand_as(q)).to(torch.bfloat16)
+    ref_o, ref_lse = oracle.attention_fwd(bshd_to_bhsd_np(q), bshd_to_bhsd_np(k),
+                                          bshd_to_bhsd_np(v))
+    out, lse = ops.attn_fwd(q, k, v, window=0)
+    torch.cuda.synchronize()
+    assert rel_l2(out.float().cpu().numpy(), bhsd_to_bshd(ref_o)) <= REL_L2_TOL
+    assert lse_abs_err(lse.cpu().numpy(), ref_lse) <= LSE_ABS_TOL
