@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         asm volatile("bar.sync 2, 256;" ::: "memory");
         mt = fmaxf(pmax[(j & 1) * 256 + r], pmax[(j & 1) * 256 + 128 + r]);
         float alpha = 1.f;
-        if (mt > m_run + 8.f) {  // lazy rescale; also the first finite tile
+        if (mt > m_run + kLazyRescaleLog2) {  // lazy rescale; also the first finite tile
           alpha = m_run == -INFINITY ? 0.f : ex2(m_run - mt);
           m_run = mt;
         }
@@ -594,6 +594,7 @@ struct GemmMisc {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  uint32_t flag_bits[64];  // forward: rescale flags of up to 2048 key tiles
 };
 
 // One k-step of 64 (half a scratch tile): where A and B come from.
@@ -732,18 +733,30 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else if (warp == 5) {
+    if (WHICH == kGemmO && n_steps > 0) {
+      // gather the rescale flags into a bitmask first: a dependent global load
+      // per tile on the MMA issue path would stall the tensor pipe
+      const int4 rg = p.ranges[qg];
+      const int64_t flag_base = static_cast<int64_t>(head) * p.head_cap_tiles + rg.z;
+      for (int w0 = 0; w0 < (rg.y + 31) / 32 && w0 < 64; ++w0) {
+        const int j = w0 * 32 + lane;
+        const bool f = j < rg.y && p.fwd_flags[flag_base + j] != 0;
+        const uint32_t bits = __ballot_sync(0xffffffffu, f);
+        if (lane == 0) misc->flag_bits[w0] = bits;
+      }
+      __syncwarp();
+    }
     if (lane == 0 && n_steps > 0) {
       constexpr uint32_t kId = idesc_bf16(128, 256, !Cfg::kQMajor, true);
       const uint32_t sb0 = smem_addr(smem);
       uint32_t it = 0;
       bool ok = true;
       int tile_j = 0, events = 0;
-      const int64_t flag_base =
-          WHICH == kGemmO ? static_cast<int64_t>(head) * p.head_cap_tiles + p.ranges[qg].z : 0;
       for_each_tile([&](const uint8_t*, int, int) {
         // forward: before the first product of a flagged tile, let the
         // correction warps rescale O once every earlier product completed
-        if (WHICH == kGemmO && tile_j > 0 && p.fwd_flags[flag_base + tile_j]) {
+        if (WHICH == kGemmO && tile_j > 0 &&
+            ((misc->flag_bits[(tile_j >> 5) & 63] >> (tile_j & 31)) & 1u)) {
           umma_commit(&misc->o_done);
           if (!(ok = mbar_wait(&misc->o_ready, events & 1, ab, kDevTimeoutPeer))) return false;
           tc_fence_after();

@@ -14,8 +14,8 @@
 // exact order the MMA warp consumes them: K(0), K(1), V(0), K(2), V(1), ...
 //
 // Online softmax in the exp2 domain with lazy rescaling: the running max only
-// moves (and O is only rescaled) when a tile's max exceeds it by more than 8,
-// so P <= 2^8.  Fully masked rows give O = 0 and LSE = -inf (reference.py:70-75).
+// moves (and O is only rescaled) when a tile's max exceeds it by more than
+// kLazyRescaleLog2, so P <= 2^kLazyRescaleLog2.  Fully masked rows give O = 0 and LSE = -inf (reference.py:70-75).
 //
 // Reference interface replaced: flash_attn.cute.flash_attn_func /
 // flash_attn_varlen_func forward as called by src/gemma4_fa4/h100.py:766-778,
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(192, 1)
       mt *= kLog2e;
       float alpha = 1.f;
       bool rescale = false;
-      if (mt > m_run + 8.f) {  // also true for the first finite tile (m_run = -inf)
+      if (mt > m_run + kLazyRescaleLog2) {  // also true for the first finite tile
         alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - mt);
         m_run = mt;
         rescale = true;

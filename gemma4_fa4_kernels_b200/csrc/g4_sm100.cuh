@@ -261,6 +261,12 @@ __device__ __forceinline__ void tmem_wait_st() {
 // small numeric helpers
 // ------------------------------------------------------------------------------------
 constexpr float kLog2e = 1.4426950408889634f;
+// Online softmax keeps a stale running max until a tile's max exceeds it by
+// more than this many powers of two; P (bf16) then stays below 2^32 and every
+// fp32 row sum / accumulator stays far inside range (2^32 * 2^18 keys).  With
+// unit-RMS d512 vectors the score spread is ~32 in log2 units, so a smaller
+// threshold would rescale O (a pipeline drain) on most tiles.
+constexpr float kLazyRescaleLog2 = 32.f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 __device__ __forceinline__ float ex2(float x) {
