@@ -143,8 +143,16 @@ struct ScoreMisc {
   int abort;
 };
 
-constexpr int kScoreThreads = 320;  // 8 math warps + producer + MMA
-constexpr int kScoreMathThreads = 256;
+// Math warps: warp w reads TMEM lanes 32*(w%4).. and the 32-column chunks
+// [kChunksPerWarp*(w/4), +kChunksPerWarp) of each 128-column tile.  Sixteen
+// warps (four per scheduler) hide the TMEM-load and exp latencies.
+constexpr int kScoreMathWarps = 16;
+constexpr int kScoreGroups = kScoreMathWarps / 4;     // column groups per row
+constexpr int kChunksPerWarp = 4 / kScoreGroups;
+constexpr int kScoreMathThreads = kScoreMathWarps * 32;
+constexpr int kScoreThreads = kScoreMathThreads + 64;  // + producer + MMA warps
+constexpr int kProducerWarp = kScoreMathWarps;
+constexpr int kMmaWarp = kScoreMathWarps + 1;
 
 template <int D, int MODE>
 __global__ void __launch_bounds__(kScoreThreads, 1)
@@ -196,7 +204,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     misc->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == kProducerWarp) {
     tmem_alloc(&misc->tmem_base, 512);
     tmem_relinquish();
   }
@@ -220,7 +228,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   // TS dS pass: P ring after the extra V stages in the resident area
   uint8_t* pring = res_area + Cfg::kExtraStages * 32768;
 
-  if (warp == 8) {
+  if (warp == kProducerWarp) {
     if (lane == 0 && work > 0) {
       mbar_expect_tx(&misc->res_full, Cfg::kQBytes + Cfg::kDoBytes);
       const int qrow = si.q_base + qt * kTileM;
@@ -266,7 +274,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0 && work > 0) {
       constexpr uint32_t kId = idesc_bf16(128, 128, false, false);
       const uint32_t qb = smem_addr(q_s), db = smem_addr(do_s), rb = smem_addr(ring);
@@ -310,8 +318,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     // ---------------- math warps: P / dS tiles to HBM ----------------
     // warp w reads TMEM lanes 32*(w%4).. (its rows) and columns [64*(w/4), +64)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const int r = (warp & 3) * 32 + lane;  // row in the query tile
-    const int c_begin = (warp >> 2) * 2;   // first of this warp's two 32-column chunks
+    const int r = (warp & 3) * 32 + lane;              // row in the query tile
+    const int grp = warp >> 2;                         // column group
+    const int c_begin = grp * kChunksPerWarp;          // first 32-column chunk
     const int q_idx = qt * kTileM + r;
     const bool row_valid = q_idx < si.len_q;
     const int q_abs = q_idx + q_off;
@@ -331,11 +340,11 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         const uint8_t* src = Cfg::kS ? q_s : do_s;
-        const int h = warp >> 2;
+        constexpr int kBlkPerGroup = (D / 64) / kScoreGroups;
 #pragma unroll 1
-        for (int blk = 0; blk < 4; ++blk) {  // 64 K elements = 32 columns per block
+        for (int blk = 0; blk < kBlkPerGroup; ++blk) {  // 64 K elements = 32 columns
           uint32_t v[32];
-          const int dblk = h * 4 + blk;
+          const int dblk = grp * kBlkPerGroup + blk;
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch) {
             const uint4 w = *reinterpret_cast<const uint4*>(src + dblk * 16384 + r * 128 +
@@ -358,14 +367,13 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       // Rows are shared by warps w and w+4 (64 columns each); the tile row max
       // and the final row sum are combined through shared memory, and both
       // halves take identical rescale decisions from identical inputs.
-      const int half = warp >> 2;
-      // [2 parity][2 half][128] in the resident area past the extra stages (free
+      // [2 parity][group][128] in the resident area past the extra stages (free
       // once Q is in TMEM; every math thread passed that point before use)
       float* pmax = reinterpret_cast<float*>(res_area + Cfg::kExtraStages * 32768);
-      float* lsum = pmax + 512;                         // [2 half][128]
+      float* lsum = pmax + 2 * kScoreGroups * 128;      // [group][128]
       const int64_t tile_base = static_cast<int64_t>(head) * p.head_cap_tiles + t_off;
       for (int j = tid; j < work; j += kScoreMathThreads) p.fwd_flags[tile_base + j] = 0;
-      asm volatile("bar.sync 2, 256;" ::: "memory");
+      asm volatile("bar.sync 2, %0;" ::"n"(kScoreMathThreads) : "memory");
       float m_run = -INFINITY, l_half = 0.f;
       for (int j = 0; j < work; ++j) {
         const int b = j & 1;
@@ -373,30 +381,29 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         const int cls = p.mask.doc ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
         if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
         ok = __all_sync(0xffffffffu, ok);
-        float sv[64];
+        constexpr int kCols = 32 * kChunksPerWarp;
+        float sv[kCols];
         if (ok) {
           tc_fence_after();
-          uint32_t r0[32], r1[32];
-          tmem_ld32(lane_base + s_col(b) + c_begin * 32, r0);
-          tmem_ld32(lane_base + s_col(b) + c_begin * 32 + 32, r1);
-          tmem_wait_ld();
-          reg_fence32(r0);
-          reg_fence32(r1);
+#pragma unroll
+          for (int cc = 0; cc < kChunksPerWarp; ++cc) {
+            uint32_t r0[32];
+            tmem_ld32(lane_base + s_col(b) + (c_begin + cc) * 32, r0);
+            tmem_wait_ld();
+            reg_fence32(r0);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sv[cc * 32 + i] = __uint_as_float(r0[i]);
+          }
           tc_fence_before();
           mbar_arrive(&misc->buf_free[b]);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            sv[i] = __uint_as_float(r0[i]);
-            sv[32 + i] = __uint_as_float(r1[i]);
-          }
         } else {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) sv[i] = -INFINITY;
+          for (int i = 0; i < kCols; ++i) sv[i] = -INFINITY;
         }
         const int kc = k0 + c_begin * 32;
-        if (!(cls == 1 && kc + 64 <= si.len_k)) {
+        if (!(cls == 1 && kc + kCols <= si.len_k)) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
+          for (int i = 0; i < kCols; ++i) {
             const int k = kc + i;
             bool keep = k < si.len_k;
             if (cls != 1 && keep) {
@@ -408,10 +415,13 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         }
         float mt = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mt = fmaxf(mt, sv[i]);
-        pmax[(j & 1) * 256 + half * 128 + r] = mt * kLog2e;
-        asm volatile("bar.sync 2, 256;" ::: "memory");
-        mt = fmaxf(pmax[(j & 1) * 256 + r], pmax[(j & 1) * 256 + 128 + r]);
+        for (int i = 0; i < kCols; ++i) mt = fmaxf(mt, sv[i]);
+        float* pm = pmax + (j & 1) * kScoreGroups * 128;
+        pm[grp * 128 + r] = mt * kLog2e;
+        asm volatile("bar.sync 2, %0;" ::"n"(kScoreMathThreads) : "memory");
+        mt = pm[r];
+#pragma unroll
+        for (int gi = 1; gi < kScoreGroups; ++gi) mt = fmaxf(mt, pm[gi * 128 + r]);
         float alpha = 1.f;
         if (mt > m_run + kLazyRescaleLog2) {  // lazy rescale; also the first finite tile
           alpha = m_run == -INFINITY ? 0.f : ex2(m_run - mt);
@@ -421,7 +431,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         float rowsum = 0.f;
         uint8_t* ptile = scratch_tile(p.p_tiles, p, head, t_off, j);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < kCols / 8; ++u) {
           float pe[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -436,15 +446,17 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           *reinterpret_cast<uint4*>(ptile + tile_chunk_offset(r, c_begin * 4 + u)) = w;
         }
         l_half = l_half * alpha + rowsum;
-        if (half == 0) {
+        if (grp == 0) {
           p.fwd_alpha[(tile_base + j) * 128 + r] = alpha;
           if (j > 0 && alpha != 1.f && row_valid) atomicOr(&p.fwd_flags[tile_base + j], 1);
         }
       }
-      lsum[half * 128 + r] = l_half;
-      asm volatile("bar.sync 2, 256;" ::: "memory");
-      if (half == 0 && row_valid) {
-        const float l = lsum[r] + lsum[128 + r];
+      lsum[grp * 128 + r] = l_half;
+      asm volatile("bar.sync 2, %0;" ::"n"(kScoreMathThreads) : "memory");
+      if (grp == 0 && row_valid) {
+        float l = 0.f;
+#pragma unroll
+        for (int gi = 0; gi < kScoreGroups; ++gi) l += lsum[gi * 128 + r];
         const float lse = l > 0.f ? (m_run + __log2f(l)) * kLn2 : -INFINITY;
         p.lse_out[static_cast<int64_t>(si.b_coord) * p.lse_stride[0] +
                   static_cast<int64_t>(head) * p.lse_stride[1] + si.q_base + q_idx] = lse;
@@ -466,7 +478,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       uint8_t* ptile = Cfg::kS || MODE == kScoreDs ? scratch_tile(p.p_tiles, p, head, t_off, j) : nullptr;
       uint8_t* dtile = Cfg::kDP ? scratch_tile(p.ds_tiles, p, head, t_off, j) : nullptr;
 #pragma unroll 1
-      for (int c = c_begin; c < c_begin + 2; ++c) {
+      for (int c = c_begin; c < c_begin + kChunksPerWarp; ++c) {
         uint32_t sr[32], dr[32];
         if (Cfg::kS && Cfg::kDP) {
           tmem_ld32(lane_base + s_col(b) + c * 32, sr);
@@ -483,7 +495,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           tmem_wait_ld();
           reg_fence32(dr);
         }
-        if (c == c_begin + 1) {  // this warp's TMEM values are all in registers
+        if (c == c_begin + kChunksPerWarp - 1) {  // this warp's TMEM values are in registers
           tc_fence_before();
           mbar_arrive(&misc->buf_free[b]);
         }
@@ -561,7 +573,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kProducerWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
