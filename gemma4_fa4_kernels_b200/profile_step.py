@@ -28,6 +28,10 @@ def main() -> None:
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
     ap.add_argument("--steps", type=int, default=1)
     ap.add_argument("--seq", type=int, default=None, help="override the sequence length")
+    ap.add_argument("--fwd", choices=("auto", "single"), default="auto",
+                    help="forward algorithm (auto: two-pass for d512 when the scratch fits)")
+    ap.add_argument("--bwd", choices=("auto", "recompute"), default="auto",
+                    help="backward algorithm (auto: materialised P/dS when the scratch fits)")
     args = ap.parse_args()
     c = dict(CONFIGS[args.config])
     if args.seq:
@@ -45,8 +49,8 @@ def main() -> None:
     do = torch.randn(1, s, hq, d, generator=g).to(torch.bfloat16).to(dev)
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        out, lse = ops.attn_fwd(q, k, v, window=c["window"])
-        ops.attn_bwd(q, k, v, out, lse, do, window=c["window"])
+        out, lse = ops.attn_fwd(q, k, v, window=c["window"], algorithm=args.fwd)
+        ops.attn_bwd(q, k, v, out, lse, do, window=c["window"], algorithm=args.bwd)
         torch.cuda.synchronize()
         print(f"step {time.perf_counter() - t0:.4f} s", flush=True)
 
