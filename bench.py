@@ -17,7 +17,9 @@ The JSON line carries, besides the contract keys:
                 sample of the same workload on this host's cores;
   e2e           the same metric through the public adapter with pinned host
                 buffers: H2D of q, k, v, dO and D2H of dq, dk, dv every step;
-  local_c0      the local d256 S2048 config measured the same way (secondary).
+  local_c0      the local d256 S2048 config measured the same way (secondary);
+  decode_c4     single-token decode against 32768-token global and 1024-token
+                local static caches (secondary): HBM GB/s of the decode kernel.
 """
 
 from __future__ import annotations
@@ -42,6 +44,11 @@ L2_BYTES = 126 * 1024**2
 
 C1 = dict(name="c1 global d512 causal fwd+bwd", seq=4096, hq=32, hkv=4, d=512, window=0)
 C0 = dict(name="c0 local d256 W1024 fwd+bwd", seq=2048, hq=32, hkv=16, d=256, window=1024)
+# BASELINE configs[4](iii): one query token against a static BF16 KV cache
+DECODE = (dict(key="global_d512", name="global d512 32Q/4KV, 32768-token cache", hq=32, hkv=4,
+               d=512, window=0, cache=32768),
+          dict(key="local_d256", name="local d256 32Q/16KV W1024, 1024-token rolling cache",
+               hq=32, hkv=16, d=256, window=1024, cache=1024))
 
 
 # ------------------------------------------------------------------------------------
@@ -94,6 +101,66 @@ def load_peaks():
             pk = json.load(f)
         return pk.get("bf16_tflops_sustained"), pk.get("bf16_tflops"), "measured"
     return 1400.0, 1590.0, "fallback"
+
+
+def load_hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get("hbm_gbs"), "measured"
+    return 6650.0, "fallback"
+
+
+def decode_measure(ops, _lib, dev, seed, iters):
+    """Single-token decode against each DECODE cache: device time per call and the
+    decode kernel's own time, L2 flushed before every call (the global cache is
+    268 MB, the local one 16.8 MB).  Algorithmic bytes = K + V of the active
+    cache + Q + O + LSE."""
+    g = torch.Generator().manual_seed(seed)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    hbm_peak, hbm_kind = load_hbm_peak()
+
+    def rms(x):
+        return x * torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + 1e-6)
+
+    out = {"l2": "flushed before every call", "hbm_peak_gbs": hbm_peak,
+           "peak_kind": f"{hbm_kind} HBM copy bandwidth"}
+    for c in DECODE:
+        cap, hq, hkv, d = c["cache"], c["hq"], c["hkv"], c["d"]
+        # static cache backings (B, H, capacity, D); the kernel reads (B, S, H, D) views
+        kc = rms(torch.randn(1, hkv, cap, d, generator=g)).to(torch.bfloat16).to(dev)
+        vc = rms(torch.randn(1, hkv, cap, d, generator=g)).to(torch.bfloat16).to(dev)
+        q = rms(torch.randn(1, 1, hq, d, generator=g)).to(torch.bfloat16).to(dev)
+        k, v = kc.transpose(1, 2), vc.transpose(1, 2)
+        for _ in range(3):
+            ops.attn_fwd(q, k, v, window=c["window"])
+        torch.cuda.synchronize(dev)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(iters)]
+        _lib.profile_reset()
+        _lib.profile_enable(True)
+        for a, b in evs:
+            flush.zero_()
+            a.record()
+            ops.attn_fwd(q, k, v, window=c["window"])
+            b.record()
+        torch.cuda.synchronize(dev)
+        _lib.profile_enable(False)
+        prof = _lib.profile_read()
+        call_us = statistics.median(a.elapsed_time(b) for a, b in evs) * 1e3
+        n_dec, dec_ms = prof.get("decode", (0, 0.0))
+        kern_us = dec_ms / max(n_dec, 1) * 1e3
+        nbytes = 2 * cap * hkv * d * 2 + 2 * hq * d * 2 + hq * 4
+        gbs = nbytes / (kern_us * 1e-6) / 1e9
+        out[c["key"]] = {"workload": c["name"], "us_per_call": round(call_us, 2),
+                         "decode_kernel_us": round(kern_us, 2), "bytes": nbytes,
+                         "kernel_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4),
+                         "call_gbs": round(nbytes / (call_us * 1e-6) / 1e9, 1),
+                         "launches_per_call": {n: prof[n][0] // iters for n in prof
+                                               if prof[n][0] > 0}}
+        del kc, vc, q, k, v
+    del flush
+    return out
 
 
 def load_traffic():
@@ -313,6 +380,9 @@ def run_b200(args, world, rank, local):
     local_tf = flops_of(C0)["total"] / (lms * 1e-3) / 1e12
     del lq, lk, lv, ldo
 
+    # ---- single-token decode (secondary line item, BASELINE configs[4](iii)) ----
+    decode = decode_measure(ops, _lib, dev, seed=3000 + rank, iters=50)
+
     # ---- end to end through the public adapter, host buffers ----
     hq_, hk_, hv_, hdo_ = (t.cpu().pin_memory() for t in (q, k, v, do))
     hgrads = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, k, v)]
@@ -376,6 +446,7 @@ def run_b200(args, world, rank, local):
             "local_c0": {"workload": C0["name"] + " (BASELINE configs[0])",
                          "ms_per_step": round(lms, 4), "value": round(local_tf, 2),
                          "unit": "TFLOP/s", "pct_peak": round(local_tf / peak_sus, 4)},
+            "decode_c4": decode,
         }
         print(json.dumps(line), flush=True)
 
@@ -414,8 +485,8 @@ def run_reference(args, world, rank):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--cpu-heads", type=int, default=4,
                     help="query heads in the CPU-baseline sample")

@@ -51,12 +51,15 @@ enum KernelId {
   kKGemmDq,
   kKFwdScore,
   kKFwdPv,
+  kKDecode,
+  kKDecodeCombine,
   kKCount
 };
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
                                            "plan",     "mask",           "bwd_score",
                                            "bwd_gemm_dv", "bwd_gemm_dk", "bwd_gemm_dq",
-                                           "fwd_score",   "fwd_pv"};
+                                           "fwd_score",   "fwd_pv",      "decode",
+                                           "decode_combine"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -194,6 +197,11 @@ struct Workspace {
   size_t fwd_alpha = 0;    // two-pass forward: float[Hq * head_cap * 128]
   size_t fwd_flags = 0;    // int[Hq * head_cap]
   size_t fwd_inv_l = 0;    // float[Hq * tokens_q]
+  // single-token decode
+  bool decode = false;
+  int decode_splits = 0;
+  size_t part_o = 0;       // float[B * Hq * splits * D]
+  size_t part_ml = 0;      // float2[B * Hq * splits]
   bool materialized = false;
   int n_qt_total = 0;
   int64_t head_cap_tiles = 0;
@@ -202,6 +210,50 @@ struct Workspace {
   int max_k_tiles = 0;
   int64_t tokens_q = 0;
 };
+
+// SM count of the current device (148 on B200; also the answer when no device
+// is visible, so that size queries work on hosts without a GPU).
+int sm_count() {
+  constexpr int kDev = 64;
+  static std::atomic<int> cached[kDev];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDev) {
+    cudaGetLastError();
+    return 148;
+  }
+  int n = cached[dev].load();
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cached[dev].store(n);
+  }
+  return n;
+}
+
+// One query token per sequence: the split-key decode kernels serve the call.
+bool decode_eligible(const g4_attn_args* a) {
+  const bool packed = a->cu_seqlens_q != nullptr;
+  const int sq = packed ? a->max_seqlen_q : a->seqlen_q;
+  return sq == 1 && a->num_kv_heads > 0 && a->num_q_heads % a->num_kv_heads == 0 &&
+         a->num_q_heads / a->num_kv_heads <= g4::kDecodeMaxGroup;
+}
+
+// Key-range splits per (sequence, KV head): enough CTAs for one per SM, never
+// more splits than 128-key tiles, and no split left without a tile at the
+// longest sequence.
+int decode_splits(const g4_attn_args* a) {
+  const bool packed = a->cu_seqlens_q != nullptr;
+  int64_t keys = packed ? a->max_seqlen_k : a->seqlen_k;
+  if (a->window > 0) keys = std::min<int64_t>(keys, a->window);
+  const int64_t max_tiles = std::max<int64_t>(1, (keys + g4::kTileN - 1) / g4::kTileN);
+  const int64_t units = std::max<int64_t>(1, int64_t(a->batch) * a->num_kv_heads);
+  int64_t n = (sm_count() + units - 1) / units;
+  n = std::max<int64_t>(1, std::min(n, max_tiles));
+  const int64_t tps = (max_tiles + n - 1) / n;
+  return static_cast<int>((max_tiles + tps - 1) / tps);
+}
 
 // Upper bound of scratch tiles per query head for the materialised backward:
 // exact band sizes for fixed layouts, a per-tile bound for packed layouts.
@@ -236,6 +288,20 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 Workspace plan_workspace(const g4_attn_args* a, int mode) {
   Workspace w;
   const bool packed = a->cu_seqlens_q != nullptr;
+  if ((mode == 0 || mode == 3) && decode_eligible(a)) {
+    size_t off = 256;
+    w.decode = true;
+    w.decode_splits = decode_splits(a);
+    if (w.decode_splits > 1) {
+      const size_t rows = size_t(a->batch) * size_t(a->num_q_heads) * size_t(w.decode_splits);
+      w.part_o = off;
+      off = align256(off + rows * size_t(a->head_dim_v) * sizeof(float));
+      w.part_ml = off;
+      off = align256(off + rows * 2 * sizeof(float));
+    }
+    w.total = off;
+    return w;
+  }
   const bool vision = a->vision_ids && a->window > 0;
   const bool two_pass_fwd = mode == 3 && !vision && a->head_dim_qk == 512;
   const int backward = (mode == 1 || mode == 2) ? mode : 0;
@@ -360,6 +426,57 @@ int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream
   return G4_OK;
 }
 
+// Single-token decode: split-key kernel, then the merge of the splits.
+int run_decode(const g4_attn_args* a, cudaStream_t st) {
+  const Workspace w = plan_workspace(a, 0);
+  if (!a->workspace || a->workspace_bytes < w.total)
+    return fail(G4_ERR_WORKSPACE, "workspace of %zu bytes required", w.total);
+  cudaError_t ce = cudaMemsetAsync(a->workspace, 0, 256, st);
+  if (ce != cudaSuccess) return cuda_fail(ce, "workspace reset");
+  const bool packed = a->cu_seqlens_q != nullptr;
+  g4::DecodeParams p;
+  memset(&p, 0, sizeof(p));
+  p.layout = make_layout(a);
+  p.window = a->window;
+  p.doc = a->window > 0 ? a->document_ids : nullptr;
+  p.group = a->num_q_heads / a->num_kv_heads;
+  p.num_q_heads = a->num_q_heads;
+  p.n_split = w.decode_splits;
+  p.q = static_cast<const __nv_bfloat16*>(a->q);
+  p.o = static_cast<__nv_bfloat16*>(a->o);
+  for (int i = 0; i < 3; ++i) {
+    p.q_stride[i] = a->q_stride[i];
+    p.o_stride[i] = a->o_stride[i];
+  }
+  p.lse = a->lse;
+  p.lse_stride[0] = packed ? 0 : a->lse_stride[0];
+  p.lse_stride[1] = packed ? a->seqlen_q : a->lse_stride[1];
+  p.part_o = w.part_o ? ws_ptr<float>(a, w.part_o) : nullptr;
+  p.part_ml = w.part_ml ? ws_ptr<float2>(a, w.part_ml) : nullptr;
+  p.err = ws_ptr<int>(a, 0);
+  const int D = a->head_dim_qk;
+  const int64_t bk = packed ? 1 : a->batch;
+  CUtensorMap tk, tv;
+  int rc;
+  if ((rc = make_map(&tk, a->k, D, a->num_kv_heads, a->seqlen_k, bk, a->k_stride[2],
+                     a->k_stride[1], a->k_stride[0], 128)))
+    return rc;
+  if ((rc = make_map(&tv, a->v, a->head_dim_v, a->num_kv_heads, a->seqlen_k, bk, a->v_stride[2],
+                     a->v_stride[1], a->v_stride[0], 128)))
+    return rc;
+  {
+    LaunchScope ls(kKDecode, st);
+    const int e = g4::launch_decode(D, tk, tv, p, a->num_kv_heads, st);
+    if (e) return cuda_fail(static_cast<cudaError_t>(e), "decode launch");
+  }
+  if (p.n_split > 1) {
+    LaunchScope ls(kKDecodeCombine, st);
+    const int e = g4::launch_decode_combine(D, p, st);
+    if (e) return cuda_fail(static_cast<cudaError_t>(e), "decode combine launch");
+  }
+  return G4_OK;
+}
+
 // Scratch for g4_attn_bwd_noalloc: a fixed-size static device array instead of
 // a caller-provided workspace.  Host code must not use the symbol itself as a
 // device address; noalloc_scratch() fetches the real address once per device.
@@ -421,6 +538,7 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
   if (!packed && (a->lse_stride[0] <= 0 || a->lse_stride[1] <= 0))
     return fail(G4_ERR_INVALID, "lse strides must be positive");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (decode_eligible(a)) return run_decode(a, st);
   // Two-pass d512 forward (P tiles in HBM, no QK^T recomputation) when the
   // workspace holds its scratch; otherwise the single-kernel forward.
   const Workspace w3 = plan_workspace(a, 3);

@@ -89,6 +89,33 @@ struct MatParams {
   int* err;
 };
 
+// Single-token decode against a (static) KV cache (attn_decode.cu): one query
+// token per sequence, keys split across CTAs, partial results merged by a
+// second kernel unless one split covers the whole key range.
+struct DecodeParams {
+  SeqLayout layout;                // fixed: Sq == 1; packed: every segment has <= 1 query
+  int window;                      // 0 = global
+  const int* doc;                  // nullable; local layers only
+  int group;                       // query heads per KV head, <= kDecodeMaxGroup
+  int num_q_heads;
+  int n_split;                     // key-range splits per (sequence, KV head)
+  const __nv_bfloat16* q;
+  int64_t q_stride[3];             // batch, token, head (elements)
+  __nv_bfloat16* o;
+  int64_t o_stride[3];
+  float* lse;
+  int64_t lse_stride[2];           // batch, head (floats); token stride 1
+  float* part_o;                   // [seq][Hq][n_split][D] unnormalised O (n_split > 1)
+  float2* part_ml;                 // [seq][Hq][n_split] (running max log2, row sum)
+  int* err;
+};
+constexpr int kDecodeMaxGroup = 16;
+constexpr int kDecodeStages = 6;   // 32 KB ring stages
+int decode_smem_bytes(int d);
+int launch_decode(int d, const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
+                  int num_kv_heads, cudaStream_t stream);
+int launch_decode_combine(int d, const DecodeParams& p, cudaStream_t stream);
+
 int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream);
 // pass: d512 runs pass 0 (P) then pass 1 (dS); d256 computes both in pass 0;
 // pass 2 is the forward's first pass (online softmax, d512 only).

@@ -233,6 +233,18 @@ __device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
 }
+// Load 16 consecutive columns of this thread's lane (no wait).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : G4_R8(0), G4_R8(8)
+      : "r"(taddr));
+}
+__device__ __forceinline__ void reg_fence16(uint32_t (&r)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) asm volatile("" : "+r"(r[i]));
+}
 // Store 32 consecutive columns of this thread's lane.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
