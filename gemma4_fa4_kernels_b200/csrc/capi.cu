@@ -250,7 +250,7 @@ int decode_splits(const g4_attn_args* a) {
   const int64_t max_tiles = std::max<int64_t>(1, (keys + g4::kTileN - 1) / g4::kTileN);
   const int64_t units = std::max<int64_t>(1, int64_t(a->batch) * a->num_kv_heads);
   int64_t n = (sm_count() + units - 1) / units;
-  n = std::max<int64_t>(1, std::min(n, max_tiles));
+  n = std::max<int64_t>(1, std::min<int64_t>(std::min(n, max_tiles), g4::kDecodeMaxSplits));
   const int64_t tps = (max_tiles + n - 1) / n;
   return static_cast<int>((max_tiles + tps - 1) / tps);
 }

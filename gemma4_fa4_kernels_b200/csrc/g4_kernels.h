@@ -110,6 +110,7 @@ struct DecodeParams {
   int* err;
 };
 constexpr int kDecodeMaxGroup = 16;
+constexpr int kDecodeMaxSplits = 1024;
 constexpr int kDecodeStages = 6;   // 32 KB ring stages
 int decode_smem_bytes(int d);
 int launch_decode(int d, const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p,
