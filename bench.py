@@ -246,10 +246,12 @@ def dist_setup():
 
         import torch.distributed as dist
 
-        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        kw = {}
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            kw["device_id"] = torch.device("cuda", local)
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     return world, rank, local
 
 

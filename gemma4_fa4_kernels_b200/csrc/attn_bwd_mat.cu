@@ -424,7 +424,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         for (int gi = 1; gi < kScoreGroups; ++gi) mt = fmaxf(mt, pm[gi * 128 + r]);
         float alpha = 1.f;
         if (mt > m_run + kLazyRescaleLog2) {  // lazy rescale; also the first finite tile
-          alpha = m_run == -INFINITY ? 0.f : ex2(m_run - mt);
+          // a row without any finite score so far has O = 0 and l = 0: it needs
+          // no correction (alpha stays 1, the tile is not flagged for it)
+          if (m_run != -INFINITY) alpha = ex2(m_run - mt);
           m_run = mt;
         }
         const float m_sub = m_run == -INFINITY ? 0.f : m_run;

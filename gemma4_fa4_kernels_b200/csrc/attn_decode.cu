@@ -322,9 +322,12 @@ __global__ void __launch_bounds__(192, 1)
       for (int j = 0; j < 16; ++j) {
         alpha[j] = 1.f;
         if (mt[j] > m_run[j] + kLazyRescaleLog2) {  // also the first finite tile
-          alpha[j] = (m_run[j] == -INFINITY) ? 0.f : ex2(m_run[j] - mt[j]);
+          // a head without any finite score so far has O = 0 and l = 0
+          if (m_run[j] != -INFINITY) {
+            alpha[j] = ex2(m_run[j] - mt[j]);
+            rescale = true;
+          }
           m_run[j] = mt[j];
-          rescale = true;
         }
         const float m_sub = (m_run[j] == -INFINITY) ? 0.f : m_run[j];
         pv[j] = ex2(s[j] - m_sub);

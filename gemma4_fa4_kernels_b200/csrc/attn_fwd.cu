@@ -322,9 +322,12 @@ __global__ void __launch_bounds__(192, 1)
       float alpha = 1.f;
       bool rescale = false;
       if (mt > m_run + kLazyRescaleLog2) {  // also true for the first finite tile
-        alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - mt);
+        // a row without any finite score so far has O = 0 and l = 0: no correction
+        if (m_run != -INFINITY) {
+          alpha = ex2(m_run - mt);
+          rescale = true;
+        }
         m_run = mt;
-        rescale = true;
       }
       const float m_sub = (m_run == -INFINITY) ? 0.f : m_run;
       float rowsum = 0.f;

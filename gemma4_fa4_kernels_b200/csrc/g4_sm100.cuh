@@ -274,11 +274,15 @@ __device__ __forceinline__ void tmem_wait_st() {
 // ------------------------------------------------------------------------------------
 constexpr float kLog2e = 1.4426950408889634f;
 // Online softmax keeps a stale running max until a tile's max exceeds it by
-// more than this many powers of two; P (bf16) then stays below 2^32 and every
-// fp32 row sum / accumulator stays far inside range (2^32 * 2^18 keys).  With
-// unit-RMS d512 vectors the score spread is ~32 in log2 units, so a smaller
-// threshold would rescale O (a pipeline drain) on most tiles.
-constexpr float kLazyRescaleLog2 = 32.f;
+// more than this many powers of two, so P (bf16, whose relative precision does
+// not depend on magnitude) stays below 2^80 and an fp32 row sum or O element
+// stays below 2^80 * 2^18 keys * max|V| -- inside fp32 range for |V| < 2^29
+// (Gemma-4 values are RMS-normalised).  A rescale drains the MMA pipeline
+// (and, in the two-pass forward, rescales a whole 128 x 512 accumulator), so
+// the threshold is set where rescales become rare: with unit-RMS d512 vectors
+// the score spread is ~30 log2 units and 82% of the causal key tiles of a
+// 4096-token sequence would rescale at a threshold of 32, 0.8% at 80.
+constexpr float kLazyRescaleLog2 = 80.f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 __device__ __forceinline__ float ex2(float x) {

@@ -143,3 +143,20 @@ def test_global_forward_only_adapter_runs_decode():
                                           bshd_to_bhsd_np(v))
     assert rel_l2(out.float().cpu().numpy(), bhsd_to_bshd(ref_o)) <= REL_L2_TOL
     assert lse_abs_err(lse.cpu().numpy(), ref_lse) <= LSE_ABS_TOL
+
+
+def test_decode_rescales_when_the_running_max_jumps():
+    # Growing keys move every head's running max far past the lazy-rescale
+    # threshold from one key split / tile to the next.
+    sk = 3000
+    q, k, v = make_inputs((1, 1, 8, 512), (1, sk, 1, 512), (1, sk, 1, 512), seed=93,
+                          with_dout=False)
+    ramp = torch.linspace(0.1, 8.0, sk, device="cuda").view(1, sk, 1, 1)
+    k = (k.float() * ramp).to(torch.bfloat16)
+    q = (q.float() + 0.5 * k.float().mean(dim=1, keepdim=True).expand_as(q)).to(torch.bfloat16)
+    out, lse = ops.attn_fwd(q, k, v, window=0)
+    torch.cuda.synchronize()
+    ref_o, ref_lse = oracle.attention_fwd(bshd_to_bhsd_np(q), bshd_to_bhsd_np(k),
+                                          bshd_to_bhsd_np(v))
+    assert rel_l2(out.float().cpu().numpy(), bhsd_to_bshd(ref_o)) <= REL_L2_TOL
+    assert lse_abs_err(lse.cpu().numpy(), ref_lse) <= LSE_ABS_TOL

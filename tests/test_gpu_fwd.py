@@ -135,17 +135,20 @@ def test_global_two_pass_and_single_kernel_forward_agree_with_oracle(shape):
         assert lse_abs_err(lse.cpu().numpy(), ref_lse) <= LSE_ABS_TOL, algo
 
 
-def test_global_two_pass_rescales_when_the_running_max_jumps():
-    # Keys whose scores grow along the sequence force several lazy rescales.
-    s = 600
+@pytest.mark.parametrize("algo", ["auto", "single"])
+def test_global_rescales_when_the_running_max_jumps(algo):
+    # Keys scaled by a growing ramp and queries aligned with their mean make the
+    # row maxima climb by hundreds of log2 units across the key tiles, far past
+    # the lazy-rescale threshold, so both forwards must rescale O repeatedly.
+    s = 900
     q, k, v = make_inputs((1, s, 8, 512), (1, s, 1, 512), (1, s, 1, 512), seed=92,
                           with_dout=False)
-    ramp = torch.linspace(0.2, 3.0, s, device="cuda").view(1, s, 1, 1)
+    ramp = torch.linspace(0.1, 8.0, s, device="cuda").view(1, s, 1, 1)
     k = (k.float() * ramp).to(torch.bfloat16)
-    q = (q.float() + k.float().mean(dim=1, keepdim=True).expand_as(q)).to(torch.bfloat16)
+    q = (q.float() + 0.5 * k.float().mean(dim=1, keepdim=True).expand_as(q)).to(torch.bfloat16)
     ref_o, ref_lse = oracle.attention_fwd(bshd_to_bhsd_np(q), bshd_to_bhsd_np(k),
                                           bshd_to_bhsd_np(v))
-    out, lse = ops.attn_fwd(q, k, v, window=0)
+    out, lse = ops.attn_fwd(q, k, v, window=0, algorithm=algo)
     torch.cuda.synchronize()
     assert rel_l2(out.float().cpu().numpy(), bhsd_to_bshd(ref_o)) <= REL_L2_TOL
     assert lse_abs_err(lse.cpu().numpy(), ref_lse) <= LSE_ABS_TOL
