@@ -121,12 +121,17 @@ struct ScoreCfg {
   // memory then holds a ring of P tiles for the dS pass.
   static constexpr bool kTS = D == 512 && MODE != kScorePdS;
   // TS variant: once the resident operand sits in TMEM its 128 KB of shared
-  // memory extends the operand ring (more bytes in flight per SM): the P pass
-  // gets 3 + 4 K stages; the dS pass 3 + 2 V stages and 2 P stages.
-  // (the forward pass keeps 32 KB of that area for its row-statistics exchange)
-  static constexpr int kExtraStages = kTS ? (MODE == kScoreDs ? 2 : (MODE == kScoreFwd ? 3 : 4)) : 0;
+  // memory (four 32 KB slots) extends the operand ring (more bytes in flight
+  // per SM): the P pass gets 3 + 3 K stages and one slot that stages each P
+  // tile for a single 32 KB bulk store; the forward pass 3 + 2 K stages, the
+  // staging slot and a slot for its row-statistics exchange; the dS pass
+  // 3 + 2 V stages and 2 P stages.
+  static constexpr int kExtraStages = kTS ? (MODE == kScoreP ? 3 : 2) : 0;
   static constexpr int kRingStages = kStages + kExtraStages;
   static constexpr int kPStages = 2;
+  // P tiles leave through a shared-memory staging slot and one bulk store
+  // (a warp's direct 16-B row-chunk stores would touch 32 lines each).
+  static constexpr bool kStageP = kTS && (MODE == kScoreP || MODE == kScoreFwd);
 };
 
 struct ScoreMisc {
@@ -139,6 +144,7 @@ struct ScoreMisc {
   uint64_t p_full[4];     // P tiles in shared memory (dS pass, TS variant)
   uint64_t p_empty[4];
   uint64_t drain;
+  uint64_t stg_free;      // staging slot read by the previous tile's bulk store
   uint32_t tmem_base;
   int abort;
 };
@@ -201,6 +207,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     }
     mbar_init(&misc->a_ready, kScoreMathThreads);
     mbar_init(&misc->drain, 1);
+    mbar_init(&misc->stg_free, 1);
     misc->abort = 0;
     fence_mbar_init();
   }
@@ -225,8 +232,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     return st < static_cast<uint32_t>(Cfg::kStages) ? ring + st * 32768
                                                      : res_area + (st - Cfg::kStages) * 32768;
   };
-  // TS dS pass: P ring after the extra V stages in the resident area
+  // TS dS pass: P ring after the extra V stages in the resident area; P and
+  // forward passes: the staging slot there
   uint8_t* pring = res_area + Cfg::kExtraStages * 32768;
+  uint8_t* stg = res_area + Cfg::kExtraStages * 32768;
 
   if (warp == kProducerWarp) {
     if (lane == 0 && work > 0) {
@@ -369,7 +378,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       // halves take identical rescale decisions from identical inputs.
       // [2 parity][group][128] in the resident area past the extra stages (free
       // once Q is in TMEM; every math thread passed that point before use)
-      float* pmax = reinterpret_cast<float*>(res_area + Cfg::kExtraStages * 32768);
+      float* pmax = reinterpret_cast<float*>(res_area + (Cfg::kExtraStages + 1) * 32768);
       float* lsum = pmax + 2 * kScoreGroups * 128;      // [group][128]
       const int64_t tile_base = static_cast<int64_t>(head) * p.head_cap_tiles + t_off;
       for (int j = tid; j < work; j += kScoreMathThreads) p.fwd_flags[tile_base + j] = 0;
@@ -432,6 +441,11 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         const float m_sub = m_run == -INFINITY ? 0.f : m_run;
         float rowsum = 0.f;
         uint8_t* ptile = scratch_tile(p.p_tiles, p, head, t_off, j);
+        // the staging slot is free once the previous tile's bulk store read it
+        if (j > 0) {
+          if (ok) ok = mbar_wait(&misc->stg_free, (j - 1) & 1, ab, kDevTimeoutPeer);
+          ok = __all_sync(0xffffffffu, ok);
+        }
 #pragma unroll
         for (int u = 0; u < kCols / 8; ++u) {
           float pe[8];
@@ -445,7 +459,15 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           w.y = pack_bf16x2(pe[2], pe[3]);
           w.z = pack_bf16x2(pe[4], pe[5]);
           w.w = pack_bf16x2(pe[6], pe[7]);
-          *reinterpret_cast<uint4*>(ptile + tile_chunk_offset(r, c_begin * 4 + u)) = w;
+          *reinterpret_cast<uint4*>(stg + tile_chunk_offset(r, c_begin * 4 + u)) = w;
+        }
+        // every math thread wrote its chunks: one bulk store moves the tile
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
+        if (tid == 0 && ok) {
+          bulk_store(ptile, stg, kTileBytes);
+          bulk_store_wait_read();
+          mbar_arrive(&misc->stg_free);
         }
         l_half = l_half * alpha + rowsum;
         if (grp == 0) {
@@ -453,6 +475,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           if (j > 0 && alpha != 1.f && row_valid) atomicOr(&p.fwd_flags[tile_base + j], 1);
         }
       }
+      if (tid == 0) bulk_store_wait_all();  // the P tiles are written before the kernel ends
       lsum[grp * 128 + r] = l_half;
       asm volatile("bar.sync 2, %0;" ::"n"(kScoreMathThreads) : "memory");
       if (grp == 0 && row_valid) {
@@ -473,8 +496,14 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       if (ok && Cfg::kTS && MODE == kScoreDs)
         ok = mbar_wait(&misc->p_full[j % Cfg::kPStages], (j / Cfg::kPStages) & 1, ab,
                        kDevTimeoutTma);
+      if (Cfg::kStageP && j > 0 && ok)
+        ok = mbar_wait(&misc->stg_free, (j - 1) & 1, ab, kDevTimeoutPeer);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok) continue;
+      if (!ok) {
+        // keep the staging barrier count identical across warps
+        if (Cfg::kStageP) asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
+        continue;
+      }
       tc_fence_after();
       const uint8_t* psm = pring + (j % Cfg::kPStages) * 32768;
       uint8_t* ptile = Cfg::kS || MODE == kScoreDs ? scratch_tile(p.p_tiles, p, head, t_off, j) : nullptr;
@@ -539,6 +568,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           }
         }
         if (MODE != kScoreDs) {
+          uint8_t* pdst = Cfg::kStageP ? stg : ptile;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 w;
@@ -546,7 +576,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             w.y = pack_bf16x2(pv[u * 8 + 2], pv[u * 8 + 3]);
             w.z = pack_bf16x2(pv[u * 8 + 4], pv[u * 8 + 5]);
             w.w = pack_bf16x2(pv[u * 8 + 6], pv[u * 8 + 7]);
-            *reinterpret_cast<uint4*>(ptile + tile_chunk_offset(r, c * 4 + u)) = w;
+            *reinterpret_cast<uint4*>(pdst + tile_chunk_offset(r, c * 4 + u)) = w;
           }
         }
         if (Cfg::kDP) {
@@ -570,7 +600,19 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         fence_proxy_async_smem();
         mbar_arrive(&misc->p_empty[j % Cfg::kPStages]);
       }
+      if (Cfg::kStageP) {
+        // every math thread wrote its chunks: one bulk store moves the tile
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
+        if (tid == 0) {
+          bulk_store(ptile, stg, kTileBytes);
+          bulk_store_wait_read();
+          mbar_arrive(&misc->stg_free);
+        }
+      }
     }
+    // the tiles' bulk stores are complete before the kernel can finish
+    if (Cfg::kStageP && tid == 0) bulk_store_wait_all();
   }
 
   tc_fence_before();
