@@ -177,12 +177,15 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   ScoreMisc* misc = reinterpret_cast<ScoreMisc*>(ring + Cfg::kStages * 32768);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int head = blockIdx.y;
+  // grid (heads, query tiles): the head index varies fastest in launch order, so
+  // every head's longest causal rows are dispatched first (longest-first over
+  // the whole grid, which keeps the tail of the launch short)
+  const int head = blockIdx.x;
   const int kv_head = head / p.group;
   const bool packed = p.layout.packed();
   const int n_tiles = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
-  if (static_cast<int>(blockIdx.x) >= n_tiles) return;
-  const int g = n_tiles - 1 - static_cast<int>(blockIdx.x);  // longest causal rows first
+  if (static_cast<int>(blockIdx.y) >= n_tiles) return;
+  const int g = n_tiles - 1 - static_cast<int>(blockIdx.y);  // longest causal rows first
   const int4 rg = p.ranges[g];
   const int kt_lo = rg.x, n_kt = rg.y, t_off = rg.z, seq = rg.w;
   const int qt = packed ? p.q_tiles[g].y : g % p.n_qt_fixed;
@@ -681,9 +684,10 @@ __global__ void __launch_bounds__(192, 1)
   int half = 0;         // dV/dK: which 256-column half
   if (Cfg::kQMajor) {
     const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
-    if (static_cast<int>(blockIdx.x) >= n) return;
-    qg = n - 1 - static_cast<int>(blockIdx.x);
-    head = blockIdx.y;
+    // grid (heads, query tiles), head fastest: longest-first over the whole grid
+    if (static_cast<int>(blockIdx.y) >= n) return;
+    qg = n - 1 - static_cast<int>(blockIdx.y);
+    head = blockIdx.x;
     seq = p.ranges[qg].w;
     tile = packed ? p.q_tiles[qg].y : qg % p.n_qt_fixed;
   } else {
@@ -961,7 +965,7 @@ static int launch_score_impl(const CUtensorMap& tq, const CUtensorMap& tk, const
   cudaError_t e = cudaFuncSetAttribute(bwd_score_kernel<D, MODE>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(grid_x, p.num_q_heads);
+  dim3 grid(p.num_q_heads, grid_x);
   bwd_score_kernel<D, MODE><<<grid, kScoreThreads, smem, stream>>>(tq, tk, tv, tdo, p);
   return static_cast<int>(cudaGetLastError());
 }
@@ -987,7 +991,7 @@ static int launch_gemm_impl(const CUtensorMap& tb, const MatParams& p, int grid_
   cudaError_t e = cudaFuncSetAttribute(bwd_tile_gemm_kernel<D, WHICH>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(grid_x, grid_y);
+  dim3 grid = Cfg::kQMajor ? dim3(grid_y, grid_x) : dim3(grid_x, grid_y);
   bwd_tile_gemm_kernel<D, WHICH><<<grid, 192, smem, stream>>>(tb, p);
   return static_cast<int>(cudaGetLastError());
 }

@@ -73,21 +73,24 @@ __global__ void __launch_bounds__(192, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int head = blockIdx.y;
+  // grid (heads, work items, slabs): the head index varies fastest in launch
+  // order, so the longest causal rows of every head are dispatched first
+  const int head = blockIdx.x;
+  const int item = blockIdx.y;
   const int slab = blockIdx.z;
   const int kv_head = head / p.group;
 
   // ---- work item -> (sequence, query tile) ----
   int seq, qt;
   if (p.tiles != nullptr) {
-    if (static_cast<int>(blockIdx.x) >= *p.n_tiles) return;
-    const int2 t = p.tiles[blockIdx.x];
+    if (item >= *p.n_tiles) return;
+    const int2 t = p.tiles[item];
     seq = t.x;
     qt = t.y;
   } else {
     const int nqt = (p.layout.seqlen_q + kTileM - 1) / kTileM;
-    seq = blockIdx.x / nqt;
-    qt = nqt - 1 - static_cast<int>(blockIdx.x % nqt);  // longest causal rows first
+    seq = item % p.layout.batch;
+    qt = nqt - 1 - item / p.layout.batch;  // longest causal rows first
   }
   const SeqInfo si = p.layout.seq(seq);
   const int q_off = si.len_k - si.len_q;
@@ -428,7 +431,7 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<DQK>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(grid_x, num_q_heads, slabs);
+  dim3 grid(num_q_heads, grid_x, slabs);
   attn_fwd_kernel<DQK><<<grid, 192, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
   return static_cast<int>(cudaGetLastError());
 }
