@@ -39,7 +39,11 @@ namespace g4 {
 // =====================================================================================
 // 1. preprocess
 // =====================================================================================
-__global__ void bwd_preprocess_kernel(const BwdParams p, int dv, int64_t tokens_q) {
+// One warp per (token, head) row; every load of the row is issued before the
+// first multiply (DV / 256 pairs of 16-B loads per lane) so that a warp keeps
+// the whole row in flight.
+template <int DV>
+__global__ void __launch_bounds__(256) bwd_preprocess_kernel(const BwdParams p, int64_t tokens_q) {
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= tokens_q * p.num_q_heads) return;
@@ -55,12 +59,18 @@ __global__ void bwd_preprocess_kernel(const BwdParams p, int dv, int64_t tokens_
   }
   const __nv_bfloat16* o = p.o + b * p.o_stride[0] + s * p.o_stride[1] + h * p.o_stride[2];
   const __nv_bfloat16* g = p.dout + b * p.do_stride[0] + s * p.do_stride[1] + h * p.do_stride[2];
+  constexpr int kIters = DV / 256;
+  uint4 ov[kIters], gv[kIters];
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    ov[it] = *reinterpret_cast<const uint4*>(o + it * 256 + lane * 8);
+    gv[it] = *reinterpret_cast<const uint4*>(g + it * 256 + lane * 8);
+  }
   float acc = 0.f;
-  for (int c = lane * 8; c < dv; c += 32 * 8) {
-    const uint4 ov = *reinterpret_cast<const uint4*>(o + c);
-    const uint4 gv = *reinterpret_cast<const uint4*>(g + c);
-    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
-    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov[it]);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[it]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 a = __bfloat1622float2(o2[i]);
@@ -87,8 +97,10 @@ int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int64_t tokens_q,
   const int threads = 256;
   const int64_t blocks = (rows * 32 + threads - 1) / threads;
   if (blocks == 0) return 0;
-  bwd_preprocess_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p, head_dim_v,
-                                                                               tokens_q);
+  if (head_dim_v == 256)
+    bwd_preprocess_kernel<256><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p, tokens_q);
+  else
+    bwd_preprocess_kernel<512><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p, tokens_q);
   return static_cast<int>(cudaGetLastError());
 }
 
