@@ -3,9 +3,10 @@
     python -m gemma4_fa4_kernels_b200.profile_step --config c1 --steps 1
 
 Configs: c0 (local d256 W1024, S=2048, 32Q/16KV) and c1 (global d512 causal,
-S=4096, 32Q/4KV), B=1, BF16, inputs as in bench.py.  Inputs exceed the 126 MB
-L2 for c1.  Prints nothing but the per-step wall time; meant to be wrapped by
-ncu with -k/-c filters.
+S=4096, 32Q/4KV), B=1, BF16, inputs as in bench.py; decode (one query token
+against a 32768-token global d512 32Q/4KV static cache, forward only).  Inputs
+exceed the 126 MB L2 for c1 and decode.  Prints nothing but the per-step wall
+time; meant to be wrapped by ncu with -k/-c filters.
 """
 
 from __future__ import annotations
@@ -20,6 +21,7 @@ from . import ops
 CONFIGS = {
     "c0": dict(seq=2048, hq=32, hkv=16, d=256, window=1024),
     "c1": dict(seq=4096, hq=32, hkv=4, d=512, window=0),
+    "decode": dict(seq=32768, hq=32, hkv=4, d=512, window=0),
 }
 
 
@@ -43,6 +45,17 @@ def main() -> None:
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
 
     s, hq, hkv, d = c["seq"], c["hq"], c["hkv"], c["d"]
+    if args.config == "decode":
+        # static cache backings (B, H, capacity, D), read through (B, S, H, D) views
+        kc = rms(torch.randn(1, hkv, s, d, generator=g)).to(torch.bfloat16).to(dev)
+        vc = rms(torch.randn(1, hkv, s, d, generator=g)).to(torch.bfloat16).to(dev)
+        q = rms(torch.randn(1, 1, hq, d, generator=g)).to(torch.bfloat16).to(dev)
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            ops.attn_fwd(q, kc.transpose(1, 2), vc.transpose(1, 2), window=c["window"])
+            torch.cuda.synchronize()
+            print(f"step {time.perf_counter() - t0:.4f} s", flush=True)
+        return
     q = rms(torch.randn(1, s, hq, d, generator=g)).to(torch.bfloat16).to(dev)
     k = rms(torch.randn(1, s, hkv, d, generator=g)).to(torch.bfloat16).to(dev)
     v = rms(torch.randn(1, s, hkv, d, generator=g)).to(torch.bfloat16).to(dev)
