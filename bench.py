@@ -155,7 +155,9 @@ def decode_measure(ops, _lib, dev, seed, iters):
         kern_us = dec_ms / max(n_dec, 1) * 1e3
         nbytes = 2 * cap * hkv * d * 2 + 2 * hq * d * 2 + hq * 4
         gbs = nbytes / (kern_us * 1e-6) / 1e9
+        traffic = load_traffic().get(f"decode@{c['key']}")
         out[c["key"]] = {"workload": c["name"], "us_per_call": round(call_us, 2),
+                         "traffic": traffic,
                          "decode_kernel_us": round(kern_us, 2), "bytes": nbytes,
                          "kernel_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4),
                          "call_gbs": round(nbytes / (call_us * 1e-6) / 1e9, 1),
