@@ -132,6 +132,9 @@ struct ScoreCfg {
   // P tiles leave through a shared-memory staging slot and one bulk store
   // (a warp's direct 16-B row-chunk stores would touch 32 lines each).
   static constexpr bool kStageP = kTS && (MODE == kScoreP || MODE == kScoreFwd);
+  // dS pass: each thread overwrites the P chunks it read from the shared P slot
+  // with its dS chunks; the slot then leaves as one bulk store.
+  static constexpr bool kStageDs = kTS && MODE == kScoreDs;
 };
 
 struct ScoreMisc {
@@ -206,7 +209,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     }
     for (int s2 = 0; s2 < 4; ++s2) {
       mbar_init(&misc->p_full[s2], 1);
-      mbar_init(&misc->p_empty[s2], kScoreMathThreads);
+      mbar_init(&misc->p_empty[s2], Cfg::kStageDs ? 1 : kScoreMathThreads);
     }
     mbar_init(&misc->a_ready, kScoreMathThreads);
     mbar_init(&misc->drain, 1);
@@ -504,7 +507,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
         // keep the staging barrier count identical across warps
-        if (Cfg::kStageP) asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
+        if (Cfg::kStageP || Cfg::kStageDs)
+          asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
         continue;
       }
       tc_fence_after();
@@ -588,6 +592,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           float dv[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) dv[i] = pv[i] * (__uint_as_float(dr[i]) - delta_r);
+          uint8_t* ddst = Cfg::kStageDs ? const_cast<uint8_t*>(psm) : dtile;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 w;
@@ -595,13 +600,20 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             w.y = pack_bf16x2(dv[u * 8 + 2], dv[u * 8 + 3]);
             w.z = pack_bf16x2(dv[u * 8 + 4], dv[u * 8 + 5]);
             w.w = pack_bf16x2(dv[u * 8 + 6], dv[u * 8 + 7]);
-            *reinterpret_cast<uint4*>(dtile + tile_chunk_offset(r, c * 4 + u)) = w;
+            *reinterpret_cast<uint4*>(ddst + tile_chunk_offset(r, c * 4 + u)) = w;
           }
         }
       }
-      if (Cfg::kTS && MODE == kScoreDs) {
+      if (Cfg::kStageDs) {
+        // every math thread wrote its dS chunks over its P chunks: the slot
+        // goes to HBM as one bulk store, then back to the producer
         fence_proxy_async_smem();
-        mbar_arrive(&misc->p_empty[j % Cfg::kPStages]);
+        asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
+        if (tid == 0) {
+          bulk_store(dtile, psm, kTileBytes);
+          bulk_store_wait_read();
+          mbar_arrive(&misc->p_empty[j % Cfg::kPStages]);
+        }
       }
       if (Cfg::kStageP) {
         // every math thread wrote its chunks: one bulk store moves the tile
@@ -615,7 +627,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       }
     }
     // the tiles' bulk stores are complete before the kernel can finish
-    if (Cfg::kStageP && tid == 0) bulk_store_wait_all();
+    if ((Cfg::kStageP || Cfg::kStageDs) && tid == 0) bulk_store_wait_all();
   }
 
   tc_fence_before();
