@@ -2,7 +2,8 @@
 
 Drop-in for the operator surface of the reference ``gemma4_fa4`` package:
 the fixed-BSHD and packed-THD local-d256 / global-d512 adapters, the exact
-mask builders and the geometry contract.  Compute runs in
+mask builders and the geometry contract, and a Transformers attention backend
+(``register_gemma4_fa4_b200``).  Compute runs in
 ``libgemma4_b200.so`` (hand-written tcgen05/TMA kernels); there is no CPU or
 library fallback on the attention path.
 """
@@ -25,6 +26,15 @@ from .model_spec import (
     AttentionLayerSpec,
     Gemma4ModelSpec,
 )
+from .transformers_backend import (
+    BACKEND_NAME,
+    Gemma4DispatchResult,
+    Gemma4MaskPlan,
+    gemma4_fa4_b200_attention_forward,
+    gemma4_fa4_b200_mask,
+    gemma4_fa4_b200_prepared,
+    register_gemma4_fa4_b200,
+)
 
 __all__ = [
     "AttentionLayerSpec",
@@ -44,4 +54,11 @@ __all__ = [
     "UnsupportedH100Path",
     "gemma4_attention_mask",
     "additive_mask",
+    "BACKEND_NAME",
+    "Gemma4DispatchResult",
+    "Gemma4MaskPlan",
+    "gemma4_fa4_b200_attention_forward",
+    "gemma4_fa4_b200_mask",
+    "gemma4_fa4_b200_prepared",
+    "register_gemma4_fa4_b200",
 ]
