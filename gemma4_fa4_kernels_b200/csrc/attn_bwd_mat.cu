@@ -148,6 +148,7 @@ struct ScoreMisc {
   uint64_t p_empty[4];
   uint64_t drain;
   uint64_t stg_free;      // staging slot read by the previous tile's bulk store
+  uint64_t stg_ready[2];  // every math thread wrote tile j's chunks (slot parity j & 1)
   uint32_t tmem_base;
   int abort;
 };
@@ -159,9 +160,10 @@ constexpr int kScoreMathWarps = 16;
 constexpr int kScoreGroups = kScoreMathWarps / 4;     // column groups per row
 constexpr int kChunksPerWarp = 4 / kScoreGroups;
 constexpr int kScoreMathThreads = kScoreMathWarps * 32;
-constexpr int kScoreThreads = kScoreMathThreads + 64;  // + producer + MMA warps
+constexpr int kScoreThreads = kScoreMathThreads + 96;  // + producer, MMA and store warps
 constexpr int kProducerWarp = kScoreMathWarps;
 constexpr int kMmaWarp = kScoreMathWarps + 1;
+constexpr int kStoreWarp = kScoreMathWarps + 2;
 
 template <int D, int MODE>
 __global__ void __launch_bounds__(kScoreThreads, 1)
@@ -214,6 +216,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     mbar_init(&misc->a_ready, kScoreMathThreads);
     mbar_init(&misc->drain, 1);
     mbar_init(&misc->stg_free, 1);
+    mbar_init(&misc->stg_ready[0], kScoreMathThreads);
+    mbar_init(&misc->stg_ready[1], kScoreMathThreads);
     misc->abort = 0;
     fence_mbar_init();
   }
@@ -287,6 +291,29 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
                         (2 * cc + h) * 64, kv_head, krow, si.b_coord);
         }
       }
+    }
+    __syncwarp();
+  } else if (warp == kStoreWarp) {
+    if (lane == 0 && work > 0 && (Cfg::kStageP || Cfg::kStageDs)) {
+      // Store warp: once every math thread has written a tile into shared
+      // memory, move it to HBM with one bulk store and hand the slot back
+      // (the staging slot, or the dS pass's P slot to the producer).  The math
+      // warps never wait on a store, and the producer's waits never stall it.
+      bool ok = true;
+      for (int j = 0; j < work && ok; ++j) {
+        if (!(ok = mbar_wait(&misc->stg_ready[j & 1], (j >> 1) & 1, ab, kDevTimeoutPeer))) break;
+        if (Cfg::kStageDs) {
+          bulk_store(scratch_tile(p.ds_tiles, p, head, t_off, j),
+                     pring + (j % Cfg::kPStages) * 32768, kTileBytes);
+          bulk_store_wait_read();
+          mbar_arrive(&misc->p_empty[j % Cfg::kPStages]);
+        } else {
+          bulk_store(scratch_tile(p.p_tiles, p, head, t_off, j), stg, kTileBytes);
+          bulk_store_wait_read();
+          mbar_arrive(&misc->stg_free);
+        }
+      }
+      bulk_store_wait_all();  // the tiles are written before the kernel can finish
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
@@ -467,21 +494,15 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           w.w = pack_bf16x2(pe[6], pe[7]);
           *reinterpret_cast<uint4*>(stg + tile_chunk_offset(r, c_begin * 4 + u)) = w;
         }
-        // every math thread wrote its chunks: one bulk store moves the tile
+        // this thread's chunks are written; the store lane moves the tile
         fence_proxy_async_smem();
-        asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
-        if (tid == 0 && ok) {
-          bulk_store(ptile, stg, kTileBytes);
-          bulk_store_wait_read();
-          mbar_arrive(&misc->stg_free);
-        }
+        mbar_arrive(&misc->stg_ready[j & 1]);
         l_half = l_half * alpha + rowsum;
         if (grp == 0) {
           p.fwd_alpha[(tile_base + j) * 128 + r] = alpha;
           if (j > 0 && alpha != 1.f && row_valid) atomicOr(&p.fwd_flags[tile_base + j], 1);
         }
       }
-      if (tid == 0) bulk_store_wait_all();  // the P tiles are written before the kernel ends
       lsum[grp * 128 + r] = l_half;
       asm volatile("bar.sync 2, %0;" ::"n"(kScoreMathThreads) : "memory");
       if (grp == 0 && row_valid) {
@@ -505,12 +526,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       if (Cfg::kStageP && j > 0 && ok)
         ok = mbar_wait(&misc->stg_free, (j - 1) & 1, ab, kDevTimeoutPeer);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok) {
-        // keep the staging barrier count identical across warps
-        if (Cfg::kStageP || Cfg::kStageDs)
-          asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
-        continue;
-      }
+      if (!ok) continue;
       tc_fence_after();
       const uint8_t* psm = pring + (j % Cfg::kPStages) * 32768;
       uint8_t* ptile = Cfg::kS || MODE == kScoreDs ? scratch_tile(p.p_tiles, p, head, t_off, j) : nullptr;
@@ -604,30 +620,13 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           }
         }
       }
-      if (Cfg::kStageDs) {
-        // every math thread wrote its dS chunks over its P chunks: the slot
-        // goes to HBM as one bulk store, then back to the producer
+      if (Cfg::kStageP || Cfg::kStageDs) {
+        // this thread's chunks are written (dS over its P chunks in the dS
+        // pass); the store lane moves the tile and frees the slot
         fence_proxy_async_smem();
-        asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
-        if (tid == 0) {
-          bulk_store(dtile, psm, kTileBytes);
-          bulk_store_wait_read();
-          mbar_arrive(&misc->p_empty[j % Cfg::kPStages]);
-        }
-      }
-      if (Cfg::kStageP) {
-        // every math thread wrote its chunks: one bulk store moves the tile
-        fence_proxy_async_smem();
-        asm volatile("bar.sync 3, %0;" ::"n"(kScoreMathThreads) : "memory");
-        if (tid == 0) {
-          bulk_store(ptile, stg, kTileBytes);
-          bulk_store_wait_read();
-          mbar_arrive(&misc->stg_free);
-        }
+        mbar_arrive(&misc->stg_ready[j & 1]);
       }
     }
-    // the tiles' bulk stores are complete before the kernel can finish
-    if ((Cfg::kStageP || Cfg::kStageDs) && tid == 0) bulk_store_wait_all();
   }
 
   tc_fence_before();
