@@ -122,11 +122,12 @@ struct ScoreCfg {
   static constexpr bool kTS = D == 512 && MODE != kScorePdS;
   // TS variant: once the resident operand sits in TMEM its 128 KB of shared
   // memory (four 32 KB slots) extends the operand ring (more bytes in flight
-  // per SM): the P pass gets 3 + 3 K stages and one slot that stages each P
-  // tile for a single 32 KB bulk store; the forward pass 3 + 2 K stages, the
-  // staging slot and a slot for its row-statistics exchange; the dS pass
+  // per SM): the P pass gets 3 + 2 K stages and two slots that stage the P
+  // tiles for their 32 KB bulk stores (double-buffered, so a tile's store
+  // overlaps the next tile's math); the forward pass 3 + 1 K stages, the two
+  // staging slots and a slot for its row-statistics exchange; the dS pass
   // 3 + 2 V stages and 2 P stages.
-  static constexpr int kExtraStages = kTS ? (MODE == kScoreP ? 3 : 2) : 0;
+  static constexpr int kExtraStages = kTS ? (MODE == kScoreFwd ? 1 : 2) : 0;
   static constexpr int kRingStages = kStages + kExtraStages;
   static constexpr int kPStages = 2;
   // P tiles leave through a shared-memory staging slot and one bulk store
@@ -147,7 +148,7 @@ struct ScoreMisc {
   uint64_t p_full[4];     // P tiles in shared memory (dS pass, TS variant)
   uint64_t p_empty[4];
   uint64_t drain;
-  uint64_t stg_free;      // staging slot read by the previous tile's bulk store
+  uint64_t stg_free[2];   // staging slot j & 1 read by tile j's bulk store
   uint64_t stg_ready[2];  // every math thread wrote tile j's chunks (slot parity j & 1)
   uint32_t tmem_base;
   int abort;
@@ -215,7 +216,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     }
     mbar_init(&misc->a_ready, kScoreMathThreads);
     mbar_init(&misc->drain, 1);
-    mbar_init(&misc->stg_free, 1);
+    mbar_init(&misc->stg_free[0], 1);
+    mbar_init(&misc->stg_free[1], 1);
     mbar_init(&misc->stg_ready[0], kScoreMathThreads);
     mbar_init(&misc->stg_ready[1], kScoreMathThreads);
     misc->abort = 0;
@@ -245,7 +247,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   // TS dS pass: P ring after the extra V stages in the resident area; P and
   // forward passes: the staging slot there
   uint8_t* pring = res_area + Cfg::kExtraStages * 32768;
-  uint8_t* stg = res_area + Cfg::kExtraStages * 32768;
+  auto stg = [&](int j) { return res_area + (Cfg::kExtraStages + (j & 1)) * 32768; };
 
   if (warp == kProducerWarp) {
     if (lane == 0 && work > 0) {
@@ -308,9 +310,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           bulk_store_wait_read();
           mbar_arrive(&misc->p_empty[j % Cfg::kPStages]);
         } else {
-          bulk_store(scratch_tile(p.p_tiles, p, head, t_off, j), stg, kTileBytes);
+          bulk_store(scratch_tile(p.p_tiles, p, head, t_off, j), stg(j), kTileBytes);
           bulk_store_wait_read();
-          mbar_arrive(&misc->stg_free);
+          mbar_arrive(&misc->stg_free[j & 1]);
         }
       }
       bulk_store_wait_all();  // the tiles are written before the kernel can finish
@@ -411,7 +413,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       // halves take identical rescale decisions from identical inputs.
       // [2 parity][group][128] in the resident area past the extra stages (free
       // once Q is in TMEM; every math thread passed that point before use)
-      float* pmax = reinterpret_cast<float*>(res_area + (Cfg::kExtraStages + 1) * 32768);
+      float* pmax = reinterpret_cast<float*>(res_area + (Cfg::kExtraStages + 2) * 32768);
       float* lsum = pmax + 2 * kScoreGroups * 128;      // [group][128]
       const int64_t tile_base = static_cast<int64_t>(head) * p.head_cap_tiles + t_off;
       for (int j = tid; j < work; j += kScoreMathThreads) p.fwd_flags[tile_base + j] = 0;
@@ -474,9 +476,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         const float m_sub = m_run == -INFINITY ? 0.f : m_run;
         float rowsum = 0.f;
         uint8_t* ptile = scratch_tile(p.p_tiles, p, head, t_off, j);
-        // the staging slot is free once the previous tile's bulk store read it
-        if (j > 0) {
-          if (ok) ok = mbar_wait(&misc->stg_free, (j - 1) & 1, ab, kDevTimeoutPeer);
+        // staging slot j & 1 is free once tile j-2's bulk store has read it
+        if (j > 1) {
+          if (ok) ok = mbar_wait(&misc->stg_free[j & 1], ((j >> 1) & 1) ^ 1, ab, kDevTimeoutPeer);
           ok = __all_sync(0xffffffffu, ok);
         }
 #pragma unroll
@@ -492,7 +494,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           w.y = pack_bf16x2(pe[2], pe[3]);
           w.z = pack_bf16x2(pe[4], pe[5]);
           w.w = pack_bf16x2(pe[6], pe[7]);
-          *reinterpret_cast<uint4*>(stg + tile_chunk_offset(r, c_begin * 4 + u)) = w;
+          *reinterpret_cast<uint4*>(stg(j) + tile_chunk_offset(r, c_begin * 4 + u)) = w;
         }
         // this thread's chunks are written; the store lane moves the tile
         fence_proxy_async_smem();
@@ -523,8 +525,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       if (ok && Cfg::kTS && MODE == kScoreDs)
         ok = mbar_wait(&misc->p_full[j % Cfg::kPStages], (j / Cfg::kPStages) & 1, ab,
                        kDevTimeoutTma);
-      if (Cfg::kStageP && j > 0 && ok)
-        ok = mbar_wait(&misc->stg_free, (j - 1) & 1, ab, kDevTimeoutPeer);
+      if (Cfg::kStageP && j > 1 && ok)
+        ok = mbar_wait(&misc->stg_free[j & 1], ((j >> 1) & 1) ^ 1, ab, kDevTimeoutPeer);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) continue;
       tc_fence_after();
@@ -591,7 +593,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           }
         }
         if (MODE != kScoreDs) {
-          uint8_t* pdst = Cfg::kStageP ? stg : ptile;
+          uint8_t* pdst = Cfg::kStageP ? stg(j) : ptile;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 w;
