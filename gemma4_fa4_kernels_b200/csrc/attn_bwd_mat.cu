@@ -146,7 +146,6 @@ struct ScoreMisc {
   uint64_t s_full[2];
   uint64_t buf_free[2];
   uint64_t p_full[4];     // P tiles in shared memory (dS pass, TS variant)
-  uint64_t p_empty[4];
   uint64_t drain;
   uint64_t stg_free[2];   // staging slot j & 1 read by tile j's bulk store
   uint64_t stg_ready[2];  // every math thread wrote tile j's chunks (slot parity j & 1)
@@ -210,10 +209,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       mbar_init(&misc->s_full[b], 1);
       mbar_init(&misc->buf_free[b], kScoreMathThreads);
     }
-    for (int s2 = 0; s2 < 4; ++s2) {
-      mbar_init(&misc->p_full[s2], 1);
-      mbar_init(&misc->p_empty[s2], Cfg::kStageDs ? 1 : kScoreMathThreads);
-    }
+    for (int s2 = 0; s2 < 4; ++s2) mbar_init(&misc->p_full[s2], 1);
     mbar_init(&misc->a_ready, kScoreMathThreads);
     mbar_init(&misc->drain, 1);
     mbar_init(&misc->stg_free[0], 1);
@@ -262,21 +258,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       bool res_free = !Cfg::kTS;
-      if (Cfg::kTS && MODE == kScoreDs) {  // the P ring reuses the resident area
-        ok = mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer);
-        res_free = true;
-      }
       for (int j = 0; j < work && ok; ++j) {
         const int krow = si.k_base + (kt_lo + j) * kTileN;
-        if (Cfg::kTS && MODE == kScoreDs) {
-          const int sp = j % Cfg::kPStages;
-          if (!(ok = mbar_wait(&misc->p_empty[sp], ((j / Cfg::kPStages) & 1) ^ 1, ab,
-                               kDevTimeoutPeer)))
-            break;
-          mbar_expect_tx(&misc->p_full[sp], 32768);
-          bulk_load(pring + sp * 32768, scratch_tile(p.p_tiles, p, head, t_off, j), 32768,
-                    &misc->p_full[sp]);
-        }
         for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
           const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
@@ -302,13 +285,27 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       // (the staging slot, or the dS pass's P slot to the producer).  The math
       // warps never wait on a store, and the producer's waits never stall it.
       bool ok = true;
+      auto load_p = [&](int j) {  // dS pass: P tile j into P slot j % kPStages
+        const int sp = j % Cfg::kPStages;
+        mbar_expect_tx(&misc->p_full[sp], kTileBytes);
+        bulk_load(pring + sp * 32768, scratch_tile(p.p_tiles, p, head, t_off, j), kTileBytes,
+                  &misc->p_full[sp]);
+      };
+      if (Cfg::kStageDs) {
+        // the P slots sit in the resident area, free once dO is in TMEM
+        ok = mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer);
+        for (int j = 0; j < Cfg::kPStages && j < work && ok; ++j) load_p(j);
+      }
       for (int j = 0; j < work && ok; ++j) {
         if (!(ok = mbar_wait(&misc->stg_ready[j & 1], (j >> 1) & 1, ab, kDevTimeoutPeer))) break;
         if (Cfg::kStageDs) {
+          // the slot that held P(j) now holds dS(j): store it, then refill the
+          // slot with the P tile two steps ahead (the producer never waits on
+          // a P slot, so the V stream runs ahead independently)
           bulk_store(scratch_tile(p.ds_tiles, p, head, t_off, j),
                      pring + (j % Cfg::kPStages) * 32768, kTileBytes);
           bulk_store_wait_read();
-          mbar_arrive(&misc->p_empty[j % Cfg::kPStages]);
+          if (j + Cfg::kPStages < work) load_p(j + Cfg::kPStages);
         } else {
           bulk_store(scratch_tile(p.p_tiles, p, head, t_off, j), stg(j), kTileBytes);
           bulk_store_wait_read();
