@@ -676,7 +676,8 @@ struct GemmStep {
 
 template <int D, int WHICH>
 __global__ void __launch_bounds__(192, 1)
-    bwd_tile_gemm_kernel(const __grid_constant__ CUtensorMap tmB, const MatParams p) {
+    bwd_tile_gemm_kernel(const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmOut, const MatParams p) {
   using Cfg = GemmCfg<D, WHICH>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if ((smem_addr(smem) & 1023u) != 0) {
@@ -771,11 +772,21 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = misc->tmem_base;
   const CtaAbort ab{&misc->abort, p.err};
 
+  // k-step count (two per scratch tile).  Whether a query tile reaches this
+  // key tile does not depend on the GQA head, so the KV-major count scans the
+  // query tiles once instead of once per head.
   int n_steps = 0;
-  for_each_tile([&](const uint8_t*, int, int) {
-    n_steps += 2;
-    return true;
-  });
+  if (Cfg::kQMajor) {
+    const int4 rg = p.ranges[qg];
+    n_steps = rg.z + rg.y > p.head_cap_tiles ? 0 : 2 * rg.y;
+  } else {
+    int n_qt = 0;
+    for (int qt = 0; qt < n_qt_seq; ++qt) {
+      const int4 rg = p.ranges[first_qg + qt];
+      n_qt += (tile >= rg.x && tile < rg.x + rg.y && rg.z + rg.y <= p.head_cap_tiles) ? 1 : 0;
+    }
+    n_steps = 2 * G * n_qt;
+  }
 
   if (warp == 4) {
     if (lane == 0 && n_steps > 0) {
@@ -923,29 +934,68 @@ __global__ void __launch_bounds__(192, 1)
       dst = p.dk + static_cast<int64_t>(si.b_coord) * p.dk_stride[0] +
             static_cast<int64_t>(si.k_base + row) * p.dk_stride[1] + static_cast<int64_t>(head) * p.dk_stride[2];
     dst += half * 256;
+    // A full 128-row tile leaves through shared memory: each thread writes its
+    // row in the 128-B swizzled layout into the operand ring (idle once every
+    // MMA has completed) and one thread issues a TMA store per 64-column block,
+    // instead of 16-B row-chunk stores that touch 32 lines per warp store.  A
+    // partial tile of a packed segment would spill into the next segment, so
+    // partial tiles keep the direct stores.
+    const int seq_len = Cfg::kQMajor ? si.len_q : si.len_k;
+    const bool via_tma = have && tile * 128 + 128 <= seq_len;
+    if (via_tma) {
 #pragma unroll 1
-    for (int c = 0; c < Cfg::kNB / 32; ++c) {
-      uint32_t r[32];
-      if (have) {
+      for (int c = 0; c < Cfg::kNB / 32; ++c) {
+        uint32_t r[32];
         tmem_ld32(lane_base + c * 32, r);
         tmem_wait_ld();
         reg_fence32(r);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = 0u;
-      }
-      if (row_valid) {
-        uint4* out = reinterpret_cast<uint4*>(dst + c * 32);
+        uint8_t* rowp = smem + (c >> 1) * 16384 + tid * 128;
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          out[i] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * i + 0]) * out_scale,
-                                          __uint_as_float(r[8 * i + 1]) * out_scale),
-                              pack_bf16x2(__uint_as_float(r[8 * i + 2]) * out_scale,
-                                          __uint_as_float(r[8 * i + 3]) * out_scale),
-                              pack_bf16x2(__uint_as_float(r[8 * i + 4]) * out_scale,
-                                          __uint_as_float(r[8 * i + 5]) * out_scale),
-                              pack_bf16x2(__uint_as_float(r[8 * i + 6]) * out_scale,
-                                          __uint_as_float(r[8 * i + 7]) * out_scale));
+          *reinterpret_cast<uint4*>(rowp + ((((c & 1) * 4 + i) ^ (tid & 7)) << 4)) =
+              make_uint4(pack_bf16x2(__uint_as_float(r[8 * i + 0]) * out_scale,
+                                     __uint_as_float(r[8 * i + 1]) * out_scale),
+                         pack_bf16x2(__uint_as_float(r[8 * i + 2]) * out_scale,
+                                     __uint_as_float(r[8 * i + 3]) * out_scale),
+                         pack_bf16x2(__uint_as_float(r[8 * i + 4]) * out_scale,
+                                     __uint_as_float(r[8 * i + 5]) * out_scale),
+                         pack_bf16x2(__uint_as_float(r[8 * i + 6]) * out_scale,
+                                     __uint_as_float(r[8 * i + 7]) * out_scale));
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (tid == 0) {
+        const int tok0 = (Cfg::kQMajor ? si.q_base : si.k_base) + tile * 128;
+        for (int cb = 0; cb < Cfg::kNB / 64; ++cb)
+          tma_store_4d(&tmOut, smem + cb * 16384, half * 256 + cb * 64, head, tok0, si.b_coord);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        bulk_store_wait_all();
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < Cfg::kNB / 32; ++c) {
+        uint32_t r[32];
+        if (have) {
+          tmem_ld32(lane_base + c * 32, r);
+          tmem_wait_ld();
+          reg_fence32(r);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        if (row_valid) {
+          uint4* out = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            out[i] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * i + 0]) * out_scale,
+                                            __uint_as_float(r[8 * i + 1]) * out_scale),
+                                pack_bf16x2(__uint_as_float(r[8 * i + 2]) * out_scale,
+                                            __uint_as_float(r[8 * i + 3]) * out_scale),
+                                pack_bf16x2(__uint_as_float(r[8 * i + 4]) * out_scale,
+                                            __uint_as_float(r[8 * i + 5]) * out_scale),
+                                pack_bf16x2(__uint_as_float(r[8 * i + 6]) * out_scale,
+                                            __uint_as_float(r[8 * i + 7]) * out_scale));
+        }
       }
     }
   }
@@ -990,8 +1040,8 @@ int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& 
 }
 
 template <int D, int WHICH>
-static int launch_gemm_impl(const CUtensorMap& tb, const MatParams& p, int grid_x, int grid_y,
-                            cudaStream_t stream) {
+static int launch_gemm_impl(const CUtensorMap& tb, const CUtensorMap& tout, const MatParams& p,
+                            int grid_x, int grid_y, cudaStream_t stream) {
   using Cfg = GemmCfg<D, WHICH>;
   if (!Cfg::kQMajor) {  // KV-major: (key tile, KV head, half) all along x
     grid_x *= grid_y * Cfg::kHalves;
@@ -1002,21 +1052,21 @@ static int launch_gemm_impl(const CUtensorMap& tb, const MatParams& p, int grid_
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
   dim3 grid = Cfg::kQMajor ? dim3(grid_y, grid_x) : dim3(grid_x, grid_y);
-  bwd_tile_gemm_kernel<D, WHICH><<<grid, 192, smem, stream>>>(tb, p);
+  bwd_tile_gemm_kernel<D, WHICH><<<grid, 192, smem, stream>>>(tb, tout, p);
   return static_cast<int>(cudaGetLastError());
 }
 
-int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const MatParams& p, int grid_x,
-                         int grid_y, cudaStream_t stream) {
+int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const CUtensorMap& tout,
+                         const MatParams& p, int grid_x, int grid_y, cudaStream_t stream) {
   if (d == 256) {
-    if (which == kGemmDv) return launch_gemm_impl<256, kGemmDv>(tb, p, grid_x, grid_y, stream);
-    if (which == kGemmDk) return launch_gemm_impl<256, kGemmDk>(tb, p, grid_x, grid_y, stream);
-    return launch_gemm_impl<256, kGemmDq>(tb, p, grid_x, grid_y, stream);
+    if (which == kGemmDv) return launch_gemm_impl<256, kGemmDv>(tb, tout, p, grid_x, grid_y, stream);
+    if (which == kGemmDk) return launch_gemm_impl<256, kGemmDk>(tb, tout, p, grid_x, grid_y, stream);
+    return launch_gemm_impl<256, kGemmDq>(tb, tout, p, grid_x, grid_y, stream);
   }
-  if (which == kGemmDv) return launch_gemm_impl<512, kGemmDv>(tb, p, grid_x, grid_y, stream);
-  if (which == kGemmDk) return launch_gemm_impl<512, kGemmDk>(tb, p, grid_x, grid_y, stream);
-  if (which == kGemmO) return launch_gemm_impl<512, kGemmO>(tb, p, grid_x, grid_y, stream);
-  return launch_gemm_impl<512, kGemmDq>(tb, p, grid_x, grid_y, stream);
+  if (which == kGemmDv) return launch_gemm_impl<512, kGemmDv>(tb, tout, p, grid_x, grid_y, stream);
+  if (which == kGemmDk) return launch_gemm_impl<512, kGemmDk>(tb, tout, p, grid_x, grid_y, stream);
+  if (which == kGemmO) return launch_gemm_impl<512, kGemmO>(tb, tout, p, grid_x, grid_y, stream);
+  return launch_gemm_impl<512, kGemmDq>(tb, tout, p, grid_x, grid_y, stream);
 }
 
 }  // namespace g4

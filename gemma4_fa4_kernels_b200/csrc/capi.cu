@@ -611,9 +611,13 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
       e = g4::launch_bwd_score(D, 2, tq, tk, tv, tq, m, w.n_qt_total, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward score launch");
     }
+    CUtensorMap to128;  // O, written by TMA stores in 128-row tiles
+    if ((rc = make_map(&to128, a->o, a->head_dim_v, a->num_q_heads, a->seqlen_q, bq,
+                       a->o_stride[2], a->o_stride[1], a->o_stride[0], 128)))
+      return rc;
     {
       LaunchScope ls(kKFwdPv, st);
-      e = g4::launch_bwd_tile_gemm(D, 3, tv64, m, w.n_qt_total, a->num_q_heads, st);
+      e = g4::launch_bwd_tile_gemm(D, 3, tv64, to128, m, w.n_qt_total, a->num_q_heads, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward PV launch");
     }
     return G4_OK;
@@ -741,6 +745,16 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     if ((rc = make_map(&tdo64, a->dout, a->head_dim_v, a->num_q_heads, a->seqlen_q, bq,
                        a->do_stride[2], a->do_stride[1], a->do_stride[0], 64)))
       return rc;
+    CUtensorMap tdq128, tdk128, tdv128;  // gradients, written by TMA stores in 128-row tiles
+    if ((rc = make_map(&tdq128, a->dq, D, a->num_q_heads, a->seqlen_q, bq, a->dq_stride[2],
+                       a->dq_stride[1], a->dq_stride[0], 128)))
+      return rc;
+    if ((rc = make_map(&tdk128, a->dk, D, a->num_kv_heads, a->seqlen_k, bq, a->dk_stride[2],
+                       a->dk_stride[1], a->dk_stride[0], 128)))
+      return rc;
+    if ((rc = make_map(&tdv128, a->dv, a->head_dim_v, a->num_kv_heads, a->seqlen_k, bq,
+                       a->dv_stride[2], a->dv_stride[1], a->dv_stride[0], 128)))
+      return rc;
     {
       LaunchScope ls(kKPlan, st);
       e = g4::launch_plan_qtile_ranges(m, st);
@@ -753,17 +767,17 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     }
     {
       LaunchScope ls(kKGemmDv, st);
-      e = g4::launch_bwd_tile_gemm(D, 0, tdo64, m, gk, a->num_kv_heads, st);
+      e = g4::launch_bwd_tile_gemm(D, 0, tdo64, tdv128, m, gk, a->num_kv_heads, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV launch");
     }
     {
       LaunchScope ls(kKGemmDk, st);
-      e = g4::launch_bwd_tile_gemm(D, 1, tq64, m, gk, a->num_kv_heads, st);
+      e = g4::launch_bwd_tile_gemm(D, 1, tq64, tdk128, m, gk, a->num_kv_heads, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK launch");
     }
     {
       LaunchScope ls(kKGemmDq, st);
-      e = g4::launch_bwd_tile_gemm(D, 2, tk64, m, w.n_qt_total, a->num_q_heads, st);
+      e = g4::launch_bwd_tile_gemm(D, 2, tk64, tdq128, m, w.n_qt_total, a->num_q_heads, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "dQ launch");
     }
     return G4_OK;

@@ -124,9 +124,9 @@ int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& 
                      const CUtensorMap& tv, const CUtensorMap& tdo, const MatParams& p, int grid_x,
                      cudaStream_t stream);
 // which: 0 = dV (B = dO), 1 = dK (B = Q), 2 = dQ (B = K), 3 = forward O = P V
-// (B = V); maps use 64-row boxes.
-int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const MatParams& p, int grid_x,
-                         int grid_y, cudaStream_t stream);
+// (B = V); tb uses 64-row boxes, tout (the output: dV, dK, dQ or O) 128-row boxes.
+int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const CUtensorMap& tout,
+                         const MatParams& p, int grid_x, int grid_y, cudaStream_t stream);
 
 template <int DQK>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
