@@ -148,3 +148,29 @@ def test_recompute_and_materialized_backward_agree_with_oracle(shape):
         torch.cuda.synchronize()
         for name, got, ref in (("dq", dq, rq), ("dk", dk, rk), ("dv", dv, rv)):
             assert_close_to_oracle(f"{algo} {name}", bshd_to_bhsd_np(got), ref)
+
+
+@pytest.mark.parametrize("d,hq,hkv,window", [(512, 8, 1, 0), (256, 4, 2, 1024)])
+def test_forward_backward_capture_into_a_cuda_graph(d, hq, hkv, window):
+    # The backward forks its preprocessing onto a second stream and joins it
+    # with events; the whole step must capture into a graph and replay with
+    # results bit-identical to eager calls.
+    s = 640
+    q, k, v, do = make_inputs((1, s, hq, d), (1, s, hkv, d), (1, s, hkv, d), seed=123)
+    o_ref, l_ref = ops.attn_fwd(q, k, v, window=window)
+    dq_ref, dk_ref, dv_ref = ops.attn_bwd(q, k, v, o_ref, l_ref, do, window=window)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):  # warm-up outside capture (allocator, attributes)
+        o, l_ = ops.attn_fwd(q, k, v, window=window)
+        ops.attn_bwd(q, k, v, o, l_, do, window=window)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        o_g, l_g = ops.attn_fwd(q, k, v, window=window)
+        dq_g, dk_g, dv_g = ops.attn_bwd(q, k, v, o_g, l_g, do, window=window)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(o_g, o_ref) and torch.equal(l_g, l_ref)
+    assert torch.equal(dq_g, dq_ref) and torch.equal(dk_g, dk_ref) and torch.equal(dv_g, dv_ref)
