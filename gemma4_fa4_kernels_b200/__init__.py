@@ -3,7 +3,8 @@
 Drop-in for the operator surface of the reference ``gemma4_fa4`` package:
 the fixed-BSHD and packed-THD local-d256 / global-d512 adapters, the exact
 mask builders and the geometry contract, and a Transformers attention backend
-(``register_gemma4_fa4_b200``).  Compute runs in
+(``register_gemma4_fa4_b200``), and the fused Q/K/V preparation (RMS norm +
+rotary, with its adjoint).  Compute runs in
 ``libgemma4_b200.so`` (hand-written tcgen05/TMA kernels); there is no CPU or
 library fallback on the attention path.
 """
@@ -25,6 +26,12 @@ from .model_spec import (
     SLIDING_ATTENTION,
     AttentionLayerSpec,
     Gemma4ModelSpec,
+)
+from .prep import (
+    prepare_global_kv_from_projection_source,
+    prepare_rotary_operand,
+    prepare_shared_kv,
+    prepare_value,
 )
 from .transformers_backend import (
     BACKEND_NAME,
@@ -61,4 +68,8 @@ __all__ = [
     "gemma4_fa4_b200_mask",
     "gemma4_fa4_b200_prepared",
     "register_gemma4_fa4_b200",
+    "prepare_global_kv_from_projection_source",
+    "prepare_rotary_operand",
+    "prepare_shared_kv",
+    "prepare_value",
 ]

@@ -38,6 +38,9 @@ EXPORTED_SYMBOLS = (
     "g4_attn_bwd_noalloc",
     "g4_read_device_error",
     "g4_build_mask",
+    "g4_prep_bwd_workspace_bytes",
+    "g4_prep_fwd",
+    "g4_prep_bwd",
     "g4_kernel_count",
     "g4_kernel_name",
     "g4_launch_count",
@@ -93,6 +96,38 @@ class G4AttnArgs(ctypes.Structure):
     ]
 
 
+class G4PrepArgs(ctypes.Structure):
+    """Mirror of ``g4_prep_args``."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("cos", ctypes.c_void_p),
+        ("sin", ctypes.c_void_p),
+        ("rot", ctypes.c_void_p),
+        ("plain", ctypes.c_void_p),
+        ("drot", ctypes.c_void_p),
+        ("dplain", ctypes.c_void_p),
+        ("dx", ctypes.c_void_p),
+        ("dweight", ctypes.c_void_p),
+        ("x_stride", ctypes.c_int64 * 3),
+        ("rot_stride", ctypes.c_int64 * 3),
+        ("plain_stride", ctypes.c_int64 * 3),
+        ("drot_stride", ctypes.c_int64 * 3),
+        ("dplain_stride", ctypes.c_int64 * 3),
+        ("dx_stride", ctypes.c_int64 * 3),
+        ("cos_stride", ctypes.c_int64 * 2),
+        ("batch", ctypes.c_int32),
+        ("seqlen", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("rotary_dim", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
@@ -132,6 +167,13 @@ def load() -> ctypes.CDLL:
                                       ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p]
         lib.g4_build_mask.restype = ctypes.c_int
+        PP = ctypes.POINTER(G4PrepArgs)
+        lib.g4_prep_bwd_workspace_bytes.argtypes = [PP]
+        lib.g4_prep_bwd_workspace_bytes.restype = ctypes.c_size_t
+        for name in ("g4_prep_fwd", "g4_prep_bwd"):
+            fn = getattr(lib, name)
+            fn.argtypes = [PP, ctypes.c_void_p]
+            fn.restype = ctypes.c_int
         lib.g4_kernel_count.restype = ctypes.c_int
         lib.g4_kernel_name.argtypes = [ctypes.c_int]
         lib.g4_kernel_name.restype = ctypes.c_char_p

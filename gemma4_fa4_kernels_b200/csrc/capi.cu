@@ -53,13 +53,17 @@ enum KernelId {
   kKFwdPv,
   kKDecode,
   kKDecodeCombine,
+  kKPrepFwd,
+  kKPrepBwd,
+  kKPrepDw,
   kKCount
 };
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
                                            "plan",     "mask",           "bwd_score",
                                            "bwd_gemm_dv", "bwd_gemm_dk", "bwd_gemm_dq",
                                            "fwd_score",   "fwd_pv",      "decode",
-                                           "decode_combine"};
+                                           "decode_combine", "prep_fwd",  "prep_bwd",
+                                           "prep_dw_reduce"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -813,6 +817,204 @@ int g4_attn_bwd_noalloc(const g4_attn_args* a, void* stream) {
   local.workspace = scratch;
   local.workspace_bytes = G4_NOALLOC_SCRATCH_BYTES;
   return g4_attn_bwd(&local, stream);
+}
+
+// ---------------------------------------------------------------------------------------
+// fused Q/K/V preparation
+// ---------------------------------------------------------------------------------------
+}  // extern "C"
+
+namespace {
+
+constexpr int kPrepMaxCtasPerSm = 8;  // 256-thread CTAs: the SM's 2048-thread limit
+
+// Rows with extent > 1 must not overlap: sorted by stride, each stride covers
+// the span of the dimensions inside it (innermost: the head_dim features).
+bool prep_nonoverlapping(const int64_t* st, const int64_t* ext, int64_t d) {
+  int64_t s[3], e[3];
+  int n = 0;
+  for (int i = 0; i < 3; ++i)
+    if (ext[i] > 1) {
+      s[n] = st[i];
+      e[n] = ext[i];
+      ++n;
+    }
+  for (int i = 1; i < n; ++i)
+    for (int j = i; j > 0 && s[j] < s[j - 1]; --j) {
+      std::swap(s[j], s[j - 1]);
+      std::swap(e[j], e[j - 1]);
+    }
+  int64_t span = d;
+  for (int i = 0; i < n; ++i) {
+    if (s[i] < span) return false;
+    span = s[i] * e[i];
+  }
+  return true;
+}
+
+int prep_check_tensor(const void* ptr, const int64_t* st, const g4_prep_args* a, const char* name,
+                      bool output) {
+  if (!aligned16(ptr)) return fail(G4_ERR_INVALID, "%s must be 16-byte aligned", name);
+  for (int i = 0; i < 3; ++i)
+    if (st[i] < 0 || (st[i] % 8) != 0)
+      return fail(G4_ERR_INVALID, "%s strides must be non-negative multiples of 8 elements", name);
+  if (output) {
+    const int64_t ext[3] = {a->batch, a->seqlen, a->num_heads};
+    if (!prep_nonoverlapping(st, ext, a->head_dim))
+      return fail(G4_ERR_INVALID, "%s rows overlap", name);
+  }
+  return G4_OK;
+}
+
+int prep_check(const g4_prep_args* a, bool backward) {
+  if (!a) return fail(G4_ERR_INVALID, "null argument block");
+  if (a->batch < 0 || a->seqlen < 0 || a->num_heads < 0)
+    return fail(G4_ERR_INVALID, "batch, seqlen and num_heads must be non-negative");
+  if (static_cast<int64_t>(a->batch) * a->seqlen * a->num_heads > INT32_MAX)
+    return fail(G4_ERR_UNSUPPORTED, "batch * seqlen * num_heads must be below 2^31 rows");
+  if (a->head_dim != 256 && a->head_dim != 512)
+    return fail(G4_ERR_UNSUPPORTED, "head_dim %d is not a Gemma-4 head dimension (256 or 512)",
+                a->head_dim);
+  if (a->rotary_dim < 0 || a->rotary_dim > a->head_dim || (a->rotary_dim % 2) != 0)
+    return fail(G4_ERR_INVALID, "rotary_dim must be an even integer in [0, head_dim]");
+  if (a->rotary_dim != 0 && (a->rotary_dim < 16 || (a->rotary_dim & (a->rotary_dim - 1)) != 0))
+    return fail(G4_ERR_UNSUPPORTED, "rotary_dim must be 0 or a power of two >= 16");
+  if (!(a->eps > 0.f) || a->eps > 1.f) return fail(G4_ERR_INVALID, "eps must be in (0, 1]");
+  if (!a->x) return fail(G4_ERR_INVALID, "x is required");
+  int rc = prep_check_tensor(a->x, a->x_stride, a, "x", false);
+  if (rc) return rc;
+  if (a->weight && !aligned16(a->weight)) return fail(G4_ERR_INVALID, "weight must be 16-byte aligned");
+  const bool uses_rot = backward ? a->drot != nullptr : a->rot != nullptr;
+  if (uses_rot && a->rotary_dim > 0) {
+    if (!a->cos || !a->sin) return fail(G4_ERR_INVALID, "cos and sin are required when rotary_dim > 0");
+    if (!aligned16(a->cos) || !aligned16(a->sin))
+      return fail(G4_ERR_INVALID, "cos and sin must be 16-byte aligned");
+    if (a->cos_stride[0] < 0 || a->cos_stride[1] < 0 || (a->cos_stride[0] % 8) != 0 ||
+        (a->cos_stride[1] % 8) != 0)
+      return fail(G4_ERR_INVALID, "cos/sin strides must be non-negative multiples of 8 elements");
+  }
+  if (!backward) {
+    if (!a->rot && !a->plain) return fail(G4_ERR_INVALID, "at least one of rot and plain is required");
+    if (a->rot && (rc = prep_check_tensor(a->rot, a->rot_stride, a, "rot", true))) return rc;
+    if (a->plain && (rc = prep_check_tensor(a->plain, a->plain_stride, a, "plain", true))) return rc;
+    if (a->rot && a->plain && a->rot == a->plain)
+      return fail(G4_ERR_INVALID, "rot and plain must be distinct");
+    return G4_OK;
+  }
+  if (!a->drot && !a->dplain) return fail(G4_ERR_INVALID, "at least one of drot and dplain is required");
+  if (!a->dx) return fail(G4_ERR_INVALID, "dx is required");
+  if (a->drot && (rc = prep_check_tensor(a->drot, a->drot_stride, a, "drot", false))) return rc;
+  if (a->dplain && (rc = prep_check_tensor(a->dplain, a->dplain_stride, a, "dplain", false))) return rc;
+  if ((rc = prep_check_tensor(a->dx, a->dx_stride, a, "dx", true))) return rc;
+  if (a->dweight && (!a->weight || !a->drot))
+    return fail(G4_ERR_INVALID, "dweight needs weight and drot");
+  return G4_OK;
+}
+
+size_t prep_workspace(const g4_prep_args* a) {
+  if (!a || !a->dweight) return 0;
+  const int64_t rows = static_cast<int64_t>(a->batch) * a->seqlen * a->num_heads;
+  const int64_t need = (rows + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * kPrepMaxCtasPerSm;
+  const int64_t grid = std::max<int64_t>(1, std::min(need, cap));
+  return static_cast<size_t>(grid) * a->head_dim * sizeof(float);
+}
+
+g4::PrepParams prep_params(const g4_prep_args* a) {
+  g4::PrepParams p{};
+  p.batch = a->batch;
+  p.seqlen = a->seqlen;
+  p.heads = a->num_heads;
+  p.head_dim = a->head_dim;
+  p.rotary_dim = a->rotary_dim;
+  p.rows = static_cast<uint32_t>(static_cast<int64_t>(a->batch) * a->seqlen * a->num_heads);
+  p.div_heads = g4::prep_fastdiv(static_cast<uint32_t>(std::max(a->num_heads, 1)));
+  p.div_seqlen = g4::prep_fastdiv(static_cast<uint32_t>(std::max(a->seqlen, 1)));
+  p.eps = a->eps;
+  p.x = static_cast<const __nv_bfloat16*>(a->x);
+  p.w = static_cast<const __nv_bfloat16*>(a->weight);
+  p.cos = static_cast<const __nv_bfloat16*>(a->cos);
+  p.sin = static_cast<const __nv_bfloat16*>(a->sin);
+  p.rot = static_cast<__nv_bfloat16*>(a->rot);
+  p.plain = static_cast<__nv_bfloat16*>(a->plain);
+  p.drot = static_cast<const __nv_bfloat16*>(a->drot);
+  p.dplain = static_cast<const __nv_bfloat16*>(a->dplain);
+  p.dx = static_cast<__nv_bfloat16*>(a->dx);
+  for (int i = 0; i < 3; ++i) {
+    p.x_stride[i] = a->x_stride[i];
+    p.rot_stride[i] = a->rot_stride[i];
+    p.plain_stride[i] = a->plain_stride[i];
+    p.drot_stride[i] = a->drot_stride[i];
+    p.dplain_stride[i] = a->dplain_stride[i];
+    p.dx_stride[i] = a->dx_stride[i];
+  }
+  p.cs_stride[0] = a->cos_stride[0];
+  p.cs_stride[1] = a->cos_stride[1];
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t g4_prep_bwd_workspace_bytes(const g4_prep_args* a) { return prep_workspace(a); }
+
+int g4_prep_fwd(const g4_prep_args* a, void* stream) {
+  g_last_error.clear();
+  int rc = prep_check(a, false);
+  if (rc) return rc;
+  const int64_t rows = static_cast<int64_t>(a->batch) * a->seqlen * a->num_heads;
+  if (rows == 0) return G4_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  g4::PrepParams p = prep_params(a);
+  if (!a->rot) p.rotary_dim = 0;
+  const int grid = g4::prep_grid(false, p, sm_count());
+  int e;
+  {
+    LaunchScope ls(kKPrepFwd, st);
+    e = g4::launch_prep_fwd(p, grid, st);
+  }
+  if (e) return cuda_fail(static_cast<cudaError_t>(e), "prep forward launch");
+  return G4_OK;
+}
+
+int g4_prep_bwd(const g4_prep_args* a, void* stream) {
+  g_last_error.clear();
+  int rc = prep_check(a, true);
+  if (rc) return rc;
+  const size_t need = prep_workspace(a);
+  if (need > 0 && (!a->workspace || a->workspace_bytes < need))
+    return fail(G4_ERR_WORKSPACE, "prep backward needs %zu workspace bytes, got %zu", need,
+                a->workspace ? a->workspace_bytes : (size_t)0);
+  if (a->workspace && !aligned16(a->workspace))
+    return fail(G4_ERR_INVALID, "workspace must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rows = static_cast<int64_t>(a->batch) * a->seqlen * a->num_heads;
+  if (rows == 0) {
+    if (a->dweight) {
+      cudaError_t ce = cudaMemsetAsync(a->dweight, 0, a->head_dim * sizeof(float), st);
+      if (ce != cudaSuccess) return cuda_fail(ce, "dweight clear");
+    }
+    return G4_OK;
+  }
+  g4::PrepParams p = prep_params(a);
+  if (!a->drot) p.rotary_dim = 0;
+  p.dw_part = a->dweight ? static_cast<float*>(a->workspace) : nullptr;
+  const int grid = g4::prep_grid(true, p, sm_count());
+  if (a->dweight && static_cast<size_t>(grid) * a->head_dim * sizeof(float) > need)
+    return fail(G4_ERR_WORKSPACE, "prep backward grid exceeds the planned workspace");
+  int e;
+  {
+    LaunchScope ls(kKPrepBwd, st);
+    e = g4::launch_prep_bwd(p, grid, st);
+  }
+  if (e) return cuda_fail(static_cast<cudaError_t>(e), "prep backward launch");
+  if (a->dweight) {
+    LaunchScope ls(kKPrepDw, st);
+    e = g4::launch_prep_dw_reduce(p.dw_part, grid, a->head_dim, a->dweight, st);
+    if (e) return cuda_fail(static_cast<cudaError_t>(e), "prep dweight reduction launch");
+  }
+  return G4_OK;
 }
 
 int g4_kernel_count(void) { return kKCount; }

@@ -117,6 +117,41 @@ int launch_decode(int d, const CUtensorMap& tk, const CUtensorMap& tv, const Dec
                   int num_kv_heads, cudaStream_t stream);
 int launch_decode_combine(int d, const DecodeParams& p, cudaStream_t stream);
 
+// Fused Q/K/V preparation (prep.cu): rows (b, s, h) of head_dim features,
+// strides in elements [batch, token, head]; cos/sin (batch, token, rotary_dim)
+// with strides [batch, token] (batch stride may be 0).
+struct FastDiv {
+  uint32_t mul, shift;             // n / d = (umulhi(n, mul) + n) >> shift for n < 2^31
+};
+FastDiv prep_fastdiv(uint32_t d);
+struct PrepParams {
+  int batch, seqlen, heads, head_dim, rotary_dim;
+  uint32_t rows;                   // batch * seqlen * heads (< 2^31)
+  FastDiv div_heads, div_seqlen;
+  float eps;
+  const __nv_bfloat16* x;
+  int64_t x_stride[3];
+  const __nv_bfloat16* w;          // nullable learned scale (head_dim)
+  const __nv_bfloat16* cos;
+  const __nv_bfloat16* sin;
+  int64_t cs_stride[2];
+  __nv_bfloat16* rot;              // forward: RoPE(Norm(x) * w), nullable
+  int64_t rot_stride[3];
+  __nv_bfloat16* plain;            // forward: Norm(x), nullable
+  int64_t plain_stride[3];
+  const __nv_bfloat16* drot;       // backward cotangents, nullable
+  int64_t drot_stride[3];
+  const __nv_bfloat16* dplain;
+  int64_t dplain_stride[3];
+  __nv_bfloat16* dx;
+  int64_t dx_stride[3];
+  float* dw_part;                  // backward: [grid][head_dim] partials (nullable)
+};
+int prep_grid(bool backward, const PrepParams& p, int sm_count);
+int launch_prep_fwd(const PrepParams& p, int grid, cudaStream_t stream);
+int launch_prep_bwd(const PrepParams& p, int grid, cudaStream_t stream);
+int launch_prep_dw_reduce(const float* part, int n_parts, int d, float* dw, cudaStream_t stream);
+
 int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream);
 // pass: d512 runs pass 0 (P) then pass 1 (dS); d256 computes both in pass 0;
 // pass 2 is the forward's first pass (online softmax, d512 only).

@@ -180,13 +180,70 @@ int g4_build_mask(uint8_t* out, int32_t batch, int32_t q_len, int32_t kv_len, in
                   const int32_t* document_ids, const uint8_t* key_padding, void* stream);
 
 /*
+ * Fused Q/K/V preparation (rows of one projection output, bf16):
+ *   rot   = RoPE(Norm(x) * weight)   Norm(x) = x * (mean(x^2) + eps)^-1/2
+ *   plain = Norm(x)
+ * RoPE is rotate-half on the leading rotary_dim features, the rest passed
+ * through: rot_i = n_i cos_i - n_{i+h} sin_i (i < h), n_i cos_i + n_{i-h} sin_i
+ * (h <= i < rotary_dim), h = rotary_dim / 2.
+ * Gemma-4 uses it as Q = RoPE(QNorm(q_proj)), K = RoPE(KNorm(k_proj)),
+ * V = VNorm(v_proj) (src/gemma4_fa4/h100_torch_ops.py:302-326, :396-403) and,
+ * for global layers, K = partial_RoPE(KNorm(Z)), V = VNorm(Z) from one source
+ * Z in a single pass (both outputs set; src/gemma4_fa4/reference.py:306-328).
+ * Layer-op tables are full width (rotary_dim = head_dim) with the
+ * proportional partial rotation carried by cos = 1, sin = 0 entries; the
+ * reference helper's tables cover only the rotated subspace.
+ * The backward applies both adjoints and sums them into dx
+ * (docs/design.md:202-213), and optionally returns the FP32 gradient of the
+ * learned scale, reduced deterministically through the workspace.
+ */
+typedef struct g4_prep_args {
+  const void* x;        /* (B,S,H,head_dim), feature stride 1 */
+  const void* weight;   /* learned scale (head_dim), nullable = no scale */
+  const void* cos;      /* (B,S,rotary_dim), feature stride 1; unused if rotary_dim == 0 */
+  const void* sin;
+  void* rot;            /* forward output, nullable */
+  void* plain;          /* forward output, nullable */
+  const void* drot;     /* backward: cotangent of rot, nullable */
+  const void* dplain;   /* backward: cotangent of plain, nullable */
+  void* dx;             /* backward output */
+  float* dweight;       /* backward output (head_dim floats), nullable; needs weight and drot */
+  /* strides in elements: [batch, token, head], non-negative multiples of 8 */
+  int64_t x_stride[3];
+  int64_t rot_stride[3];
+  int64_t plain_stride[3];
+  int64_t drot_stride[3];
+  int64_t dplain_stride[3];
+  int64_t dx_stride[3];
+  int64_t cos_stride[2];  /* [batch, token]; 0 broadcasts */
+  int32_t batch;
+  int32_t seqlen;
+  int32_t num_heads;
+  int32_t head_dim;     /* 256 or 512 */
+  int32_t rotary_dim;   /* 0 (no rotation) or a power of two in [16, head_dim] */
+  float eps;            /* 1e-6 for Gemma-4 */
+  void* workspace;      /* backward with dweight: g4_prep_bwd_workspace_bytes */
+  size_t workspace_bytes;
+} g4_prep_args;
+
+/* Workspace bytes of g4_prep_bwd (0 without dweight; no device access). */
+size_t g4_prep_bwd_workspace_bytes(const g4_prep_args* args);
+/* rot and/or plain from x.  Replaces the eager norm/rotary chain of the
+ * reference layer ops (h100_torch_ops.py:396-403, :456-461, :729-733, :840-843). */
+int g4_prep_fwd(const g4_prep_args* args, void* stream);
+/* dx (and dweight) from drot and/or dplain; the adjoint of g4_prep_fwd
+ * (torch autograd through reference.py:276-328 in the reference). */
+int g4_prep_bwd(const g4_prep_args* args, void* stream);
+
+/*
  * Launch accounting and opt-in timing (benchmark/profiling support; no
  * reference counterpart -- the reference times whole Python calls).
  * Kernel ids: 0 forward, 1 backward preprocess, 2 backward dQ (recompute),
  * 3 backward dK/dV (recompute), 4 planning (tile lists, vision pairs, tile
  * ranges), 5 mask builder, 6 backward P/dS scores, 7-9 backward dV / dK / dQ
  * tile GEMMs (materialised path), 10 two-pass forward softmax, 11 two-pass
- * forward O = P V.
+ * forward O = P V, 12 decode, 13 decode combine, 14 preparation forward,
+ * 15 preparation backward, 16 preparation dweight reduction.
  *  - g4_launch_count: launches of `kernel_id` issued by this process so far.
  *  - g4_profile_enable(1): every later launch is bracketed by CUDA events on
  *    its own stream; g4_profile_read synchronises those events and returns the

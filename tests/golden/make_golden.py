@@ -14,7 +14,13 @@ small seeded cases, the outputs of its own CPU path:
 * ``gemma4_attention_mask`` bool masks (``masks.py:8-80``);
 * ``build_gemma4_local_sparse_schedule`` rows and storage bytes
   (``sparse_schedule.py:291-374``) and the storage upper bound;
-* ``attention_flops`` (``reference.py:338-356``).
+* ``attention_flops`` (``reference.py:338-356``);
+* the Q/K/V preparation: ``prepare_global_kv_from_projection_source``
+  (``reference.py:306-328``) and the layer ops' ``_rms_norm`` /
+  ``_apply_rotary`` (``h100_torch_ops.py:302-326``), with float64 autograd
+  gradients of the source and the learned norm scale.
+
+``--prep-only`` regenerates just the preparation fixtures.
 
 The fixtures are written to ``tests/golden/*.npz`` / ``*.json`` next to this
 script.  Nothing under ``tests/`` reads the reference at test time.
@@ -98,8 +104,59 @@ def _varlen_case(ref, name, *, cu_q, cu_k, hq, hkv, d, window, vision=None, docs
     np.savez_compressed(os.path.join(HERE, f"varlen_{name}.npz"), **arrays, meta=json.dumps(meta))
 
 
+def _prep_case(name, fn, arrays_in, grads_seed):
+    """Run ``fn`` (returning (rot, plain)) under float64 autograd; save inputs,
+    outputs, the cotangents and the gradients of x and the norm weight."""
+    x = torch.from_numpy(arrays_in["x"]).requires_grad_(True)
+    w = torch.from_numpy(arrays_in["weight"]).requires_grad_(True)
+    cos, sin = torch.from_numpy(arrays_in["cos"]), torch.from_numpy(arrays_in["sin"])
+    rot, plain = fn(x, w, cos, sin)
+    g = torch.Generator().manual_seed(grads_seed)
+    g_rot = torch.randn(rot.shape, dtype=torch.float64, generator=g)
+    g_plain = torch.randn(plain.shape, dtype=torch.float64, generator=g)
+    torch.autograd.backward((rot, plain), (g_rot, g_plain))
+    np.savez_compressed(os.path.join(HERE, f"prep_{name}.npz"), **arrays_in,
+                        rot=rot.detach().numpy(), plain=plain.detach().numpy(),
+                        g_rot=g_rot.numpy(), g_plain=g_plain.numpy(), dx=x.grad.numpy(),
+                        dweight=w.grad.numpy(),
+                        meta=json.dumps(dict(rotary_dim=arrays_in["rotary_dim"].item())))
+
+
+def prep_cases() -> None:
+    import gemma4_fa4.h100_torch_ops as layer_ops
+    import gemma4_fa4.reference as ref
+
+    rng = np.random.default_rng(41)
+    # global shared source Z in the reference helper's (B, H, S, D) layout with
+    # (B, S, rotary_dim) tables: K = partial_RoPE(KNorm(Z)), V = VNorm(Z).
+    x = rng.standard_normal((1, 2, 3, 512)) * 1.7
+    ang = rng.uniform(0.0, 6.0, size=(1, 3, 128))
+    arrays = dict(x=x, weight=rng.uniform(0.5, 1.5, size=512), cos=np.cos(ang), sin=np.sin(ang),
+                  rotary_dim=np.array(128))
+
+    def global_kv(x, w, cos, sin):
+        return ref.prepare_global_kv_from_projection_source(
+            x, k_norm_weight=w, cos=cos, sin=sin, partial_rotary_factor=0.25)
+
+    _prep_case("global_kv_partial", global_kv, arrays, 42)
+
+    # layer-op order: (B, S, H, D) operand, full-width HF tables (B, S, D).
+    x = rng.standard_normal((1, 3, 2, 256)) * 0.6
+    ang = rng.uniform(0.0, 6.0, size=(1, 3, 128))
+    ang = np.concatenate((ang, ang), axis=-1)
+    arrays = dict(x=x, weight=rng.uniform(0.5, 1.5, size=256), cos=np.cos(ang), sin=np.sin(ang),
+                  rotary_dim=np.array(256))
+
+    def layer_qk(x, w, cos, sin):
+        return (layer_ops._apply_rotary(layer_ops._rms_norm(x, w), cos, sin),
+                layer_ops._rms_norm(x, None))
+
+    _prep_case("layer_full_d256", layer_qk, arrays, 43)
+
+
 def main(reference_src: str) -> None:
     sys.path.insert(0, reference_src)
+    prep_cases()
     import gemma4_fa4.reference as ref
     from gemma4_fa4.masks import gemma4_attention_mask
     from gemma4_fa4.model_spec import GLOBAL_ATTENTION, SLIDING_ATTENTION
@@ -200,4 +257,10 @@ def main(reference_src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    src = args[0] if args else "/root/reference/src"
+    if "--prep-only" in sys.argv:
+        sys.path.insert(0, src)
+        prep_cases()
+    else:
+        main(src)

@@ -163,3 +163,39 @@ def test_mask_aware_pairs_text_matches_closed_form():
             oracle.valid_pair_count(s, w)
     assert oracle.valid_pair_count(2048, 1024) == 1_573_376
     assert oracle.valid_pair_count(4096, None) == 8_390_656
+
+
+@pytest.mark.parametrize("name,layout", [("global_kv_partial", "bhsd"), ("layer_full_d256", "bshd")])
+def test_prep_oracle_matches_reference_golden(name, layout):
+    # The reference computes the RMS statistics through ``x.float()`` even for
+    # float64 inputs (reference.py:277, h100_torch_ops.py:308), so its float64
+    # fixtures carry float32 rounding of the norm: agreement is to ~1e-6.
+    from oracle import prep
+
+    z = np.load(os.path.join(GOLD, f"prep_{name}.npz"))
+    rd = int(z["rotary_dim"])
+    axis = 1 if layout == "bhsd" else 2  # where the head axis sits in x
+    cos, sin = np.expand_dims(z["cos"], axis), np.expand_dims(z["sin"], axis)
+    rot = prep.apply_partial_rotary(prep.rms_norm(z["x"], z["weight"]), cos, sin, rd)
+    np.testing.assert_allclose(rot, z["rot"], rtol=0, atol=5e-6)
+    np.testing.assert_allclose(prep.rms_norm(z["x"]), z["plain"], rtol=0, atol=5e-6)
+    dx, dw = prep.prepare_bwd(z["x"], z["weight"], cos, sin, rd, z["g_rot"], z["g_plain"])
+    np.testing.assert_allclose(dx, z["dx"], rtol=0, atol=5e-6)
+    np.testing.assert_allclose(dw, z["dweight"], rtol=1e-5, atol=5e-6)
+    if name == "global_kv_partial":
+        k, v = prep.prepare_global_kv(z["x"], z["weight"], cos, sin, 0.25)
+        np.testing.assert_allclose(k, z["rot"], rtol=0, atol=5e-6)
+        np.testing.assert_allclose(v, z["plain"], rtol=0, atol=5e-6)
+
+
+def test_prep_rotary_adjoint_is_the_transpose():
+    from oracle import prep
+
+    rng = np.random.default_rng(5)
+    for rd in (0, 8, 16, 32):
+        x, g = rng.standard_normal((3, 32)), rng.standard_normal((3, 32))
+        ang = rng.uniform(0, 6, size=(3, rd))
+        c, s = np.cos(ang), np.sin(ang)
+        lhs = np.sum(prep.apply_partial_rotary(x, c, s, rd) * g)
+        rhs = np.sum(x * prep.rotary_adjoint(g, c, s, rd))
+        assert abs(lhs - rhs) < 1e-12
