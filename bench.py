@@ -19,7 +19,9 @@ The JSON line carries, besides the contract keys:
                 buffers: H2D of q, k, v, dO and D2H of dq, dk, dv every step;
   local_c0      the local d256 S2048 config measured the same way (secondary);
   decode_c4     single-token decode against 32768-token global and 1024-token
-                local static caches (secondary): HBM GB/s of the decode kernel.
+                local static caches (secondary): HBM GB/s of the decode kernel;
+  prep_c1       the fused Q/K/V preparation of the c1 global layer (secondary):
+                HBM GB/s of the preparation kernels, forward and backward.
 """
 
 from __future__ import annotations
@@ -164,6 +166,62 @@ def decode_measure(ops, _lib, dev, seed, iters):
                          "launches_per_call": {n: prof[n][0] // iters for n in prof
                                                if prof[n][0] > 0}}
         del kc, vc, q, k, v
+    del flush
+    return out
+
+
+def prep_measure(dev, seed, iters):
+    """Fused Q/K/V preparation of the c1 global layer (S=4096): Q rows (32 heads)
+    and the shared K/V source Z (4 heads, K and V from one read), forward and
+    backward (with the norm-scale gradient), full-width tables with 25% of the
+    frequencies rotated.  Device time of the prep kernels per call (CUDA events
+    around each launch), L2 flushed before every call by a 1 GiB read.
+    Algorithmic bytes: every row read and written once (x, outputs,
+    cotangents, dx) plus the tables once per token."""
+    from gemma4_fa4_kernels_b200 import _lib
+    from gemma4_fa4_kernels_b200.prep import prep_bwd, prep_fwd
+
+    g = torch.Generator().manual_seed(seed)
+    flush = torch.empty(1 << 28, dtype=torch.float32, device=dev)
+    hbm_peak, hbm_kind = load_hbm_peak()
+    s, d = C1["seq"], C1["d"]
+    inv = 1.0 / (1_000_000.0 ** (torch.arange(0, d // 4, 2, dtype=torch.float64) / d))
+    inv = torch.cat((inv, torch.zeros(d // 2 - d // 8, dtype=torch.float64)))
+    ang = torch.arange(s, dtype=torch.float64)[:, None] * inv
+    ang = torch.cat((ang, ang), dim=-1)[None]
+    cos, sin = ang.cos().to(torch.bfloat16).to(dev), ang.sin().to(torch.bfloat16).to(dev)
+    w = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16).to(dev)
+    out = {"l2": "flushed before every call (1 GiB read)", "hbm_peak_gbs": hbm_peak,
+           "peak_kind": f"{hbm_kind} HBM copy bandwidth"}
+    for key, heads, plain in (("q_global", C1["hq"], False), ("kv_shared_global", C1["hkv"], True)):
+        x = torch.randn(1, s, heads, d, generator=g).to(torch.bfloat16).to(dev)
+        gr = torch.randn(1, s, heads, d, generator=g).to(torch.bfloat16).to(dev)
+        gp = torch.randn(1, s, heads, d, generator=g).to(torch.bfloat16).to(dev) if plain else None
+        row = s * heads * d * 2
+        tables = 2 * s * d * 2
+        for phase, fn, nbytes, kernels in (
+                ("fwd", lambda: prep_fwd(x, w, cos, sin, d, want_plain=plain),
+                 row * (2 + plain) + tables, ("prep_fwd",)),
+                ("bwd", lambda: prep_bwd(x, w, cos, sin, d, gr, gp),
+                 row * (3 + plain) + tables, ("prep_bwd", "prep_dw_reduce"))):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(dev)
+            _lib.profile_reset()
+            _lib.profile_enable(True)
+            for _ in range(iters):
+                flush.max()
+                fn()
+            torch.cuda.synchronize(dev)
+            _lib.profile_enable(False)
+            prof = _lib.profile_read()
+            per = {k: prof[k][1] / max(prof[k][0], 1) * 1e3 for k in kernels}
+            kern_us = sum(per.values())
+            gbs = nbytes / (kern_us * 1e-6) / 1e9
+            out[f"{key}_{phase}"] = {"rows": s * heads, "head_dim": d, "bytes": nbytes,
+                                     "kernel_us": {k: round(v, 2) for k, v in per.items()},
+                                     "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4)}
+        del x, gr, gp
     del flush
     return out
 
@@ -390,6 +448,9 @@ def run_b200(args, world, rank, local):
     # ---- single-token decode (secondary line item, BASELINE configs[4](iii)) ----
     decode = decode_measure(ops, _lib, dev, seed=3000 + rank, iters=50)
 
+    # ---- fused Q/K/V preparation of the c1 layer (secondary line item) ----
+    prep = prep_measure(dev, seed=4000 + rank, iters=20)
+
     # ---- end to end through the public adapter, host buffers ----
     hq_, hk_, hv_, hdo_ = (t.cpu().pin_memory() for t in (q, k, v, do))
     hgrads = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, k, v)]
@@ -454,6 +515,7 @@ def run_b200(args, world, rank, local):
                          "ms_per_step": round(lms, 4), "value": round(local_tf, 2),
                          "unit": "TFLOP/s", "pct_peak": round(local_tf / peak_sus, 4)},
             "decode_c4": decode,
+            "prep_c1": prep,
         }
         print(json.dumps(line), flush=True)
 
@@ -495,7 +557,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--cpu-heads", type=int, default=4,
+    ap.add_argument("--cpu-heads", type=int, default=16,
                     help="query heads in the CPU-baseline sample")
     ap.add_argument("--ref-heads", type=int, default=1,
                     help="query heads per step of the reference arm")

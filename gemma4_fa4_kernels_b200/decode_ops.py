@@ -20,7 +20,9 @@ The attention runs on the split-key decode kernels of this package through
 ``ops.attn_fwd`` on (1, L, H, D) views of the caches (no copy); the reference
 pads the query to the cache length below position 1024 and otherwise calls
 its packed forward, both of which equal this single-row lower-right result.
-Projections are plain cuBLAS BF16 GEMMs (``torch.nn.functional.linear``).
+Projections are plain cuBLAS BF16 GEMMs (``torch.nn.functional.linear``); the
+Q/K norms, the rotary embedding and the value norm run in the fused
+``g4_prep_fwd`` kernel (global layers: K and V from one read of Z).
 """
 
 from __future__ import annotations
@@ -29,6 +31,7 @@ import torch
 
 from . import ops
 from .errors import UnsupportedB200Path
+from .prep import prep_fwd
 
 HIDDEN_SIZE = 5376
 LOCAL_GEOMETRY = (32, 16, 256)   # query heads, KV heads, head dim
@@ -38,25 +41,6 @@ MAX_POSITION = 262144
 
 GLOBAL_STATIC_CACHE_DECODE_OP_NAME = "gemma4_fa4_b200::global_static_cache_decode_fwd"
 LOCAL_STATIC_CACHE_DECODE_OP_NAME = "gemma4_fa4_b200::local_static_cache_decode_fwd"
-
-
-# ------------------------------------------------------------------------------------
-# Gemma-4 layer pieces (reference h100_torch_ops.py:302-326)
-# ------------------------------------------------------------------------------------
-def _rms_norm(x: torch.Tensor, weight: torch.Tensor | None) -> torch.Tensor:
-    """RMS over the last dim in FP32 (eps 1e-6), optional weight, back to x's dtype."""
-    xf = x.float()
-    y = xf * torch.pow(xf.pow(2).mean(-1, keepdim=True) + 1e-6, -0.5)
-    if weight is not None:
-        y = y * weight.float()
-    return y.type_as(x)
-
-
-def _rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """x * cos + rotate_half(x) * sin for (B, S, H, D) x and (B, S, D) cos/sin."""
-    half = x.shape[-1] // 2
-    rotated = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
-    return x * cos.unsqueeze(2) + rotated * sin.unsqueeze(2)
 
 
 # ------------------------------------------------------------------------------------
@@ -151,11 +135,10 @@ def _global_impl(hidden_states: T, cos: T, sin: T, position_ids: T, cache_k: T, 
                               cache_length, weights)
     hq, hkv, d = GLOBAL_GEOMETRY
     lin = torch.nn.functional.linear
-    q = _rotary(_rms_norm(lin(hidden_states, q_proj_weight).view(1, 1, hq, d), q_norm_weight),
-                cos, sin)
-    z = lin(hidden_states, k_proj_weight).view(1, 1, hkv, d)
-    k = _rotary(_rms_norm(z, k_norm_weight), cos, sin)
-    v = _rms_norm(z, None)
+    q, _ = prep_fwd(lin(hidden_states, q_proj_weight).view(1, 1, hq, d), q_norm_weight, cos, sin,
+                    d)
+    k, v = prep_fwd(lin(hidden_states, k_proj_weight).view(1, 1, hkv, d), k_norm_weight, cos, sin,
+                    d, want_plain=True)
     slot = torch.arange(1, device=cache_k.device) + cache_length
     cache_k.index_copy_(2, slot, k.transpose(1, 2))
     cache_v.index_copy_(2, slot, v.transpose(1, 2))
@@ -176,11 +159,13 @@ def _local_impl(hidden_states: T, cos: T, sin: T, position_ids: T, cache_k: T, c
                                cache_length, weights)
     hq, hkv, d = LOCAL_GEOMETRY
     lin = torch.nn.functional.linear
-    q = _rotary(_rms_norm(lin(hidden_states, q_proj_weight).view(1, 1, hq, d), q_norm_weight),
-                cos, sin)
-    k = _rotary(_rms_norm(lin(hidden_states, k_proj_weight).view(1, 1, hkv, d), k_norm_weight),
-                cos, sin).transpose(1, 2)
-    v = _rms_norm(lin(hidden_states, v_proj_weight).view(1, 1, hkv, d), None).transpose(1, 2)
+    q, _ = prep_fwd(lin(hidden_states, q_proj_weight).view(1, 1, hq, d), q_norm_weight, cos, sin,
+                    d)
+    k, _ = prep_fwd(lin(hidden_states, k_proj_weight).view(1, 1, hkv, d), k_norm_weight, cos, sin,
+                    d)
+    _, v = prep_fwd(lin(hidden_states, v_proj_weight).view(1, 1, hkv, d), None, None, None, 0,
+                    want_rot=False, want_plain=True)
+    k, v = k.transpose(1, 2), v.transpose(1, 2)
     if position < LOCAL_WINDOW:
         slot = torch.arange(1, dtype=cache_length.dtype, device=cache_k.device) + cache_length
         cache_k.index_copy_(2, slot, k)

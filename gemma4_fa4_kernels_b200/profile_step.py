@@ -4,9 +4,11 @@
 
 Configs: c0 (local d256 W1024, S=2048, 32Q/16KV) and c1 (global d512 causal,
 S=4096, 32Q/4KV), B=1, BF16, inputs as in bench.py; decode (one query token
-against a 32768-token global d512 32Q/4KV static cache, forward only).  Inputs
-exceed the 126 MB L2 for c1 and decode.  Prints nothing but the per-step wall
-time; meant to be wrapped by ncu with -k/-c filters.
+against a 32768-token global d512 32Q/4KV static cache, forward only); prep
+(the fused preparation of the c1 layer's Q rows, 4096 x 32 x 512: forward,
+then backward with the norm-scale gradient).  Inputs exceed the 126 MB L2 for
+c1, decode and prep.  Prints nothing but the per-step wall time; meant to be
+wrapped by ncu with -k/-c filters.
 """
 
 from __future__ import annotations
@@ -22,6 +24,7 @@ CONFIGS = {
     "c0": dict(seq=2048, hq=32, hkv=16, d=256, window=1024),
     "c1": dict(seq=4096, hq=32, hkv=4, d=512, window=0),
     "decode": dict(seq=32768, hq=32, hkv=4, d=512, window=0),
+    "prep": dict(seq=4096, hq=32, hkv=4, d=512, window=0),
 }
 
 
@@ -53,6 +56,22 @@ def main() -> None:
         for _ in range(args.steps):
             t0 = time.perf_counter()
             ops.attn_fwd(q, kc.transpose(1, 2), vc.transpose(1, 2), window=c["window"])
+            torch.cuda.synchronize()
+            print(f"step {time.perf_counter() - t0:.4f} s", flush=True)
+        return
+    if args.config == "prep":
+        from .prep import prep_bwd, prep_fwd
+
+        x = torch.randn(1, s, hq, d, generator=g).to(torch.bfloat16).to(dev)
+        gr = torch.randn(1, s, hq, d, generator=g).to(torch.bfloat16).to(dev)
+        w = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16).to(dev)
+        ang = torch.rand(1, s, d // 2, generator=g, dtype=torch.float64) * 6.0
+        ang = torch.cat((ang, ang), dim=-1)
+        cos, sin = ang.cos().to(torch.bfloat16).to(dev), ang.sin().to(torch.bfloat16).to(dev)
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            prep_fwd(x, w, cos, sin, d)
+            prep_bwd(x, w, cos, sin, d, gr, None)
             torch.cuda.synchronize()
             print(f"step {time.perf_counter() - t0:.4f} s", flush=True)
         return

@@ -66,16 +66,3 @@ def test_host_tensors_are_refused_before_any_work():
         d.global_static_cache_decode_fwd(*_global_args())
     with torch.no_grad(), pytest.raises(UnsupportedB200Path, match="CUDA device"):
         d.local_static_cache_decode_fwd(*_local_args())
-
-
-def test_rotary_and_norm_follow_the_gemma_formulas():
-    x = torch.randn(1, 1, 2, 8, dtype=torch.float64)
-    cos = torch.rand(1, 1, 8, dtype=torch.float64)
-    sin = torch.rand(1, 1, 8, dtype=torch.float64)
-    y = d._rotary(x, cos, sin)
-    rot = torch.cat((-x[..., 4:], x[..., :4]), dim=-1)
-    assert torch.allclose(y, x * cos[:, :, None] + rot * sin[:, :, None])
-    w = torch.rand(8, dtype=torch.float64)
-    n = d._rms_norm(x, w)
-    ref = x / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * w
-    assert torch.allclose(n, ref)

@@ -17,8 +17,23 @@ if not torch.cuda.is_available():  # pragma: no cover - CPU containers
 
 from gemma4_fa4_kernels_b200 import _lib  # noqa: E402
 from gemma4_fa4_kernels_b200 import decode_ops as d  # noqa: E402
+from gemma4_fa4_kernels_b200.prep import prep_fwd  # noqa: E402
 
 H = d.HIDDEN_SIZE
+
+
+def _rms_norm(x, weight):
+    """Gemma RMS norm in FP32 (eps 1e-6), optional scale (h100_torch_ops.py:302-313)."""
+    xf = x.float()
+    y = xf * torch.pow(xf.pow(2).mean(-1, keepdim=True) + 1e-6, -0.5)
+    return y if weight is None else y * weight.float()
+
+
+def _rotary(x, cos, sin):
+    """x * cos + rotate_half(x) * sin on (B, S, H, D) with (B, S, D) tables."""
+    half = x.shape[-1] // 2
+    rotated = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return x * cos.unsqueeze(2) + rotated * sin.unsqueeze(2)
 
 
 def _rms_unit(x):
@@ -45,21 +60,22 @@ def _ref_layer(h, cos, sin, wq, wk, wv, wo, qn, kn, cache_k, cache_v, active, hq
                window):
     """FP32 composition: projections, norms and rotary in FP32 from the BF16
     operands; attention in float64 over the op's BF16 cache contents.  Also
-    returns the float64 LSE for the query as the op's BF16 dataflow forms it
-    (BF16 projection, norm and rotary), which isolates the attention kernel:
-    with d512 scores near 80, BF16 rounding of Q alone moves the LSE by ~0.1."""
+    returns the float64 LSE for the query exactly as the op forms it (BF16
+    projection, then the fused preparation kernel), which isolates the
+    attention kernel: with d512 scores near 80, BF16 rounding of Q alone moves
+    the LSE by ~0.1."""
     f = lambda t: t.float()  # noqa: E731
     lin = torch.nn.functional.linear
-    q = d._rotary(d._rms_norm(lin(f(h), f(wq)).view(1, 1, hq, dim), qn), f(cos), f(sin))
+    q = _rotary(_rms_norm(lin(f(h), f(wq)).view(1, 1, hq, dim), qn), f(cos), f(sin))
     z = lin(f(h), f(wk)).view(1, 1, hkv, dim)
-    k_new = d._rotary(d._rms_norm(z, kn), f(cos), f(sin))
-    v_new = d._rms_norm(z if wv is None else lin(f(h), f(wv)).view(1, 1, hkv, dim), None)
+    k_new = _rotary(_rms_norm(z, kn), f(cos), f(sin))
+    v_new = _rms_norm(z if wv is None else lin(f(h), f(wv)).view(1, 1, hkv, dim), None)
     kk = cache_k[:, :, :active].double().cpu().numpy()
     vv = cache_v[:, :, :active].double().cpu().numpy()
     o, _ = oracle.attention_fwd(q.transpose(1, 2).double().cpu().numpy(), kk, vv,
                                 sliding_window=window)
     out = lin(torch.from_numpy(o).float().cuda().transpose(1, 2).reshape(1, 1, hq * dim), f(wo))
-    q_bf = d._rotary(d._rms_norm(lin(h, wq).view(1, 1, hq, dim), qn), cos, sin)
+    q_bf, _ = prep_fwd(lin(h, wq).view(1, 1, hq, dim), qn, cos, sin, dim)
     _, lse_bf = oracle.attention_fwd(q_bf.transpose(1, 2).double().cpu().numpy(), kk, vv,
                                      sliding_window=window)
     return out, lse_bf, k_new, v_new
