@@ -16,7 +16,8 @@ The JSON line carries, besides the contract keys:
   cpu_baseline  the numpy oracle (the reference CPU path restated) on a bounded
                 sample of the same workload on this host's cores;
   e2e           the same metric through the public adapter with pinned host
-                buffers: H2D of q, k, v, dO and D2H of dq, dk, dv every step;
+                buffers: H2D of q, k, v, dO and D2H of dq, dk, dv every step,
+                the copies of neighbouring steps overlapping the compute;
   local_c0      the local d256 S2048 config measured the same way (secondary);
   decode_c4     single-token decode against 32768-token global and 1024-token
                 local static caches (secondary): HBM GB/s of the decode kernel;
@@ -457,24 +458,48 @@ def run_b200(args, world, rank, local):
     h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_, hdo_))
     d2h = sum(t.numel() * t.element_size() for t in hgrads)
 
-    def e2e_step():
-        dq_in = hq_.to(dev, non_blocking=True).requires_grad_(True)
-        dk_in = hk_.to(dev, non_blocking=True).requires_grad_(True)
-        dv_in = hv_.to(dev, non_blocking=True).requires_grad_(True)
-        ddo = hdo_.to(dev, non_blocking=True)
-        out, _lse = fa4_global_text_forward(dq_in, dk_in, dv_in)
-        out.backward(ddo)
-        for h, t in zip(hgrads, (dq_in.grad, dk_in.grad, dv_in.grad)):
-            h.copy_(t, non_blocking=True)
+    # Two-stage pipeline on the public API: inputs of step i+1 go up on one copy
+    # stream and gradients of step i come down on another while step i computes
+    # on the current stream.  Every step still moves its own inputs and results
+    # between pinned host memory and the device inside the timed region.
+    compute = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dbufs = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
+    loaded = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]
 
-    for _ in range(2):
-        e2e_step()
+    def upload(slot):
+        up.wait_event(used[slot])  # the slot's previous step has finished reading it
+        with torch.cuda.stream(up):
+            for d_, h_ in zip(dbufs[slot], (hq_, hk_, hv_, hdo_)):
+                d_.copy_(h_, non_blocking=True)
+            loaded[slot].record(up)
+
+    def e2e_run(n):
+        upload(0)
+        for i in range(n):
+            slot = i % 2
+            if i + 1 < n:
+                upload(slot ^ 1)
+            compute.wait_event(loaded[slot])
+            bq, bk, bv, bdo = dbufs[slot]
+            dq_in, dk_in, dv_in = (t.detach().requires_grad_(True) for t in (bq, bk, bv))
+            out, _lse = fa4_global_text_forward(dq_in, dk_in, dv_in)
+            out.backward(bdo)
+            used[slot].record(compute)
+            down.wait_event(used[slot])
+            with torch.cuda.stream(down):
+                for h, t in zip(hgrads, (dq_in.grad, dk_in.grad, dv_in.grad)):
+                    t.record_stream(down)
+                    h.copy_(t, non_blocking=True)
+        compute.wait_stream(down)
+
+    e2e_run(2)
     torch.cuda.synchronize(dev)
     barrier(world)
     b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     b0.record()
-    for _ in range(args.steps):
-        e2e_step()
+    e2e_run(args.steps)
     b1.record()
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(b0.elapsed_time(b1) / args.steps, world, dev)
@@ -508,7 +533,8 @@ def run_b200(args, world, rank, local):
             "e2e": {"value": round(world * fl["total"] / (e2e_ms * 1e-3) / 1e12, 2),
                     "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 3),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "fa4_global_text_forward + autograd backward"},
+                    "api": "fa4_global_text_forward + autograd backward; H2D of step i+1 and "
+                           "D2H of step i overlap step i on two copy streams"},
             "clocks": clocks,
             "gpu_launches": gpu_launches,
             "local_c0": {"workload": C0["name"] + " (BASELINE configs[0])",

@@ -4,10 +4,15 @@
 // One CTA owns a 128-row query tile of one query head and one 256-wide slab
 // of the value/output head dimension (local d256: one slab; global d512: two
 // slabs, each recomputing the 512-deep QK^T because a 128x512 fp32 O would
-// fill all of TMEM).  Warp roles (192 threads):
-//   warps 0-3  softmax + epilogue: thread r owns query row r (TMEM lane r)
-//   warp  4    TMA producer (one elected lane); also allocates TMEM
-//   warp  5    MMA issuer (one elected lane)
+// fill all of TMEM).  Warp roles (320 threads):
+//   warps 0-7  softmax + epilogue: warps w and w+4 share TMEM lanes
+//              32*(w%4).. (their query rows); warp w handles keys [0, 64) of
+//              each tile and O columns [0, 128), warp w+4 keys [64, 128) and
+//              O columns [128, 256).  The two halves of a row exchange their
+//              partial row max through shared memory, so both take identical
+//              rescale decisions, and add their row sums at the end.
+//   warp  8    TMA producer (one elected lane); also allocates TMEM
+//   warp  9    MMA issuer (one elected lane)
 // TMEM columns: S0 [0,128), S1 [128,256), O [256,512); P (bf16 pairs) is
 // written over the first 64 columns of its S buffer and consumed from TMEM by
 // the PV MMA.  K/V chunks stream through a ring of 32 KB shared stages in the
@@ -30,6 +35,12 @@
 
 namespace g4 {
 
+constexpr int kFwdSoftWarps = 8;
+constexpr int kFwdSoftThreads = kFwdSoftWarps * 32;
+constexpr int kFwdProducerWarp = kFwdSoftWarps;
+constexpr int kFwdMmaWarp = kFwdSoftWarps + 1;
+constexpr int kFwdThreads = kFwdSoftThreads + 64;
+
 template <int DQK>
 struct FwdCfg {
   static constexpr int kQBytes = DQK * kTileM * 2;
@@ -37,8 +48,8 @@ struct FwdCfg {
   static constexpr int kStages = DQK == 256 ? 5 : 3;
   static constexpr int kKChunks = DQK / 128;  // 128-deep K chunks per key tile
   static constexpr int kVChunks = 2;          // 64 keys x 256 values per chunk
-  static constexpr int kMiscBytes = 2048;
-  static constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + kMiscBytes + 1024;
+  static constexpr int kMiscBytes = 3072;
+  static constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + kMiscBytes;
 };
 
 struct FwdMisc {
@@ -54,18 +65,25 @@ struct FwdMisc {
   int k_lo;
   int k_hi;
   int pad[4];
-  int kvis[kTileN];
-  int kdoc[kTileN];
+  // Two 1 KB exchange buffers.  Tile j uses xbuf[j & 1] for the partial row
+  // maxima ([half][row]) and, with mask metadata, xbuf[(j + 1) & 1] for the
+  // tile's key vision / document ids ([0..127] vision, [128..255] document):
+  // that buffer's last readers finished before the tile's first barrier.  After
+  // the loop xbuf[n_kt & 1] carries the partial row sums.
+  float xbuf[2][2 * kTileM];
 };
+static_assert(sizeof(FwdMisc) <= 3072, "forward misc block exceeds its shared-memory budget");
 
 template <int DQK>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   using Cfg = FwdCfg<DQK>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_addr(smem) & 1023u) != 0) {  // the 128-B swizzle atoms need 1024-B alignment
+    if (p.err) atomicCAS(p.err, 0, 5);
+    return;
+  }
   uint8_t* q_s = smem;
   uint8_t* ring = smem + Cfg::kQBytes;
   FwdMisc* misc = reinterpret_cast<FwdMisc*>(ring + Cfg::kStages * Cfg::kStageBytes);
@@ -103,7 +121,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&misc->s_full[b], 1);
-      mbar_init(&misc->p_full[b], kTileM);
+      mbar_init(&misc->p_full[b], kFwdSoftThreads);
     }
     mbar_init(&misc->o_done, 1);
     mbar_init(&misc->drain, 1);
@@ -112,16 +130,16 @@ __global__ void __launch_bounds__(192, 1)
     misc->k_hi = -1;
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == kFwdProducerWarp) {
     tmem_alloc(&misc->tmem_base, 512);
     tmem_relinquish();
   }
   __syncthreads();
 
   // ---- key range of this query tile (exact bounds; tiles inside are classified) ----
-  const int row = tid;  // valid for tid < 128
+  const int row = tid & (kTileM - 1);  // softmax threads: the TMEM lane (query row)
   const int q_idx = qt * kTileM + row;
-  const bool row_valid = tid < kTileM && q_idx < si.len_q;
+  const bool row_valid = tid < kFwdSoftThreads && q_idx < si.len_q;
   const int q_abs = q_idx + q_off;
   int qvis = -1, qdoc = 0;
   if (row_valid) {
@@ -132,8 +150,10 @@ __global__ void __launch_bounds__(192, 1)
     if (p.mask.window > 0 && qvis >= 0) {
       hi = p.mask.pair_last ? max(hi, p.mask.pair_last[si.meta_base + q_abs]) : si.len_k - 1;
     }
-    atomicMin(&misc->k_lo, lo);
-    atomicMax(&misc->k_hi, min(hi, si.len_k - 1));
+    if (tid < kTileM) {
+      atomicMin(&misc->k_lo, lo);
+      atomicMax(&misc->k_hi, min(hi, si.len_k - 1));
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -144,7 +164,7 @@ __global__ void __launch_bounds__(192, 1)
   const int n_kt = misc->k_hi >= 0 ? misc->k_hi / kTileN - kt_lo + 1 : 0;
   const CtaAbort ab{&misc->abort, p.err};
 
-  if (warp == 4) {
+  if (warp == kFwdProducerWarp) {
     // ============================ TMA producer ============================
     if (lane == 0 && n_kt > 0) {
       tma_prefetch_desc(&tmQ);
@@ -192,7 +212,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kFwdMmaWarp) {
     // ============================ MMA issuer ============================
     if (lane == 0 && n_kt > 0) {
       constexpr uint32_t kIdS = idesc_bf16(128, 128, false, false);
@@ -255,63 +275,67 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
-    // ======================= softmax + epilogue (warps 0-3) =======================
+    // ======================= softmax + epilogue (warps 0-7) =======================
     // Every tcgen05.ld/st below is .sync.aligned, so all control flow around
     // them is kept warp-uniform: `ok` is reduced with __all_sync after each
-    // wait and the rescale decision with __any_sync.  Loops never break, so
-    // the named barriers are reached the same number of times by all warps.
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // wait and the rescale decision with __any_sync.  Loops never break, and
+    // the named barrier 1 (all softmax threads) is reached once per tile (twice
+    // with mask metadata) by every thread, whatever `ok` says.
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int half = warp >> 2;  // keys [64*half, +64) of a tile; O columns [128*half, +128)
     const bool meta = p.mask.has_meta();
     const int qa0 = qt * kTileM + q_off;
     const int qa1 = min((qt + 1) * kTileM, si.len_q) - 1 + q_off;
     float m_run = -INFINITY;  // running max, log2 domain
-    float l_run = 0.f;
+    float l_half = 0.f;       // this half's share of the row sum
     bool ok = true;
     for (int j = 0; j < n_kt; ++j) {
       const int k0 = (kt_lo + j) * kTileN;
+      const int kh = k0 + half * 64;  // first key of this thread's half
       const int cls = meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
+      int* kvis = reinterpret_cast<int*>(misc->xbuf[(j + 1) & 1]);
+      int* kdoc = kvis + kTileN;
       if (meta) {
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        const int kk = k0 + tid;
-        const bool in = kk < si.len_k;
-        misc->kvis[tid] = (p.mask.vis && in) ? p.mask.vis[si.meta_base + kk] : -1;
-        misc->kdoc[tid] = (p.mask.doc && in) ? p.mask.doc[si.meta_base + kk] : 0;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
+        if (tid < kTileN) {
+          const int kk = k0 + tid;
+          const bool in = kk < si.len_k;
+          kvis[tid] = (p.mask.vis && in) ? p.mask.vis[si.meta_base + kk] : -1;
+          kdoc[tid] = (p.mask.doc && in) ? p.mask.doc[si.meta_base + kk] : 0;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
       }
       if (ok) ok = mbar_wait(&misc->s_full[j & 1], (j >> 1) & 1, ab, kDevTimeoutMma);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok) continue;
-      tc_fence_after();
-      float s[kTileN];
-      {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        const uint32_t sb = lane_base + (j & 1) * 128;
+      float s[64];
+      if (ok) {
+        tc_fence_after();
+        uint32_t r0[32], r1[32];
+        const uint32_t sb = lane_base + (j & 1) * 128 + half * 64;
         tmem_ld32(sb + 0, r0);
         tmem_ld32(sb + 32, r1);
-        tmem_ld32(sb + 64, r2);
-        tmem_ld32(sb + 96, r3);
         tmem_wait_ld();
         reg_fence32(r0);
         reg_fence32(r1);
-        reg_fence32(r2);
-        reg_fence32(r3);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           s[i] = __uint_as_float(r0[i]);
           s[32 + i] = __uint_as_float(r1[i]);
-          s[64 + i] = __uint_as_float(r2[i]);
-          s[96 + i] = __uint_as_float(r3[i]);
         }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s[i] = -INFINITY;
       }
       if (cls != 1) {
 #pragma unroll
-        for (int i = 0; i < kTileN; ++i) {
-          const int k = k0 + i;
+        for (int i = 0; i < 64; ++i) {
+          const int k = kh + i;
           bool keep;
           if (k >= si.len_k) {
             keep = false;
           } else if (meta) {
-            keep = mask_allows(p.mask.window, q_abs, k, qvis, qdoc, misc->kvis[i], misc->kdoc[i]);
+            keep = mask_allows(p.mask.window, q_abs, k, qvis, qdoc, kvis[half * 64 + i],
+                               kdoc[half * 64 + i]);
           } else {
             keep = mask_allows(p.mask.window, q_abs, k, -1, 0, -1, 0);
           }
@@ -320,8 +344,11 @@ __global__ void __launch_bounds__(192, 1)
       }
       float mt = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < kTileN; ++i) mt = fmaxf(mt, s[i]);
-      mt *= kLog2e;
+      for (int i = 0; i < 64; ++i) mt = fmaxf(mt, s[i]);
+      float* pm = misc->xbuf[j & 1];
+      pm[half * kTileM + row] = mt * kLog2e;
+      asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
+      mt = fmaxf(pm[row], pm[kTileM + row]);
       float alpha = 1.f;
       bool rescale = false;
       if (mt > m_run + kLazyRescaleLog2) {  // also true for the first finite tile
@@ -332,23 +359,23 @@ __global__ void __launch_bounds__(192, 1)
         }
         m_run = mt;
       }
+      if (!ok) continue;
       const float m_sub = (m_run == -INFINITY) ? 0.f : m_run;
       float rowsum = 0.f;
       {
         uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float p0 = ex2(fmaf(s[c * 64 + 2 * i], kLog2e, -m_sub));
-            const float p1 = ex2(fmaf(s[c * 64 + 2 * i + 1], kLog2e, -m_sub));
-            rowsum += p0 + p1;
-            pk[i] = pack_bf16x2(p0, p1);
-          }
-          tmem_st32(lane_base + (j & 1) * 128 + c * 32, pk);
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = ex2(fmaf(s[2 * i], kLog2e, -m_sub));
+          const float p1 = ex2(fmaf(s[2 * i + 1], kLog2e, -m_sub));
+          rowsum += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
         }
+        // P (bf16 pairs) over the first 64 columns of the S buffer: keys
+        // [64*half, +64) at columns [32*half, +32)
+        tmem_st32(lane_base + (j & 1) * 128 + half * 32, pk);
       }
-      l_run = l_run * alpha + rowsum;
+      l_half = l_half * alpha + rowsum;
       tmem_wait_st();
       if (j > 0) {
         ok = mbar_wait(&misc->o_done, (j - 1) & 1, ab, kDevTimeoutMma);
@@ -356,10 +383,11 @@ __global__ void __launch_bounds__(192, 1)
         if (ok && __any_sync(0xffffffffu, rescale)) {
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 8; c += 2) {
+          for (int c = 0; c < 4; c += 2) {
+            const uint32_t oc = lane_base + 256 + half * 128 + c * 32;
             uint32_t r0[32], r1[32];
-            tmem_ld32(lane_base + 256 + c * 32, r0);
-            tmem_ld32(lane_base + 256 + c * 32 + 32, r1);
+            tmem_ld32(oc, r0);
+            tmem_ld32(oc + 32, r1);
             tmem_wait_ld();
             reg_fence32(r0);
             reg_fence32(r1);
@@ -368,8 +396,8 @@ __global__ void __launch_bounds__(192, 1)
               r0[i] = __float_as_uint(__uint_as_float(r0[i]) * alpha);
               r1[i] = __float_as_uint(__uint_as_float(r1[i]) * alpha);
             }
-            tmem_st32(lane_base + 256 + c * 32, r0);
-            tmem_st32(lane_base + 256 + c * 32 + 32, r1);
+            tmem_st32(oc, r0);
+            tmem_st32(oc + 32, r1);
           }
           tmem_wait_st();
         }
@@ -378,6 +406,10 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) mbar_arrive(&misc->p_full[j & 1]);
     }
     // ---- epilogue: O / l -> bf16, LSE ----
+    float* ls = misc->xbuf[n_kt & 1];
+    ls[half * kTileM + row] = l_half;
+    asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
+    const float l_run = ls[row] + ls[kTileM + row];
     if (ok && n_kt > 0) ok = mbar_wait(&misc->o_done, (n_kt - 1) & 1, ab, kDevTimeoutMma);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
@@ -385,12 +417,12 @@ __global__ void __launch_bounds__(192, 1)
     const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
     __nv_bfloat16* orow = p.o + static_cast<int64_t>(si.b_coord) * p.o_stride[0] +
                           static_cast<int64_t>(si.q_base + q_idx) * p.o_stride[1] +
-                          static_cast<int64_t>(head) * p.o_stride[2] + slab * 256;
+                          static_cast<int64_t>(head) * p.o_stride[2] + slab * 256 + half * 128;
 #pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 4; ++c) {
       uint32_t r[32];
       if (have_o) {
-        tmem_ld32(lane_base + 256 + c * 32, r);
+        tmem_ld32(lane_base + 256 + half * 128 + c * 32, r);
         tmem_wait_ld();
         reg_fence32(r);
       } else {
@@ -409,7 +441,7 @@ __global__ void __launch_bounds__(192, 1)
           dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
     }
-    if (row_valid && slab == 0) {
+    if (row_valid && slab == 0 && half == 0) {
       const float lse = (l_run > 0.f) ? (m_run + __log2f(l_run)) * kLn2 : -INFINITY;
       p.lse[static_cast<int64_t>(si.b_coord) * p.lse_stride[0] +
             static_cast<int64_t>(head) * p.lse_stride[1] + si.q_base + q_idx] = lse;
@@ -418,7 +450,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kFwdProducerWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -432,7 +464,7 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   dim3 grid(num_q_heads, grid_x, slabs);
-  attn_fwd_kernel<DQK><<<grid, 192, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
+  attn_fwd_kernel<DQK><<<grid, kFwdThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
   return static_cast<int>(cudaGetLastError());
 }
 
