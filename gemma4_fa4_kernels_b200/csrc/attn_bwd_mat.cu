@@ -130,6 +130,11 @@ struct ScoreCfg {
   static constexpr int kExtraStages = kTS ? (MODE == kScoreFwd ? 1 : 2) : 0;
   static constexpr int kRingStages = kStages + kExtraStages;
   static constexpr int kPStages = 2;
+  // d256 S-and-dP pass: Q moves into TMEM (S = Q K^T as a TS MMA; dP = dO V^T
+  // stays SS with dO in shared memory), which frees Q's 64 KB of shared
+  // memory for one P and one dS staging slot.  TMEM: S double-buffered at
+  // b*128, Q at 256, dP single-buffered at 384.
+  static constexpr bool kQT = D == 256 && MODE == kScorePdS;
   // P tiles leave through a shared-memory staging slot and one bulk store
   // (a warp's direct 16-B row-chunk stores would touch 32 lines each).
   static constexpr bool kStageP = kTS && (MODE == kScoreP || MODE == kScoreFwd);
@@ -149,6 +154,7 @@ struct ScoreMisc {
   uint64_t drain;
   uint64_t stg_free[2];   // staging slot j & 1 read by tile j's bulk store
   uint64_t stg_ready[2];  // every math thread wrote tile j's chunks (slot parity j & 1)
+  uint64_t dp_free;       // single dP buffer read by every math thread (d256 PdS)
   uint32_t tmem_base;
   int abort;
 };
@@ -216,6 +222,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     mbar_init(&misc->stg_free[1], 1);
     mbar_init(&misc->stg_ready[0], kScoreMathThreads);
     mbar_init(&misc->stg_ready[1], kScoreMathThreads);
+    mbar_init(&misc->dp_free, kScoreMathThreads);
     misc->abort = 0;
     fence_mbar_init();
   }
@@ -231,8 +238,12 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   const int work = cap_ok ? n_kt : 0;
   // TMEM: PdS mode: buffer b holds S at b*256 and dP at b*256+128.  TS
   // variant: buffer b at b*128, the resident A operand (bf16 pairs) at 256.
-  auto s_col = [](int b) { return static_cast<uint32_t>(Cfg::kTS ? b * 128 : b * 256); };
-  auto dp_col = [](int b) { return static_cast<uint32_t>(Cfg::kTS ? b * 128 : b * 256 + 128); };
+  auto s_col = [](int b) {
+    return static_cast<uint32_t>(Cfg::kTS || Cfg::kQT ? b * 128 : b * 256);
+  };
+  auto dp_col = [](int b) {
+    return static_cast<uint32_t>(Cfg::kTS ? b * 128 : (Cfg::kQT ? 384 : b * 256 + 128));
+  };
   uint8_t* res_area = Cfg::kS ? q_s : do_s;
   // ring stage s: the first kStages in the ring area, the rest in the
   // resident area (usable once the resident operand has moved to TMEM)
@@ -279,7 +290,18 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     }
     __syncwarp();
   } else if (warp == kStoreWarp) {
-    if (lane == 0 && work > 0 && (Cfg::kStageP || Cfg::kStageDs)) {
+    if (lane == 0 && work > 0 && Cfg::kQT) {
+      // d256 PdS: one P and one dS slot in the former Q area, refilled per tile
+      bool ok = true;
+      for (int j = 0; j < work && ok; ++j) {
+        if (!(ok = mbar_wait(&misc->stg_ready[0], j & 1, ab, kDevTimeoutPeer))) break;
+        bulk_store(scratch_tile(p.p_tiles, p, head, t_off, j), q_s, kTileBytes);
+        bulk_store(scratch_tile(p.ds_tiles, p, head, t_off, j), q_s + 32768, kTileBytes);
+        bulk_store_wait_read();
+        mbar_arrive(&misc->stg_free[0]);
+      }
+      bulk_store_wait_all();
+    } else if (lane == 0 && work > 0 && (Cfg::kStageP || Cfg::kStageDs)) {
       // Store warp: once every math thread has written a tile into shared
       // memory, move it to HBM with one bulk store and hand the slot back
       // (the staging slot, or the dS pass's P slot to the producer).  The math
@@ -320,8 +342,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       constexpr uint32_t kId = idesc_bf16(128, 128, false, false);
       const uint32_t qb = smem_addr(q_s), db = smem_addr(do_s), rb = smem_addr(ring);
       uint32_t it = 0;
-      bool ok = Cfg::kTS ? mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer)
-                         : mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
+      bool ok = Cfg::kTS || Cfg::kQT ? mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer)
+                                     : mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
       for (int j = 0; j < work && ok; ++j) {
         const int b = j & 1;
         if (j >= 2 && !(ok = mbar_wait(&misc->buf_free[b], ((j - 2) >> 1) & 1, ab, kDevTimeoutPeer)))
@@ -331,8 +353,12 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
           if (!(ok = mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma))) break;
-          tc_fence_after();
           const bool is_k = Cfg::kS && c < D / 128;
+          // single dP buffer: tile j's dP waits until every math thread read tile j-1's
+          if (Cfg::kQT && c == D / 128 && j > 0 &&
+              !(ok = mbar_wait(&misc->dp_free, (j - 1) & 1, ab, kDevTimeoutPeer)))
+            break;
+          tc_fence_after();
           const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
           const uint32_t abase = is_k ? qb : db;
           const uint32_t dcol = is_k ? s_col(b) : dp_col(b);
@@ -341,7 +367,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           for (int kk = 0; kk < 8; ++kk) {
             const int gk = cc * 8 + kk;
             const uint64_t bdesc = sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-            if (Cfg::kTS)
+            if (Cfg::kTS || (Cfg::kQT && is_k))
               umma_ts(tmem + dcol, tmem + 256 + gk * 8, bdesc, kId, (cc | kk) != 0);
             else
               umma_ss(tmem + dcol, sdesc_sw128(abase + (gk >> 2) * 16384 + (gk & 3) * 32, 16, 1024),
@@ -374,9 +400,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     const int qa0 = qt * kTileM + q_off;
     const int qa1 = min((qt + 1) * kTileM, si.len_q) - 1 + q_off;
     bool ok = true;
-    if (Cfg::kTS && work > 0) {
+    if ((Cfg::kTS || Cfg::kQT) && work > 0) {
       // resident Q / dO (128-B swizzled rows) -> TMEM lane r, bf16 pairs from
-      // column 256; this warp copies K elements [256*(w/4), +256) of its rows.
+      // column 256; this warp copies K elements [D/4*(w/4), +D/4) of its rows.
       ok = mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
@@ -551,6 +577,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         if (c == c_begin + kChunksPerWarp - 1) {  // this warp's TMEM values are in registers
           tc_fence_before();
           mbar_arrive(&misc->buf_free[b]);
+          if (Cfg::kQT) mbar_arrive(&misc->dp_free);
         }
         float pv[32];
         if (MODE == kScoreDs) {
@@ -589,8 +616,14 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             }
           }
         }
+        if (Cfg::kQT && j > 0 && c == c_begin) {
+          // the staging slots are free once tile j-1's bulk stores have read them
+          if (ok) ok = mbar_wait(&misc->stg_free[0], (j - 1) & 1, ab, kDevTimeoutPeer);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+        }
         if (MODE != kScoreDs) {
-          uint8_t* pdst = Cfg::kStageP ? stg(j) : ptile;
+          uint8_t* pdst = Cfg::kQT ? q_s : (Cfg::kStageP ? stg(j) : ptile);
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 w;
@@ -607,7 +640,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           float dv[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) dv[i] = pv[i] * (__uint_as_float(dr[i]) - delta_r);
-          uint8_t* ddst = Cfg::kStageDs ? const_cast<uint8_t*>(psm) : dtile;
+          uint8_t* ddst = Cfg::kQT ? q_s + 32768 : (Cfg::kStageDs ? const_cast<uint8_t*>(psm) : dtile);
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 w;
@@ -619,11 +652,12 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           }
         }
       }
-      if (Cfg::kStageP || Cfg::kStageDs) {
+      if (Cfg::kStageP || Cfg::kStageDs || Cfg::kQT) {
         // this thread's chunks are written (dS over its P chunks in the dS
         // pass); the store lane moves the tile and frees the slot
+        if (!ok) continue;
         fence_proxy_async_smem();
-        mbar_arrive(&misc->stg_ready[j & 1]);
+        mbar_arrive(&misc->stg_ready[Cfg::kQT ? 0 : j & 1]);
       }
     }
   }
