@@ -677,13 +677,21 @@ enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2, kGemmO = 3 };
 
 // dQ CTAs produce all D output columns (A loaded once); dV / dK CTAs produce
 // one 256-column half each, which doubles the KV-major grid for load balance.
-template <int D, int WHICH>
+// PAIR (d512 dQ and forward O): the CTAs of a 2-CTA cluster take query heads
+// 2i and 2i+1 of one KV group for the same query tile, so they read the same K
+// (or V) rows.  Each CTA loads its own dS (or P) halves (A) and half of every
+// stage's K (V) columns (B), and the leader issues cta_group::2 MMAs with
+// M = 256: 48 KB per CTA and k-step instead of 80 KB, four ring stages instead
+// of two.  Forward O: the MMA pauses at the union of both heads' rescale
+// points; each CTA's correction warps rescale their own rows (if flagged) and
+// arrive on the leader's o_ready.
+template <int D, int WHICH, bool PAIR = false>
 struct GemmCfg {
   static constexpr bool kQMajor = WHICH >= 2;       // dQ and the forward O
   static constexpr int kNB = kQMajor ? D : 256;     // output columns per CTA
   static constexpr int kHalves = D / kNB;
   static constexpr int kABytes = 16384;             // 128 rows x 64 deep
-  static constexpr int kBBytes = 64 * kNB * 2;      // 64 deep x kNB
+  static constexpr int kBBytes = 64 * (PAIR ? kNB / 2 : kNB) * 2;  // 64 deep x (this CTA's) columns
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = kStageBytes > 64 * 1024 ? 2 : 4;
 };
@@ -708,11 +716,13 @@ struct GemmStep {
   int b_row;         // TMA token coordinate for B (first of 64 rows)
 };
 
-template <int D, int WHICH>
+template <int D, int WHICH, bool PAIR>
 __global__ void __launch_bounds__(192, 1)
     bwd_tile_gemm_kernel(const __grid_constant__ CUtensorMap tmB,
-                         const __grid_constant__ CUtensorMap tmOut, const MatParams p) {
-  using Cfg = GemmCfg<D, WHICH>;
+                         const __grid_constant__ CUtensorMap tmOut,
+                         const __grid_constant__ CUtensorMap tmA, const MatParams p) {
+  using Cfg = GemmCfg<D, WHICH, PAIR>;
+  static_assert(!PAIR || (Cfg::kQMajor && D == 512), "CTA pairs serve the d512 Q-major GEMMs");
   extern __shared__ __align__(1024) uint8_t smem[];
   if ((smem_addr(smem) & 1023u) != 0) {
     if (p.err) atomicCAS(p.err, 0, 5);
@@ -791,14 +801,24 @@ __global__ void __launch_bounds__(192, 1)
     }
     mbar_init(&misc->acc_full, 1);
     mbar_init(&misc->o_done, 1);
-    mbar_init(&misc->o_ready, 128);
+    mbar_init(&misc->o_ready, PAIR ? 8 : 128);  // pair: one arrival per correction warp of each CTA
     mbar_init(&misc->drain, 1);
     misc->abort = 0;
     fence_mbar_init();
   }
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0;  // 0: pair leader (or no pair)
+  if (PAIR) {
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
+  }
   if (warp == 4) {
-    tmem_alloc(&misc->tmem_base, 512);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(&misc->tmem_base, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&misc->tmem_base, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -832,6 +852,22 @@ __global__ void __launch_bounds__(192, 1)
           ++it;
           if (!(ok = mbar_wait(&misc->empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
           uint8_t* dst = smem + st * Cfg::kStageBytes;
+          if (PAIR) {
+            // this CTA's dS half (one 16 KB box of the byte view of the scratch)
+            // and its two 128-column slices of the 64 K rows (one per 256-wide
+            // MMA); both CTAs' bytes complete on the leader's barrier
+            if (crank == 0) mbar_expect_tx(&misc->full[st], 2 * Cfg::kStageBytes);
+            const uint32_t lbar = mapa_shared(&misc->full[st], 0);
+            const uint8_t* abase = WHICH == kGemmO ? p.p_tiles : p.ds_tiles;
+            const int half_idx = static_cast<int>((t - abase) / 16384) + h;
+            tma_load_3d_pair(dst, &tmA, lbar, 0, 0, half_idx);
+            for (int nh = 0; nh < 2; ++nh)
+              for (int bx = 0; bx < 2; ++bx)
+                tma_load_4d_pair(dst + Cfg::kABytes + (nh * 2 + bx) * 8192, &tmB, lbar,
+                                 nh * 256 + static_cast<int>(crank) * 128 + bx * 64, b_head,
+                                 b_row + h * 64, si.b_coord);
+            continue;
+          }
           mbar_expect_tx(&misc->full[st], Cfg::kStageBytes);
           if (Cfg::kQMajor) {
             bulk_load(dst, t + h * 16384, 16384, &misc->full[st]);
@@ -853,15 +889,55 @@ __global__ void __launch_bounds__(192, 1)
       // per tile on the MMA issue path would stall the tensor pipe
       const int4 rg = p.ranges[qg];
       const int64_t flag_base = static_cast<int64_t>(head) * p.head_cap_tiles + rg.z;
+      const int64_t peer_base = static_cast<int64_t>(head ^ 1) * p.head_cap_tiles + rg.z;
       for (int w0 = 0; w0 < (rg.y + 31) / 32 && w0 < 64; ++w0) {
         const int j = w0 * 32 + lane;
-        const bool f = j < rg.y && p.fwd_flags[flag_base + j] != 0;
+        const bool f = j < rg.y && (p.fwd_flags[flag_base + j] != 0 ||
+                                    (PAIR && p.fwd_flags[peer_base + j] != 0));
         const uint32_t bits = __ballot_sync(0xffffffffu, f);
         if (lane == 0) misc->flag_bits[w0] = bits;
       }
       __syncwarp();
     }
-    if (lane == 0 && n_steps > 0) {
+    if (PAIR) {
+      if (lane == 0 && n_steps > 0 && crank == 0) {
+        // leader: M = 256 (both CTAs' query rows), N = 256 per MMA (128
+        // columns from each CTA's stage)
+        constexpr uint32_t kId = idesc_bf16(256, 256, false, true);
+        const uint32_t sb0 = smem_addr(smem);
+        bool ok = true;
+        int events = 0;
+        for (int it = 0; it < n_steps && ok; ++it) {
+          const int tj = it >> 1;  // scratch tile of this half-step
+          if (WHICH == kGemmO && (it & 1) == 0 && tj > 0 &&
+              ((misc->flag_bits[(tj >> 5) & 63] >> (tj & 31)) & 1u)) {
+            // both CTAs' correction warps rescale O once every earlier product completed
+            umma_commit_pair_both(&misc->o_done);
+            if (!(ok = mbar_wait_cluster(&misc->o_ready, events & 1, ab, kDevTimeoutPeer))) break;
+            tc_fence_after();
+            ++events;
+          }
+          const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+          if (!(ok = mbar_wait(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
+          tc_fence_after();
+          const uint32_t a = sb0 + st * Cfg::kStageBytes;
+          const uint32_t bb = a + Cfg::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t adesc = sdesc_sw128(a + kk * 32, 16, 1024);
+#pragma unroll
+            for (int nh = 0; nh < 2; ++nh)
+              umma_ss_pair(tmem + nh * 256, adesc,
+                           sdesc_sw128(bb + nh * 16384 + kk * 2048, 8192, 1024), kId,
+                           !(it == 0 && kk == 0));
+          }
+          umma_commit_pair_both(&misc->empty[st]);
+        }
+        umma_commit_pair_both(&misc->acc_full);
+        umma_commit_pair_both(&misc->drain);
+        mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+      }
+    } else if (lane == 0 && n_steps > 0) {
       constexpr uint32_t kId = idesc_bf16(128, 256, !Cfg::kQMajor, true);
       const uint32_t sb0 = smem_addr(smem);
       uint32_t it = 0;
@@ -912,9 +988,10 @@ __global__ void __launch_bounds__(192, 1)
       // correction: apply the forward's lazy rescale factors at flagged tiles
       const int4 rg = p.ranges[qg];
       const int64_t tile_base = static_cast<int64_t>(head) * p.head_cap_tiles + rg.z;
+      const int64_t peer_base = static_cast<int64_t>(head ^ 1) * p.head_cap_tiles + rg.z;
       int events = 0;
       for (int j = 1; j < rg.y && ok; ++j) {
-        if (!p.fwd_flags[tile_base + j]) continue;
+        if (!p.fwd_flags[tile_base + j] && !(PAIR && p.fwd_flags[peer_base + j])) continue;
         ok = mbar_wait(&misc->o_done, events & 1, ab, kDevTimeoutMma);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
@@ -940,7 +1017,12 @@ __global__ void __launch_bounds__(192, 1)
           tmem_wait_st();
         }
         tc_fence_before();
-        mbar_arrive(&misc->o_ready);
+        if (PAIR) {  // one arrival per warp on the leader's barrier
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(&misc->o_ready, 0));
+        } else {
+          mbar_arrive(&misc->o_ready);
+        }
         ++events;
       }
     }
@@ -1036,9 +1118,13 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // the peer's MMAs into this CTA's TMEM are complete
   if (warp == 4) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if (PAIR)
+      tmem_dealloc_pair(tmem, 512);
+    else
+      tmem_dealloc(tmem, 512);
   }
 }
 
@@ -1073,34 +1159,61 @@ int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& 
   return launch_score_impl<512, kScoreDs>(tq, tk, tv, tdo, p, grid_x, stream);
 }
 
-template <int D, int WHICH>
-static int launch_gemm_impl(const CUtensorMap& tb, const CUtensorMap& tout, const MatParams& p,
-                            int grid_x, int grid_y, cudaStream_t stream) {
-  using Cfg = GemmCfg<D, WHICH>;
+template <int D, int WHICH, bool PAIR = false>
+static int launch_gemm_impl(const CUtensorMap& tb, const CUtensorMap& tout, const CUtensorMap& ta,
+                            const MatParams& p, int grid_x, int grid_y, cudaStream_t stream) {
+  using Cfg = GemmCfg<D, WHICH, PAIR>;
   if (!Cfg::kQMajor) {  // KV-major: (key tile, KV head, half) all along x
     grid_x *= grid_y * Cfg::kHalves;
     grid_y = 1;
   }
   const int smem = Cfg::kStages * Cfg::kStageBytes + sizeof(GemmMisc);
-  cudaError_t e = cudaFuncSetAttribute(bwd_tile_gemm_kernel<D, WHICH>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  auto kernel = bwd_tile_gemm_kernel<D, WHICH, PAIR>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid = Cfg::kQMajor ? dim3(grid_y, grid_x) : dim3(grid_x, grid_y);
-  bwd_tile_gemm_kernel<D, WHICH><<<grid, 192, smem, stream>>>(tb, tout, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = Cfg::kQMajor ? dim3(grid_y, grid_x) : dim3(grid_x, grid_y);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (PAIR) {  // query heads 2i, 2i+1 (grid x) form a cluster
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  e = cudaLaunchKernelEx(&cfg, kernel, tb, tout, ta, p);
+  if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }
 
+bool gemm_pairs_ok(int d, int which, const MatParams& p) {
+  return d == 512 && (which == kGemmDq || which == kGemmO) && (p.group % 2) == 0 &&
+         (p.num_q_heads % 2) == 0;
+}
+
 int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const CUtensorMap& tout,
-                         const MatParams& p, int grid_x, int grid_y, cudaStream_t stream) {
+                         const CUtensorMap* ta, const MatParams& p, int grid_x, int grid_y,
+                         cudaStream_t stream) {
+  const CUtensorMap& a = ta ? *ta : tb;  // only read by the pair variant
   if (d == 256) {
-    if (which == kGemmDv) return launch_gemm_impl<256, kGemmDv>(tb, tout, p, grid_x, grid_y, stream);
-    if (which == kGemmDk) return launch_gemm_impl<256, kGemmDk>(tb, tout, p, grid_x, grid_y, stream);
-    return launch_gemm_impl<256, kGemmDq>(tb, tout, p, grid_x, grid_y, stream);
+    if (which == kGemmDv) return launch_gemm_impl<256, kGemmDv>(tb, tout, a, p, grid_x, grid_y, stream);
+    if (which == kGemmDk) return launch_gemm_impl<256, kGemmDk>(tb, tout, a, p, grid_x, grid_y, stream);
+    return launch_gemm_impl<256, kGemmDq>(tb, tout, a, p, grid_x, grid_y, stream);
   }
-  if (which == kGemmDv) return launch_gemm_impl<512, kGemmDv>(tb, tout, p, grid_x, grid_y, stream);
-  if (which == kGemmDk) return launch_gemm_impl<512, kGemmDk>(tb, tout, p, grid_x, grid_y, stream);
-  if (which == kGemmO) return launch_gemm_impl<512, kGemmO>(tb, tout, p, grid_x, grid_y, stream);
-  return launch_gemm_impl<512, kGemmDq>(tb, tout, p, grid_x, grid_y, stream);
+  if (which == kGemmDv) return launch_gemm_impl<512, kGemmDv>(tb, tout, a, p, grid_x, grid_y, stream);
+  if (which == kGemmDk) return launch_gemm_impl<512, kGemmDk>(tb, tout, a, p, grid_x, grid_y, stream);
+  if (which == kGemmO) {
+    if (ta && gemm_pairs_ok(d, which, p))
+      return launch_gemm_impl<512, kGemmO, true>(tb, tout, *ta, p, grid_x, grid_y, stream);
+    return launch_gemm_impl<512, kGemmO>(tb, tout, a, p, grid_x, grid_y, stream);
+  }
+  if (ta && gemm_pairs_ok(d, which, p))
+    return launch_gemm_impl<512, kGemmDq, true>(tb, tout, *ta, p, grid_x, grid_y, stream);
+  return launch_gemm_impl<512, kGemmDq>(tb, tout, a, p, grid_x, grid_y, stream);
 }
 
 }  // namespace g4

@@ -139,6 +139,23 @@ int make_map(CUtensorMap* map, const void* ptr, int64_t d, int64_t h, int64_t s,
   return G4_OK;
 }
 
+// Scratch tiles viewed as bytes: (256, 64, n_half) with (256, 64, 1) boxes, one
+// box per 16 KB half of a 32 KB pre-swizzled tile (copied as is, no swizzle).
+int make_scratch_map(CUtensorMap* map, const void* ptr, int64_t n_half) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(G4_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {256, 64, (cuuint64_t)(n_half > 0 ? n_half : 1)};
+  cuuint64_t strides[2] = {256, 16384};
+  cuuint32_t box[3] = {256, 64, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(G4_ERR_INVALID, "scratch tensor map encoding failed (CUresult %d)", (int)r);
+  return G4_OK;
+}
+
 // ---------------------------------------------------------------------------------------
 // argument checks shared by forward and backward
 // ---------------------------------------------------------------------------------------
@@ -621,7 +638,13 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
       return rc;
     {
       LaunchScope ls(kKFwdPv, st);
-      e = g4::launch_bwd_tile_gemm(D, 3, tv64, to128, m, w.n_qt_total, a->num_q_heads, st);
+      CUtensorMap tp;  // the P scratch as bytes: the d512 O = P V GEMM runs as CTA pairs
+      const bool pairs = g4::gemm_pairs_ok(D, 3, m);
+      if (pairs && (rc = make_scratch_map(&tp, m.p_tiles,
+                                          2 * int64_t(a->num_q_heads) * w.head_cap_tiles)))
+        return rc;
+      e = g4::launch_bwd_tile_gemm(D, 3, tv64, to128, pairs ? &tp : nullptr, m, w.n_qt_total,
+                                   a->num_q_heads, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward PV launch");
     }
     return G4_OK;
@@ -771,17 +794,23 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     }
     {
       LaunchScope ls(kKGemmDv, st);
-      e = g4::launch_bwd_tile_gemm(D, 0, tdo64, tdv128, m, gk, a->num_kv_heads, st);
+      e = g4::launch_bwd_tile_gemm(D, 0, tdo64, tdv128, nullptr, m, gk, a->num_kv_heads, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV launch");
     }
     {
       LaunchScope ls(kKGemmDk, st);
-      e = g4::launch_bwd_tile_gemm(D, 1, tq64, tdk128, m, gk, a->num_kv_heads, st);
+      e = g4::launch_bwd_tile_gemm(D, 1, tq64, tdk128, nullptr, m, gk, a->num_kv_heads, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK launch");
     }
     {
       LaunchScope ls(kKGemmDq, st);
-      e = g4::launch_bwd_tile_gemm(D, 2, tk64, tdq128, m, w.n_qt_total, a->num_q_heads, st);
+      CUtensorMap tds;  // the dS scratch as bytes: the d512 dQ GEMM runs as CTA pairs
+      const bool pairs = g4::gemm_pairs_ok(D, 2, m);
+      if (pairs && (rc = make_scratch_map(&tds, m.ds_tiles,
+                                          2 * int64_t(a->num_q_heads) * w.head_cap_tiles)))
+        return rc;
+      e = g4::launch_bwd_tile_gemm(D, 2, tk64, tdq128, pairs ? &tds : nullptr, m, w.n_qt_total,
+                                   a->num_q_heads, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "dQ launch");
     }
     return G4_OK;

@@ -160,8 +160,13 @@ int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& 
                      cudaStream_t stream);
 // which: 0 = dV (B = dO), 1 = dK (B = Q), 2 = dQ (B = K), 3 = forward O = P V
 // (B = V); tb uses 64-row boxes, tout (the output: dV, dK, dQ or O) 128-row boxes.
+// ta (nullable): the A scratch (dS for dQ, P for O) viewed as bytes, (256, 64,
+// half tiles) with (256, 64, 1) boxes; given it, the d512 dQ and O GEMMs run as
+// CTA pairs.
 int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const CUtensorMap& tout,
-                         const MatParams& p, int grid_x, int grid_y, cudaStream_t stream);
+                         const CUtensorMap* ta, const MatParams& p, int grid_x, int grid_y,
+                         cudaStream_t stream);
+bool gemm_pairs_ok(int d, int which, const MatParams& p);
 
 template <int DQK>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
