@@ -155,7 +155,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 }
 
 // ------------------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA: every load delivers into the issuing CTA's own shared memory
 // ------------------------------------------------------------------------------------
 // Pair forms of the tiled loads: the box lands in this CTA's shared memory and
 // its bytes complete on the leader CTA's mbarrier (`leader_bar`, a
@@ -346,13 +346,16 @@ __device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, u
       : "memory");
 }
 // Arrive once on `bar` in both CTAs of the pair when every pair MMA previously
-// issued by this thread completes.
+// issued by this thread completes (called by the leader: one commit on its own
+// barrier, one on the peer CTA's copy through its shared::cluster address).
 __device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
   asm volatile(
-      "{\n\t.reg .b16 m;\n\t"
-      "mov.b16 m, 3;\n\t"
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
-      "[%0], m;\n\t}" ::"r"(smem_addr(bar))
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_addr(bar))
+      : "memory");
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          mapa_shared(bar, 1))
       : "memory");
 }
 
