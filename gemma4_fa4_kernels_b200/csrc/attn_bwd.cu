@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(192, 1)
   BwdMisc* misc = reinterpret_cast<BwdMisc*>(ring + kBwdStages * kStageBytes);
 
   const int tid = threadIdx.x;
-  const int warp = tid >> 5;
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);  // provably warp-uniform
   const int lane = tid & 31;
   const int head = blockIdx.y;
   const int slab = blockIdx.z;
@@ -305,19 +305,21 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0 && n_kt > 0) {
+    // the whole warp runs the issue loop (warp-uniform waits, one elected
+    // lane per MMA): see mbar_wait_warp
+    if (n_kt > 0) {
       constexpr uint32_t kIdS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t kIdQ = idesc_bf16(128, 256, false, true);
       const uint32_t qb = smem_addr(q_s);
       const uint32_t db = smem_addr(do_s);
       const uint32_t rb = smem_addr(ring);
       uint32_t it = 0;
-      bool ok = mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
+      bool ok = mbar_wait_warp(&misc->res_full, 0, ab, kDevTimeoutTma);
       auto take = [&]() -> int {
         const uint32_t st = it % kBwdStages;
         const uint32_t ph = (it / kBwdStages) & 1;
         ++it;
-        if (!mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma)) {
+        if (!mbar_wait_warp(&misc->ring_full[st], ph, ab, kDevTimeoutTma)) {
           ok = false;
           return -1;
         }
@@ -333,11 +335,11 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const int g = c * 8 + kk;
-            umma_ss(tmem, sdesc_sw128(qb + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024),
+            umma_ss_w(tmem, sdesc_sw128(qb + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024),
                     sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), kIdS,
                     (c | kk) != 0);
           }
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
         }
         // dP = dO V^T
         for (int c = 0; c < Cfg::kPChunks && ok; ++c) {
@@ -348,21 +350,21 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
               const int g = c * 8 + kk;
-              umma_ss(tmem + 128, sdesc_sw128(db + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024),
+              umma_ss_w(tmem + 128, sdesc_sw128(db + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024),
                       sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), kIdS,
                       (c | kk) != 0);
             }
           } else {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_ss(tmem + 128, sdesc_sw128(sb + kk * 32, 16, 1024),
+              umma_ss_w(tmem + 128, sdesc_sw128(sb + kk * 32, 16, 1024),
                       sdesc_sw128(sb + 16384 + kk * 32, 16, 1024), kIdS, (c | kk) != 0);
           }
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
         }
-        umma_commit(&misc->s_full);
+        umma_commit_w(&misc->s_full);
         if (!ok) break;
-        if (!(ok = mbar_wait(&misc->ds_full, j & 1, ab, kDevTimeoutPeer))) break;
+        if (!(ok = mbar_wait_warp(&misc->ds_full, j & 1, ab, kDevTimeoutPeer))) break;
         tc_fence_after();
         // dQ += dS K   (dS: bf16 pairs in TMEM columns [0,64))
         for (int h = 0; h < 2 && ok; ++h) {
@@ -371,14 +373,14 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t sb = rb + st * kStageBytes;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_ts(tmem + 256, tmem + h * 32 + kk * 8, sdesc_sw128(sb + kk * 2048, 8192, 1024),
+            umma_ts_w(tmem + 256, tmem + h * 32 + kk * 8, sdesc_sw128(sb + kk * 2048, 8192, 1024),
                     kIdQ, (j | h | kk) != 0);
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
         }
-        umma_commit(&misc->step_done);
+        umma_commit_w(&misc->step_done);
       }
-      umma_commit(&misc->drain);
-      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+      umma_commit_w(&misc->drain);
+      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
@@ -512,7 +514,7 @@ __global__ void __launch_bounds__(192, 1)
   BwdMisc* misc = reinterpret_cast<BwdMisc*>(ring + kBwdStages * kStageBytes);
 
   const int tid = threadIdx.x;
-  const int warp = tid >> 5;
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);  // provably warp-uniform
   const int lane = tid & 31;
   const int kv_head = blockIdx.y;
   const int slab = blockIdx.z;
@@ -649,19 +651,21 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0 && n_steps > 0) {
+    // the whole warp runs the issue loop (warp-uniform waits, one elected
+    // lane per MMA): see mbar_wait_warp
+    if (n_steps > 0) {
       constexpr uint32_t kIdS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t kIdAcc = idesc_bf16(128, 128, false, true);
       const uint32_t kb = smem_addr(k_s);
       const uint32_t vb = smem_addr(v_s);
       const uint32_t rb = smem_addr(ring);
       uint32_t it = 0;
-      bool ok = mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
+      bool ok = mbar_wait_warp(&misc->res_full, 0, ab, kDevTimeoutTma);
       auto take = [&]() -> int {
         const uint32_t st = it % kBwdStages;
         const uint32_t ph = (it / kBwdStages) & 1;
         ++it;
-        if (!mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma)) {
+        if (!mbar_wait_warp(&misc->ring_full[st], ph, ab, kDevTimeoutTma)) {
           ok = false;
           return -1;
         }
@@ -677,11 +681,11 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const int g = c * 8 + kk;
-            umma_ss(tmem, sdesc_sw128(kb + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024),
+            umma_ss_w(tmem, sdesc_sw128(kb + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024),
                     sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), kIdS,
                     (c | kk) != 0);
           }
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
         }
         // dP^T = V dO^T
         for (int c = 0; c < Cfg::kPChunks && ok; ++c) {
@@ -692,21 +696,21 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
               const int g = c * 8 + kk;
-              umma_ss(tmem + 128, sdesc_sw128(vb + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024),
+              umma_ss_w(tmem + 128, sdesc_sw128(vb + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024),
                       sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), kIdS,
                       (c | kk) != 0);
             }
           } else {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_ss(tmem + 128, sdesc_sw128(sb + kk * 32, 16, 1024),
+              umma_ss_w(tmem + 128, sdesc_sw128(sb + kk * 32, 16, 1024),
                       sdesc_sw128(sb + 16384 + kk * 32, 16, 1024), kIdS, (c | kk) != 0);
           }
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
         }
-        umma_commit(&misc->s_full);
+        umma_commit_w(&misc->s_full);
         if (!ok) break;
-        if (!(ok = mbar_wait(&misc->ds_full, step & 1, ab, kDevTimeoutPeer))) break;
+        if (!(ok = mbar_wait_warp(&misc->ds_full, step & 1, ab, kDevTimeoutPeer))) break;
         tc_fence_after();
         // dV += P^T dO[:, slab]
         {
@@ -715,9 +719,9 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t sb = rb + st * kStageBytes;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_ts(tmem + 256, tmem + kk * 8, sdesc_sw128(sb + kk * 2048, 16384, 1024), kIdAcc,
+            umma_ts_w(tmem + 256, tmem + kk * 8, sdesc_sw128(sb + kk * 2048, 16384, 1024), kIdAcc,
                     (step | kk) != 0);
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
         }
         // dK += dS^T Q[:, slab]
         {
@@ -726,14 +730,14 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t sb = rb + st * kStageBytes;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_ts(tmem + 384, tmem + 128 + kk * 8, sdesc_sw128(sb + kk * 2048, 16384, 1024),
+            umma_ts_w(tmem + 384, tmem + 128 + kk * 8, sdesc_sw128(sb + kk * 2048, 16384, 1024),
                     kIdAcc, (step | kk) != 0);
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
         }
-        umma_commit(&misc->step_done);
+        umma_commit_w(&misc->step_done);
       }
-      umma_commit(&misc->drain);
-      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+      umma_commit_w(&misc->drain);
+      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {

@@ -187,7 +187,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   uint8_t* ring = do_s + Cfg::kDoBytes;
   ScoreMisc* misc = reinterpret_cast<ScoreMisc*>(ring + Cfg::kStages * 32768);
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // warp index through a shuffle: provably warp-uniform for the compiler
+  const int tid = threadIdx.x, warp = __shfl_sync(0xffffffffu, tid >> 5, 0), lane = tid & 31;
   // grid (heads, query tiles): the head index varies fastest in launch order, so
   // every head's longest causal rows are dispatched first (longest-first over
   // the whole grid, which keeps the tail of the launch short)
@@ -338,25 +339,28 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
-    if (lane == 0 && work > 0) {
+    // the whole warp runs the issue loop (warp-uniform waits, one elected lane
+    // per MMA): see mbar_wait_warp
+    if (work > 0) {
       constexpr uint32_t kId = idesc_bf16(128, 128, false, false);
-      const uint32_t qb = smem_addr(q_s), db = smem_addr(do_s), rb = smem_addr(ring);
+      const uint32_t qb = smem_addr(q_s), db = smem_addr(do_s);
       uint32_t it = 0;
-      bool ok = Cfg::kTS || Cfg::kQT ? mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer)
-                                     : mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
+      bool ok = Cfg::kTS || Cfg::kQT ? mbar_wait_warp(&misc->a_ready, 0, ab, kDevTimeoutPeer)
+                                     : mbar_wait_warp(&misc->res_full, 0, ab, kDevTimeoutTma);
       for (int j = 0; j < work && ok; ++j) {
         const int b = j & 1;
-        if (j >= 2 && !(ok = mbar_wait(&misc->buf_free[b], ((j - 2) >> 1) & 1, ab, kDevTimeoutPeer)))
+        if (j >= 2 &&
+            !(ok = mbar_wait_warp(&misc->buf_free[b], ((j - 2) >> 1) & 1, ab, kDevTimeoutPeer)))
           break;
         tc_fence_after();
         for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
           const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
-          if (!(ok = mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma))) break;
+          if (!(ok = mbar_wait_warp(&misc->ring_full[st], ph, ab, kDevTimeoutTma))) break;
           const bool is_k = Cfg::kS && c < D / 128;
           // single dP buffer: tile j's dP waits until every math thread read tile j-1's
           if (Cfg::kQT && c == D / 128 && j > 0 &&
-              !(ok = mbar_wait(&misc->dp_free, (j - 1) & 1, ab, kDevTimeoutPeer)))
+              !(ok = mbar_wait_warp(&misc->dp_free, (j - 1) & 1, ab, kDevTimeoutPeer)))
             break;
           tc_fence_after();
           const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
@@ -368,17 +372,18 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             const int gk = cc * 8 + kk;
             const uint64_t bdesc = sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
             if (Cfg::kTS || (Cfg::kQT && is_k))
-              umma_ts(tmem + dcol, tmem + 256 + gk * 8, bdesc, kId, (cc | kk) != 0);
+              umma_ts_w(tmem + dcol, tmem + 256 + gk * 8, bdesc, kId, (cc | kk) != 0);
             else
-              umma_ss(tmem + dcol, sdesc_sw128(abase + (gk >> 2) * 16384 + (gk & 3) * 32, 16, 1024),
-                      bdesc, kId, (cc | kk) != 0);
+              umma_ss_w(tmem + dcol,
+                        sdesc_sw128(abase + (gk >> 2) * 16384 + (gk & 3) * 32, 16, 1024), bdesc,
+                        kId, (cc | kk) != 0);
           }
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
         }
-        umma_commit(&misc->s_full[b]);
+        umma_commit_w(&misc->s_full[b]);
       }
-      umma_commit(&misc->drain);
-      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+      umma_commit_w(&misc->drain);
+      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
@@ -729,7 +734,8 @@ __global__ void __launch_bounds__(192, 1)
     return;
   }
   GemmMisc* misc = reinterpret_cast<GemmMisc*>(smem + Cfg::kStages * Cfg::kStageBytes);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // warp index through a shuffle: provably warp-uniform for the compiler
+  const int tid = threadIdx.x, warp = __shfl_sync(0xffffffffu, tid >> 5, 0), lane = tid & 31;
   const bool packed = p.layout.packed();
   const int G = p.group;
 
@@ -899,8 +905,10 @@ __global__ void __launch_bounds__(192, 1)
       }
       __syncwarp();
     }
+    // the MMA issue loops run on the whole warp (warp-uniform waits, one
+    // elected lane per MMA): see mbar_wait_warp
     if (PAIR) {
-      if (lane == 0 && n_steps > 0 && crank == 0) {
+      if (n_steps > 0 && crank == 0) {
         // leader: M = 256 (both CTAs' query rows), N = 256 per MMA (128
         // columns from each CTA's stage)
         constexpr uint32_t kId = idesc_bf16(256, 256, false, true);
@@ -912,13 +920,14 @@ __global__ void __launch_bounds__(192, 1)
           if (WHICH == kGemmO && (it & 1) == 0 && tj > 0 &&
               ((misc->flag_bits[(tj >> 5) & 63] >> (tj & 31)) & 1u)) {
             // both CTAs' correction warps rescale O once every earlier product completed
-            umma_commit_pair_both(&misc->o_done);
-            if (!(ok = mbar_wait_cluster(&misc->o_ready, events & 1, ab, kDevTimeoutPeer))) break;
+            umma_commit_pair_both_w(&misc->o_done);
+            if (!(ok = mbar_wait_cluster_warp(&misc->o_ready, events & 1, ab, kDevTimeoutPeer)))
+              break;
             tc_fence_after();
             ++events;
           }
           const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
-          if (!(ok = mbar_wait(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
+          if (!(ok = mbar_wait_warp(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
           tc_fence_after();
           const uint32_t a = sb0 + st * Cfg::kStageBytes;
           const uint32_t bb = a + Cfg::kABytes;
@@ -927,17 +936,17 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t adesc = sdesc_sw128(a + kk * 32, 16, 1024);
 #pragma unroll
             for (int nh = 0; nh < 2; ++nh)
-              umma_ss_pair(tmem + nh * 256, adesc,
-                           sdesc_sw128(bb + nh * 16384 + kk * 2048, 8192, 1024), kId,
-                           !(it == 0 && kk == 0));
+              umma_ss_pair_w(tmem + nh * 256, adesc,
+                             sdesc_sw128(bb + nh * 16384 + kk * 2048, 8192, 1024), kId,
+                             !(it == 0 && kk == 0));
           }
-          umma_commit_pair_both(&misc->empty[st]);
+          umma_commit_pair_both_w(&misc->empty[st]);
         }
-        umma_commit_pair_both(&misc->acc_full);
-        umma_commit_pair_both(&misc->drain);
-        mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+        umma_commit_pair_both_w(&misc->acc_full);
+        umma_commit_pair_both_w(&misc->drain);
+        mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
       }
-    } else if (lane == 0 && n_steps > 0) {
+    } else if (n_steps > 0) {
       constexpr uint32_t kId = idesc_bf16(128, 256, !Cfg::kQMajor, true);
       const uint32_t sb0 = smem_addr(smem);
       uint32_t it = 0;
@@ -948,8 +957,9 @@ __global__ void __launch_bounds__(192, 1)
         // correction warps rescale O once every earlier product completed
         if (WHICH == kGemmO && tile_j > 0 &&
             ((misc->flag_bits[(tile_j >> 5) & 63] >> (tile_j & 31)) & 1u)) {
-          umma_commit(&misc->o_done);
-          if (!(ok = mbar_wait(&misc->o_ready, events & 1, ab, kDevTimeoutPeer))) return false;
+          umma_commit_w(&misc->o_done);
+          if (!(ok = mbar_wait_warp(&misc->o_ready, events & 1, ab, kDevTimeoutPeer)))
+            return false;
           tc_fence_after();
           ++events;
         }
@@ -958,7 +968,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
           const uint32_t first = it == 0;
           ++it;
-          if (!(ok = mbar_wait(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
+          if (!(ok = mbar_wait_warp(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
           tc_fence_after();
           const uint32_t a = sb0 + st * Cfg::kStageBytes;
           const uint32_t bb = a + Cfg::kABytes;
@@ -968,16 +978,17 @@ __global__ void __launch_bounds__(192, 1)
                                                 : sdesc_sw128(a + kk * 2048, 8192, 1024);
 #pragma unroll
             for (int nh = 0; nh < Cfg::kNB / 256; ++nh)
-              umma_ss(tmem + nh * 256, adesc, sdesc_sw128(bb + nh * 32768 + kk * 2048, 8192, 1024),
-                      kId, !(first && kk == 0));
+              umma_ss_w(tmem + nh * 256, adesc,
+                        sdesc_sw128(bb + nh * 32768 + kk * 2048, 8192, 1024), kId,
+                        !(first && kk == 0));
           }
-          umma_commit(&misc->empty[st]);
+          umma_commit_w(&misc->empty[st]);
         }
         return ok;
       });
-      umma_commit(&misc->acc_full);
-      umma_commit(&misc->drain);
-      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+      umma_commit_w(&misc->acc_full);
+      umma_commit_w(&misc->drain);
+      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {

@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(192, 1)
   DecMisc* misc = reinterpret_cast<DecMisc*>(p_s + 2 * kPBufBytes);
 
   const int tid = threadIdx.x;
-  const int warp = tid >> 5;
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);  // provably warp-uniform
   const int lane = tid & 31;
   const int split = blockIdx.x;
   const int kv_head = blockIdx.y;
@@ -174,24 +174,27 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else if (warp == 5) {
     // ============================ MMA issuer ============================
-    if (lane == 0 && n > 0) {
+    // the whole warp runs the issue loop (warp-uniform waits, one elected
+    // lane per MMA): see mbar_wait_warp
+    if (n > 0) {
       constexpr uint32_t kIdS = idesc_bf16(128, 16, false, false);
       constexpr uint32_t kIdO = idesc_bf16(128, 16, true, false);
       const uint32_t ring_b = smem_addr(ring);
       const uint32_t q_b = smem_addr(q_s);
       const uint32_t p_b = smem_addr(p_s);
       uint32_t it = 0;
-      bool ok = mbar_wait(&misc->q_ready, 0, ab, kDevTimeoutPeer);
+      bool ok = mbar_wait_warp(&misc->q_ready, 0, ab, kDevTimeoutPeer);
       auto take = [&](uint32_t& stage) -> bool {
         stage = it % kDecodeStages;
         const uint32_t ph = (it / kDecodeStages) & 1;
-        if (!mbar_wait(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
+        if (!mbar_wait_warp(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
         tc_fence_after();
         return true;
       };
       auto issue_s = [&](int u) {
         const int b = u & 1;
-        if (!(ok = mbar_wait(&misc->s_empty[b], ((u >> 1) & 1) ^ 1, ab, kDevTimeoutPeer))) return;
+        if (!(ok = mbar_wait_warp(&misc->s_empty[b], ((u >> 1) & 1) ^ 1, ab, kDevTimeoutPeer)))
+          return;
         tc_fence_after();
         const uint32_t d = tmem + b * 16;
         for (int c = 0; c < Cfg::kChunks && ok; ++c) {
@@ -203,12 +206,12 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t a = sdesc_sw128(kb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
             const uint64_t bq =
                 sdesc_sw128(q_b + (2 * c + (kk >> 2)) * 2048 + (kk & 3) * 32, 16, 1024);
-            umma_ss(d, a, bq, kIdS, (c | kk) != 0);
+            umma_ss_w(d, a, bq, kIdS, (c | kk) != 0);
           }
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
           ++it;
         }
-        umma_commit(&misc->s_full[b]);
+        umma_commit_w(&misc->s_full[b]);
       };
       auto issue_o = [&](int u) {
         const int b = u & 1;
@@ -221,24 +224,25 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t a = sdesc_sw128(vb + kk * 2048, 16384, 1024);
             const uint64_t bp =
                 sdesc_sw128(p_b + b * kPBufBytes + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024);
-            umma_ss(tmem + 32 + c * 16, a, bp, kIdO, (u | kk) != 0);
+            umma_ss_w(tmem + 32 + c * 16, a, bp, kIdO, (u | kk) != 0);
           }
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
           ++it;
         }
-        umma_commit(&misc->p_free[b]);
+        umma_commit_w(&misc->p_free[b]);
       };
       if (ok) issue_s(0);
       for (int u = 0; u < n && ok; ++u) {
         if (u + 1 < n) issue_s(u + 1);
         if (!ok) break;
-        if (!(ok = mbar_wait(&misc->p_full[u & 1], (u >> 1) & 1, ab, kDevTimeoutPeer))) break;
+        if (!(ok = mbar_wait_warp(&misc->p_full[u & 1], (u >> 1) & 1, ab, kDevTimeoutPeer)))
+          break;
         tc_fence_after();
         issue_o(u);
       }
-      // Drain: every MMA this thread issued has completed before TMEM is freed.
-      umma_commit(&misc->drain);
-      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+      // Drain: every MMA this warp issued has completed before TMEM is freed.
+      umma_commit_w(&misc->drain);
+      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {

@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   FwdMisc* misc = reinterpret_cast<FwdMisc*>(ring + Cfg::kStages * Cfg::kStageBytes);
 
   const int tid = threadIdx.x;
-  const int warp = tid >> 5;
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);  // provably warp-uniform
   const int lane = tid & 31;
   // grid (heads, work items, slabs): the head index varies fastest in launch
   // order, so the longest causal rows of every head are dispatched first
@@ -214,17 +214,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     __syncwarp();
   } else if (warp == kFwdMmaWarp) {
     // ============================ MMA issuer ============================
-    if (lane == 0 && n_kt > 0) {
+    // the whole warp runs the issue loop (warp-uniform waits, one elected lane
+    // per MMA): see mbar_wait_warp
+    if (n_kt > 0) {
       constexpr uint32_t kIdS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t kIdPV = idesc_bf16(128, 256, false, true);
       const uint32_t q_base = smem_addr(q_s);
       const uint32_t ring_base = smem_addr(ring);
       uint32_t it = 0;
-      bool ok = mbar_wait(&misc->q_full, 0, ab, kDevTimeoutTma);
+      bool ok = mbar_wait_warp(&misc->q_full, 0, ab, kDevTimeoutTma);
       auto take = [&](uint32_t& stage) -> bool {
         stage = it % Cfg::kStages;
         const uint32_t ph = (it / Cfg::kStages) & 1;
-        if (!mbar_wait(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
+        if (!mbar_wait_warp(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
         tc_fence_after();
         return true;
       };
@@ -239,12 +241,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const int g = c * 8 + kk;
             const uint64_t a = sdesc_sw128(q_base + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024);
             const uint64_t b = sdesc_sw128(kb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-            umma_ss(d, a, b, kIdS, (c | kk) != 0);
+            umma_ss_w(d, a, b, kIdS, (c | kk) != 0);
           }
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
           ++it;
         }
-        umma_commit(&misc->s_full[j & 1]);
+        umma_commit_w(&misc->s_full[j & 1]);
       };
       auto issue_pv = [&](int j) {
         const uint32_t a_t = tmem + (j & 1) * 128;
@@ -255,23 +257,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t b = sdesc_sw128(vb + kk * 2048, 8192, 1024);
-            umma_ts(tmem + 256, a_t + c * 32 + kk * 8, b, kIdPV, (j | c | kk) != 0);
+            umma_ts_w(tmem + 256, a_t + c * 32 + kk * 8, b, kIdPV, (j | c | kk) != 0);
           }
-          umma_commit(&misc->ring_empty[st]);
+          umma_commit_w(&misc->ring_empty[st]);
           ++it;
         }
-        umma_commit(&misc->o_done);
+        umma_commit_w(&misc->o_done);
       };
       if (ok) issue_s(0);
       for (int j = 0; j < n_kt && ok; ++j) {
         if (j + 1 < n_kt) issue_s(j + 1);
-        if (!(ok = mbar_wait(&misc->p_full[j & 1], (j >> 1) & 1, ab, kDevTimeoutPeer))) break;
+        if (!(ok = mbar_wait_warp(&misc->p_full[j & 1], (j >> 1) & 1, ab, kDevTimeoutPeer)))
+          break;
         tc_fence_after();
         issue_pv(j);
       }
-      // Drain: every MMA this thread issued has completed before TMEM is freed.
-      umma_commit(&misc->drain);
-      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+      // Drain: every MMA this warp issued has completed before TMEM is freed.
+      umma_commit_w(&misc->drain);
+      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {

@@ -154,6 +154,59 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   }
 }
 
+// Waits of the MMA-issuing warps.  The whole warp polls inside one PTX block,
+// bounded by %globaltimer (kWaitLimitNs) and by the CTA abort word; the timer
+// is read only after a failed first try.  Measured with a tcgen05.mma issue
+// probe (M128 N128 K16, a wait per 8 MMAs): one lane polling through a C++ loop
+// around try_wait issues an MMA every 135 cycles, the converged warp polling
+// here every 70 (the tensor pipe needs 68).
+#define G4_WAIT_WARP_ASM(TRY)                                                         \
+  asm volatile(                                                                       \
+      "{\n\t.reg .pred p;\n\t.reg .u64 t0, t1;\n\t.reg .u32 f;\n\t"                \
+      TRY " p, [%1], %2;\n\t"                                                        \
+      "@p bra LAB_DONE;\n\t"                                                         \
+      "mov.u64 t0, %%globaltimer;\n"                                                  \
+      "LAB_WAIT:\n\t"                                                                \
+      TRY " p, [%1], %2;\n\t"                                                        \
+      "@p bra LAB_DONE;\n\t"                                                         \
+      "ld.volatile.shared.u32 f, [%3];\n\t"                                          \
+      "setp.ne.u32 p, f, 0;\n\t"                                                     \
+      "@p bra LAB_FAIL;\n\t"                                                         \
+      "mov.u64 t1, %%globaltimer;\n\t"                                               \
+      "sub.u64 t1, t1, t0;\n\t"                                                      \
+      "setp.lt.u64 p, t1, %4;\n\t"                                                   \
+      "@p bra LAB_WAIT;\n"                                                            \
+      "LAB_FAIL:\n\t"                                                                \
+      "setp.ne.u32 p, 0, 0;\n"                                                        \
+      "LAB_DONE:\n\t"                                                                \
+      "selp.u32 %0, 1, 0, p;\n\t}"                                                   \
+      : "=r"(done)                                                                    \
+      : "r"(smem_addr(bar)), "r"(parity), "r"(smem_addr((const void*)ab.flag)),        \
+        "l"(kWaitLimitNs)                                                             \
+      : "memory")
+
+__device__ __forceinline__ bool wait_warp_fail(const CtaAbort& ab, int code) {
+  if (!*ab.flag) {  // this wait ran out of time (not an abort raised elsewhere)
+    *ab.flag = 1;
+    if (ab.error) atomicCAS(ab.error, 0, code);
+  }
+  return false;
+}
+// All 32 lanes of a converged warp; returns the same value in every lane.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const CtaAbort& ab,
+                                               int code) {
+  uint32_t done;
+  G4_WAIT_WARP_ASM("mbarrier.try_wait.parity.shared::cta.b64");
+  return done ? true : wait_warp_fail(ab, code);
+}
+// The same with cluster-scope acquire (barriers that receive peer-CTA arrivals).
+__device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t parity,
+                                                       const CtaAbort& ab, int code) {
+  uint32_t done;
+  G4_WAIT_WARP_ASM("mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64");
+  return done ? true : wait_warp_fail(ab, code);
+}
+
 // ------------------------------------------------------------------------------------
 // TMA: every load delivers into the issuing CTA's own shared memory
 // ------------------------------------------------------------------------------------
@@ -316,6 +369,37 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
       : "memory");
 }
 
+// Issued by a converged warp: elect.sync picks one lane inside the asm block,
+// so the issuing loop stays warp-uniform (operands in uniform registers).
+__device__ __forceinline__ void umma_ss_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_w(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_addr(bar))
+      : "memory");
+}
+
 // Pair (cta_group::2) forms.  A kernel uses either these or the cta_group::1
 // forms above for all of its tcgen05 allocation, MMA and commit operations.
 // Allocation and release are issued by the same warp of both CTAs of the pair.
@@ -356,6 +440,28 @@ __device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           mapa_shared(bar, 1))
+      : "memory");
+}
+
+// Converged-warp forms of the pair MMA and commit (one lane elected inside the asm).
+__device__ __forceinline__ void umma_ss_pair_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair_both_w(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%1];\n\t}" ::"r"(
+          smem_addr(bar)),
+      "r"(mapa_shared(bar, 1))
       : "memory");
 }
 
