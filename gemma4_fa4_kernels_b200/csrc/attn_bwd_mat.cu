@@ -258,15 +258,21 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   auto stg = [&](int j) { return res_area + (Cfg::kExtraStages + (j & 1)) * 32768; };
 
   if (warp == kProducerWarp) {
-    if (lane == 0 && work > 0) {
-      mbar_expect_tx(&misc->res_full, Cfg::kQBytes + Cfg::kDoBytes);
+    // whole warp: warp-uniform waits, copies issued by one elected lane
+    if (work > 0) {
       const int qrow = si.q_base + qt * kTileM;
-      if (Cfg::kS)
-        for (int blk = 0; blk < D / 64; ++blk)
-          tma_load_4d(q_s + blk * 16384, &tmQ, &misc->res_full, blk * 64, head, qrow, si.b_coord);
-      if (Cfg::kDP)
-        for (int blk = 0; blk < D / 64; ++blk)
-          tma_load_4d(do_s + blk * 16384, &tmDO, &misc->res_full, blk * 64, head, qrow, si.b_coord);
+      if (elect_one()) {
+        mbar_expect_tx(&misc->res_full, Cfg::kQBytes + Cfg::kDoBytes);
+        if (Cfg::kS)
+          for (int blk = 0; blk < D / 64; ++blk)
+            tma_load_4d(q_s + blk * 16384, &tmQ, &misc->res_full, blk * 64, head, qrow,
+                        si.b_coord);
+        if (Cfg::kDP)
+          for (int blk = 0; blk < D / 64; ++blk)
+            tma_load_4d(do_s + blk * 16384, &tmDO, &misc->res_full, blk * 64, head, qrow,
+                        si.b_coord);
+      }
+      __syncwarp();
       uint32_t it = 0;
       bool ok = true;
       bool res_free = !Cfg::kTS;
@@ -276,16 +282,19 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
           if (st >= static_cast<uint32_t>(Cfg::kStages) && !res_free) {
-            if (!(ok = mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer))) break;
+            if (!(ok = mbar_wait_warp(&misc->a_ready, 0, ab, kDevTimeoutPeer))) break;
             res_free = true;
           }
-          if (!(ok = mbar_wait(&misc->ring_empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
-          mbar_expect_tx(&misc->ring_full[st], 32768);
-          const bool is_k = Cfg::kS && c < D / 128;
-          const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
-          for (int h = 0; h < 2; ++h)
-            tma_load_4d(stage_ptr(st) + h * 16384, is_k ? &tmK : &tmV, &misc->ring_full[st],
-                        (2 * cc + h) * 64, kv_head, krow, si.b_coord);
+          if (!(ok = mbar_wait_warp(&misc->ring_empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
+          if (elect_one()) {
+            mbar_expect_tx(&misc->ring_full[st], 32768);
+            const bool is_k = Cfg::kS && c < D / 128;
+            const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
+            for (int h = 0; h < 2; ++h)
+              tma_load_4d(stage_ptr(st) + h * 16384, is_k ? &tmK : &tmV, &misc->ring_full[st],
+                          (2 * cc + h) * 64, kv_head, krow, si.b_coord);
+          }
+          __syncwarp();
         }
       }
     }
@@ -849,41 +858,45 @@ __global__ void __launch_bounds__(192, 1)
   }
 
   if (warp == 4) {
-    if (lane == 0 && n_steps > 0) {
+    // whole warp: warp-uniform waits, copies issued by one elected lane
+    if (n_steps > 0) {
       uint32_t it = 0;
       bool ok = true;
       for_each_tile([&](const uint8_t* t, int b_head, int b_row) {
         for (int h = 0; h < 2 && ok; ++h) {
           const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
           ++it;
-          if (!(ok = mbar_wait(&misc->empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
+          if (!(ok = mbar_wait_warp(&misc->empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
           uint8_t* dst = smem + st * Cfg::kStageBytes;
-          if (PAIR) {
-            // this CTA's dS half (one 16 KB box of the byte view of the scratch)
-            // and its two 128-column slices of the 64 K rows (one per 256-wide
-            // MMA); both CTAs' bytes complete on the leader's barrier
-            if (crank == 0) mbar_expect_tx(&misc->full[st], 2 * Cfg::kStageBytes);
-            const uint32_t lbar = mapa_shared(&misc->full[st], 0);
-            const uint8_t* abase = WHICH == kGemmO ? p.p_tiles : p.ds_tiles;
-            const int half_idx = static_cast<int>((t - abase) / 16384) + h;
-            tma_load_3d_pair(dst, &tmA, lbar, 0, 0, half_idx);
-            for (int nh = 0; nh < 2; ++nh)
-              for (int bx = 0; bx < 2; ++bx)
-                tma_load_4d_pair(dst + Cfg::kABytes + (nh * 2 + bx) * 8192, &tmB, lbar,
-                                 nh * 256 + static_cast<int>(crank) * 128 + bx * 64, b_head,
-                                 b_row + h * 64, si.b_coord);
-            continue;
+          if (elect_one()) {
+            if (PAIR) {
+              // this CTA's dS half (one 16 KB box of the byte view of the scratch)
+              // and its two 128-column slices of the 64 K rows (one per 256-wide
+              // MMA); both CTAs' bytes complete on the leader's barrier
+              if (crank == 0) mbar_expect_tx(&misc->full[st], 2 * Cfg::kStageBytes);
+              const uint32_t lbar = mapa_shared(&misc->full[st], 0);
+              const uint8_t* abase = WHICH == kGemmO ? p.p_tiles : p.ds_tiles;
+              const int half_idx = static_cast<int>((t - abase) / 16384) + h;
+              tma_load_3d_pair(dst, &tmA, lbar, 0, 0, half_idx);
+              for (int nh = 0; nh < 2; ++nh)
+                for (int bx = 0; bx < 2; ++bx)
+                  tma_load_4d_pair(dst + Cfg::kABytes + (nh * 2 + bx) * 8192, &tmB, lbar,
+                                   nh * 256 + static_cast<int>(crank) * 128 + bx * 64, b_head,
+                                   b_row + h * 64, si.b_coord);
+            } else {
+              mbar_expect_tx(&misc->full[st], Cfg::kStageBytes);
+              if (Cfg::kQMajor) {
+                bulk_load(dst, t + h * 16384, 16384, &misc->full[st]);
+              } else {
+                bulk_load(dst, t + h * 8192, 8192, &misc->full[st]);
+                bulk_load(dst + 8192, t + 16384 + h * 8192, 8192, &misc->full[st]);
+              }
+              for (int blk = 0; blk < Cfg::kNB / 64; ++blk)
+                tma_load_4d(dst + Cfg::kABytes + blk * 8192, &tmB, &misc->full[st],
+                            half * 256 + blk * 64, b_head, b_row + h * 64, si.b_coord);
+            }
           }
-          mbar_expect_tx(&misc->full[st], Cfg::kStageBytes);
-          if (Cfg::kQMajor) {
-            bulk_load(dst, t + h * 16384, 16384, &misc->full[st]);
-          } else {
-            bulk_load(dst, t + h * 8192, 8192, &misc->full[st]);
-            bulk_load(dst + 8192, t + 16384 + h * 8192, 8192, &misc->full[st]);
-          }
-          for (int blk = 0; blk < Cfg::kNB / 64; ++blk)
-            tma_load_4d(dst + Cfg::kABytes + blk * 8192, &tmB, &misc->full[st],
-                        half * 256 + blk * 64, b_head, b_row + h * 64, si.b_coord);
+          __syncwarp();
         }
         return ok;
       });

@@ -166,31 +166,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   if (warp == kFwdProducerWarp) {
     // ============================ TMA producer ============================
-    if (lane == 0 && n_kt > 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      mbar_expect_tx(&misc->q_full, Cfg::kQBytes);
-      for (int blk = 0; blk < DQK / 64; ++blk)
-        tma_load_4d(q_s + blk * 16384, &tmQ, &misc->q_full, blk * 64, head,
-                    si.q_base + qt * kTileM, si.b_coord);
+    // whole warp: warp-uniform waits, copies issued by one elected lane
+    if (n_kt > 0) {
+      if (elect_one()) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        mbar_expect_tx(&misc->q_full, Cfg::kQBytes);
+        for (int blk = 0; blk < DQK / 64; ++blk)
+          tma_load_4d(q_s + blk * 16384, &tmQ, &misc->q_full, blk * 64, head,
+                      si.q_base + qt * kTileM, si.b_coord);
+      }
+      __syncwarp();
       uint32_t it = 0;
       bool ok = true;
       auto acquire = [&](uint32_t& stage) -> bool {
         stage = it % Cfg::kStages;
         const uint32_t ph = (it / Cfg::kStages) & 1;
-        if (!mbar_wait(&misc->ring_empty[stage], ph ^ 1, ab, kDevTimeoutMma)) return false;
-        mbar_expect_tx(&misc->ring_full[stage], Cfg::kStageBytes);
-        return true;
+        return mbar_wait_warp(&misc->ring_empty[stage], ph ^ 1, ab, kDevTimeoutMma);
       };
       auto load_k = [&](int kt) {
         for (int c = 0; c < Cfg::kKChunks && ok; ++c) {
           uint32_t st;
           if (!(ok = acquire(st))) break;
-          uint8_t* dst = ring + st * Cfg::kStageBytes;
-          for (int h = 0; h < 2; ++h)
-            tma_load_4d(dst + h * 16384, &tmK, &misc->ring_full[st], (2 * c + h) * 64, kv_head,
-                        si.k_base + kt * kTileN, si.b_coord);
+          if (elect_one()) {
+            mbar_expect_tx(&misc->ring_full[st], Cfg::kStageBytes);
+            uint8_t* dst = ring + st * Cfg::kStageBytes;
+            for (int h = 0; h < 2; ++h)
+              tma_load_4d(dst + h * 16384, &tmK, &misc->ring_full[st], (2 * c + h) * 64, kv_head,
+                          si.k_base + kt * kTileN, si.b_coord);
+          }
+          __syncwarp();
           ++it;
         }
       };
@@ -198,10 +204,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int c = 0; c < Cfg::kVChunks && ok; ++c) {
           uint32_t st;
           if (!(ok = acquire(st))) break;
-          uint8_t* dst = ring + st * Cfg::kStageBytes;
-          for (int blk = 0; blk < 4; ++blk)
-            tma_load_4d(dst + blk * 8192, &tmV, &misc->ring_full[st], slab * 256 + blk * 64,
-                        kv_head, si.k_base + kt * kTileN + c * 64, si.b_coord);
+          if (elect_one()) {
+            mbar_expect_tx(&misc->ring_full[st], Cfg::kStageBytes);
+            uint8_t* dst = ring + st * Cfg::kStageBytes;
+            for (int blk = 0; blk < 4; ++blk)
+              tma_load_4d(dst + blk * 8192, &tmV, &misc->ring_full[st], slab * 256 + blk * 64,
+                          kv_head, si.k_base + kt * kTileN + c * 64, si.b_coord);
+          }
+          __syncwarp();
           ++it;
         }
       };

@@ -185,6 +185,18 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
         "l"(kWaitLimitNs)                                                             \
       : "memory")
 
+// One lane of a converged warp (elect.sync over the full mask): the lowest
+// active lane, so every call in a converged warp elects lane 0.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(e));
+  return e != 0;
+}
+
 __device__ __forceinline__ bool wait_warp_fail(const CtaAbort& ab, int code) {
   if (!*ab.flag) {  // this wait ran out of time (not an abort raised elsewhere)
     *ab.flag = 1;
