@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "g4_attn_bwd",
     "g4_attn_bwd_noalloc",
     "g4_read_device_error",
+    "g4_selftest_wait",
     "g4_build_mask",
     "g4_prep_bwd_workspace_bytes",
     "g4_prep_fwd",
@@ -162,6 +163,10 @@ def load() -> ctypes.CDLL:
         lib.g4_read_device_error.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int),
                                              ctypes.c_void_p]
         lib.g4_read_device_error.restype = ctypes.c_int
+        lib.g4_selftest_wait.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                         ctypes.POINTER(ctypes.c_int),
+                                         ctypes.POINTER(ctypes.c_double)]
+        lib.g4_selftest_wait.restype = ctypes.c_int
         lib.g4_build_mask.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
@@ -210,6 +215,17 @@ def launch_counts() -> dict[str, int]:
         lib.g4_launch_count(i, ctypes.byref(c))
         out[name] = int(c.value)
     return out
+
+
+def selftest_wait(mode: int) -> tuple[int, bool, float]:
+    """Run the bounded-wait self-test (``g4_selftest_wait``) on the current
+    device: returns (device error code, wait completed, wait duration in ms)."""
+    lib = load()
+    code, done, ms = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_double(0.0)
+    rc = lib.g4_selftest_wait(int(mode), ctypes.byref(code), ctypes.byref(done), ctypes.byref(ms))
+    if rc != G4_OK:
+        raise RuntimeError(f"g4_selftest_wait: {last_error()}")
+    return int(code.value), bool(done.value), float(ms.value)
 
 
 def profile_enable(enable: bool) -> None:

@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
     // the whole warp runs the issue loop (warp-uniform waits, one elected
-    // lane per MMA): see mbar_wait_warp
+    // lane per MMA): see mbar_wait
     if (n_kt > 0) {
       constexpr uint32_t kIdS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t kIdQ = idesc_bf16(128, 256, false, true);
@@ -314,12 +314,12 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t db = smem_addr(do_s);
       const uint32_t rb = smem_addr(ring);
       uint32_t it = 0;
-      bool ok = mbar_wait_warp(&misc->res_full, 0, ab, kDevTimeoutTma);
+      bool ok = mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
       auto take = [&]() -> int {
         const uint32_t st = it % kBwdStages;
         const uint32_t ph = (it / kBwdStages) & 1;
         ++it;
-        if (!mbar_wait_warp(&misc->ring_full[st], ph, ab, kDevTimeoutTma)) {
+        if (!mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma)) {
           ok = false;
           return -1;
         }
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         umma_commit_w(&misc->s_full);
         if (!ok) break;
-        if (!(ok = mbar_wait_warp(&misc->ds_full, j & 1, ab, kDevTimeoutPeer))) break;
+        if (!(ok = mbar_wait(&misc->ds_full, j & 1, ab, kDevTimeoutPeer))) break;
         tc_fence_after();
         // dQ += dS K   (dS: bf16 pairs in TMEM columns [0,64))
         for (int h = 0; h < 2 && ok; ++h) {
@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(192, 1)
         umma_commit_w(&misc->step_done);
       }
       umma_commit_w(&misc->drain);
-      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
+      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
@@ -652,7 +652,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 5) {
     // ---------------- MMA issuer ----------------
     // the whole warp runs the issue loop (warp-uniform waits, one elected
-    // lane per MMA): see mbar_wait_warp
+    // lane per MMA): see mbar_wait
     if (n_steps > 0) {
       constexpr uint32_t kIdS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t kIdAcc = idesc_bf16(128, 128, false, true);
@@ -660,12 +660,12 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t vb = smem_addr(v_s);
       const uint32_t rb = smem_addr(ring);
       uint32_t it = 0;
-      bool ok = mbar_wait_warp(&misc->res_full, 0, ab, kDevTimeoutTma);
+      bool ok = mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
       auto take = [&]() -> int {
         const uint32_t st = it % kBwdStages;
         const uint32_t ph = (it / kBwdStages) & 1;
         ++it;
-        if (!mbar_wait_warp(&misc->ring_full[st], ph, ab, kDevTimeoutTma)) {
+        if (!mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma)) {
           ok = false;
           return -1;
         }
@@ -710,7 +710,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         umma_commit_w(&misc->s_full);
         if (!ok) break;
-        if (!(ok = mbar_wait_warp(&misc->ds_full, step & 1, ab, kDevTimeoutPeer))) break;
+        if (!(ok = mbar_wait(&misc->ds_full, step & 1, ab, kDevTimeoutPeer))) break;
         tc_fence_after();
         // dV += P^T dO[:, slab]
         {
@@ -737,7 +737,7 @@ __global__ void __launch_bounds__(192, 1)
         umma_commit_w(&misc->step_done);
       }
       umma_commit_w(&misc->drain);
-      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
+      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {

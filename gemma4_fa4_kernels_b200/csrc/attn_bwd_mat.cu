@@ -282,10 +282,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
           if (st >= static_cast<uint32_t>(Cfg::kStages) && !res_free) {
-            if (!(ok = mbar_wait_warp(&misc->a_ready, 0, ab, kDevTimeoutPeer))) break;
+            if (!(ok = mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer))) break;
             res_free = true;
           }
-          if (!(ok = mbar_wait_warp(&misc->ring_empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
+          if (!(ok = mbar_wait(&misc->ring_empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
           if (elect_one()) {
             mbar_expect_tx(&misc->ring_full[st], 32768);
             const bool is_k = Cfg::kS && c < D / 128;
@@ -349,27 +349,27 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // the whole warp runs the issue loop (warp-uniform waits, one elected lane
-    // per MMA): see mbar_wait_warp
+    // per MMA): see mbar_wait
     if (work > 0) {
       constexpr uint32_t kId = idesc_bf16(128, 128, false, false);
       const uint32_t qb = smem_addr(q_s), db = smem_addr(do_s);
       uint32_t it = 0;
-      bool ok = Cfg::kTS || Cfg::kQT ? mbar_wait_warp(&misc->a_ready, 0, ab, kDevTimeoutPeer)
-                                     : mbar_wait_warp(&misc->res_full, 0, ab, kDevTimeoutTma);
+      bool ok = Cfg::kTS || Cfg::kQT ? mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer)
+                                     : mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
       for (int j = 0; j < work && ok; ++j) {
         const int b = j & 1;
         if (j >= 2 &&
-            !(ok = mbar_wait_warp(&misc->buf_free[b], ((j - 2) >> 1) & 1, ab, kDevTimeoutPeer)))
+            !(ok = mbar_wait(&misc->buf_free[b], ((j - 2) >> 1) & 1, ab, kDevTimeoutPeer)))
           break;
         tc_fence_after();
         for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
           const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
-          if (!(ok = mbar_wait_warp(&misc->ring_full[st], ph, ab, kDevTimeoutTma))) break;
+          if (!(ok = mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma))) break;
           const bool is_k = Cfg::kS && c < D / 128;
           // single dP buffer: tile j's dP waits until every math thread read tile j-1's
           if (Cfg::kQT && c == D / 128 && j > 0 &&
-              !(ok = mbar_wait_warp(&misc->dp_free, (j - 1) & 1, ab, kDevTimeoutPeer)))
+              !(ok = mbar_wait(&misc->dp_free, (j - 1) & 1, ab, kDevTimeoutPeer)))
             break;
           tc_fence_after();
           const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         umma_commit_w(&misc->s_full[b]);
       }
       umma_commit_w(&misc->drain);
-      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
+      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
@@ -866,7 +866,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int h = 0; h < 2 && ok; ++h) {
           const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
           ++it;
-          if (!(ok = mbar_wait_warp(&misc->empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
+          if (!(ok = mbar_wait(&misc->empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
           uint8_t* dst = smem + st * Cfg::kStageBytes;
           if (elect_one()) {
             if (PAIR) {
@@ -919,7 +919,7 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
     }
     // the MMA issue loops run on the whole warp (warp-uniform waits, one
-    // elected lane per MMA): see mbar_wait_warp
+    // elected lane per MMA): see mbar_wait
     if (PAIR) {
       if (n_steps > 0 && crank == 0) {
         // leader: M = 256 (both CTAs' query rows), N = 256 per MMA (128
@@ -934,13 +934,13 @@ __global__ void __launch_bounds__(192, 1)
               ((misc->flag_bits[(tj >> 5) & 63] >> (tj & 31)) & 1u)) {
             // both CTAs' correction warps rescale O once every earlier product completed
             umma_commit_pair_both_w(&misc->o_done);
-            if (!(ok = mbar_wait_cluster_warp(&misc->o_ready, events & 1, ab, kDevTimeoutPeer)))
+            if (!(ok = mbar_wait_cluster(&misc->o_ready, events & 1, ab, kDevTimeoutPeer)))
               break;
             tc_fence_after();
             ++events;
           }
           const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
-          if (!(ok = mbar_wait_warp(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
+          if (!(ok = mbar_wait(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
           tc_fence_after();
           const uint32_t a = sb0 + st * Cfg::kStageBytes;
           const uint32_t bb = a + Cfg::kABytes;
@@ -957,7 +957,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         umma_commit_pair_both_w(&misc->acc_full);
         umma_commit_pair_both_w(&misc->drain);
-        mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
+        mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
       }
     } else if (n_steps > 0) {
       constexpr uint32_t kId = idesc_bf16(128, 256, !Cfg::kQMajor, true);
@@ -971,7 +971,7 @@ __global__ void __launch_bounds__(192, 1)
         if (WHICH == kGemmO && tile_j > 0 &&
             ((misc->flag_bits[(tile_j >> 5) & 63] >> (tile_j & 31)) & 1u)) {
           umma_commit_w(&misc->o_done);
-          if (!(ok = mbar_wait_warp(&misc->o_ready, events & 1, ab, kDevTimeoutPeer)))
+          if (!(ok = mbar_wait(&misc->o_ready, events & 1, ab, kDevTimeoutPeer)))
             return false;
           tc_fence_after();
           ++events;
@@ -981,7 +981,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t st = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
           const uint32_t first = it == 0;
           ++it;
-          if (!(ok = mbar_wait_warp(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
+          if (!(ok = mbar_wait(&misc->full[st], ph, ab, kDevTimeoutTma))) break;
           tc_fence_after();
           const uint32_t a = sb0 + st * Cfg::kStageBytes;
           const uint32_t bb = a + Cfg::kABytes;
@@ -1001,7 +1001,7 @@ __global__ void __launch_bounds__(192, 1)
       });
       umma_commit_w(&misc->acc_full);
       umma_commit_w(&misc->drain);
-      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
+      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {

@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 5) {
     // ============================ MMA issuer ============================
     // the whole warp runs the issue loop (warp-uniform waits, one elected
-    // lane per MMA): see mbar_wait_warp
+    // lane per MMA): see mbar_wait
     if (n > 0) {
       constexpr uint32_t kIdS = idesc_bf16(128, 16, false, false);
       constexpr uint32_t kIdO = idesc_bf16(128, 16, true, false);
@@ -183,17 +183,17 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t q_b = smem_addr(q_s);
       const uint32_t p_b = smem_addr(p_s);
       uint32_t it = 0;
-      bool ok = mbar_wait_warp(&misc->q_ready, 0, ab, kDevTimeoutPeer);
+      bool ok = mbar_wait(&misc->q_ready, 0, ab, kDevTimeoutPeer);
       auto take = [&](uint32_t& stage) -> bool {
         stage = it % kDecodeStages;
         const uint32_t ph = (it / kDecodeStages) & 1;
-        if (!mbar_wait_warp(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
+        if (!mbar_wait(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
         tc_fence_after();
         return true;
       };
       auto issue_s = [&](int u) {
         const int b = u & 1;
-        if (!(ok = mbar_wait_warp(&misc->s_empty[b], ((u >> 1) & 1) ^ 1, ab, kDevTimeoutPeer)))
+        if (!(ok = mbar_wait(&misc->s_empty[b], ((u >> 1) & 1) ^ 1, ab, kDevTimeoutPeer)))
           return;
         tc_fence_after();
         const uint32_t d = tmem + b * 16;
@@ -235,14 +235,14 @@ __global__ void __launch_bounds__(192, 1)
       for (int u = 0; u < n && ok; ++u) {
         if (u + 1 < n) issue_s(u + 1);
         if (!ok) break;
-        if (!(ok = mbar_wait_warp(&misc->p_full[u & 1], (u >> 1) & 1, ab, kDevTimeoutPeer)))
+        if (!(ok = mbar_wait(&misc->p_full[u & 1], (u >> 1) & 1, ab, kDevTimeoutPeer)))
           break;
         tc_fence_after();
         issue_o(u);
       }
       // Drain: every MMA this warp issued has completed before TMEM is freed.
       umma_commit_w(&misc->drain);
-      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
+      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {

@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       auto acquire = [&](uint32_t& stage) -> bool {
         stage = it % Cfg::kStages;
         const uint32_t ph = (it / Cfg::kStages) & 1;
-        return mbar_wait_warp(&misc->ring_empty[stage], ph ^ 1, ab, kDevTimeoutMma);
+        return mbar_wait(&misc->ring_empty[stage], ph ^ 1, ab, kDevTimeoutMma);
       };
       auto load_k = [&](int kt) {
         for (int c = 0; c < Cfg::kKChunks && ok; ++c) {
@@ -225,18 +225,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else if (warp == kFwdMmaWarp) {
     // ============================ MMA issuer ============================
     // the whole warp runs the issue loop (warp-uniform waits, one elected lane
-    // per MMA): see mbar_wait_warp
+    // per MMA): see mbar_wait
     if (n_kt > 0) {
       constexpr uint32_t kIdS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t kIdPV = idesc_bf16(128, 256, false, true);
       const uint32_t q_base = smem_addr(q_s);
       const uint32_t ring_base = smem_addr(ring);
       uint32_t it = 0;
-      bool ok = mbar_wait_warp(&misc->q_full, 0, ab, kDevTimeoutTma);
+      bool ok = mbar_wait(&misc->q_full, 0, ab, kDevTimeoutTma);
       auto take = [&](uint32_t& stage) -> bool {
         stage = it % Cfg::kStages;
         const uint32_t ph = (it / Cfg::kStages) & 1;
-        if (!mbar_wait_warp(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
+        if (!mbar_wait(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
         tc_fence_after();
         return true;
       };
@@ -277,14 +277,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (ok) issue_s(0);
       for (int j = 0; j < n_kt && ok; ++j) {
         if (j + 1 < n_kt) issue_s(j + 1);
-        if (!(ok = mbar_wait_warp(&misc->p_full[j & 1], (j >> 1) & 1, ab, kDevTimeoutPeer)))
+        if (!(ok = mbar_wait(&misc->p_full[j & 1], (j >> 1) & 1, ab, kDevTimeoutPeer)))
           break;
         tc_fence_after();
         issue_pv(j);
       }
       // Drain: every MMA this warp issued has completed before TMEM is freed.
       umma_commit_w(&misc->drain);
-      mbar_wait_warp(&misc->drain, 0, ab, kDevTimeoutMma);
+      mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
     }
     __syncwarp();
   } else {

@@ -56,6 +56,7 @@ enum KernelId {
   kKPrepFwd,
   kKPrepBwd,
   kKPrepDw,
+  kKSelftest,
   kKCount
 };
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
@@ -63,7 +64,7 @@ const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq
                                            "bwd_gemm_dv", "bwd_gemm_dk", "bwd_gemm_dq",
                                            "fwd_score",   "fwd_pv",      "decode",
                                            "decode_combine", "prep_fwd",  "prep_bwd",
-                                           "prep_dw_reduce"};
+                                           "prep_dw_reduce", "selftest_wait"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -1088,6 +1089,32 @@ int g4_profile_read(int id, long long* launches, double* total_ms) {
   }
   *launches = n;
   *total_ms = ms;
+  return G4_OK;
+}
+
+int g4_selftest_wait(int mode, int* code, int* completed, double* wait_ms) {
+  if (mode < 0 || mode > 2 || !code || !completed || !wait_ms)
+    return fail(G4_ERR_INVALID, "selftest mode must be 0, 1 or 2 and every output is required");
+  void* dev = nullptr;
+  cudaError_t e = cudaMalloc(&dev, 64);
+  if (e != cudaSuccess) return cuda_fail(e, "selftest buffer");
+  int* err = static_cast<int*>(dev);
+  auto* out = reinterpret_cast<unsigned long long*>(static_cast<char*>(dev) + 16);
+  e = cudaMemset(dev, 0, 64);
+  int rc = 0;
+  if (e == cudaSuccess) {
+    LaunchScope ls(kKSelftest, nullptr);
+    rc = g4::launch_selftest_wait(mode, err, out, nullptr);
+  }
+  if (e == cudaSuccess && rc == 0) e = cudaDeviceSynchronize();
+  unsigned long long host[2] = {0, 0};
+  if (e == cudaSuccess && rc == 0) e = cudaMemcpy(code, err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && rc == 0) e = cudaMemcpy(host, out, sizeof(host), cudaMemcpyDeviceToHost);
+  cudaFree(dev);
+  if (rc) return cuda_fail(static_cast<cudaError_t>(rc), "selftest launch");
+  if (e != cudaSuccess) return cuda_fail(e, "selftest");
+  *completed = static_cast<int>(host[0]);
+  *wait_ms = static_cast<double>(host[1]) * 1e-6;
   return G4_OK;
 }
 

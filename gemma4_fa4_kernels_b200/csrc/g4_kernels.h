@@ -151,6 +151,8 @@ int prep_grid(bool backward, const PrepParams& p, int sm_count);
 int launch_prep_fwd(const PrepParams& p, int grid, cudaStream_t stream);
 int launch_prep_bwd(const PrepParams& p, int grid, cudaStream_t stream);
 int launch_prep_dw_reduce(const float* part, int n_parts, int d, float* dw, cudaStream_t stream);
+// bounded-wait self-test (one CTA): see g4_selftest_wait
+int launch_selftest_wait(int mode, int* err, unsigned long long* out, cudaStream_t stream);
 
 int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream);
 // pass: d512 runs pass 0 (P) then pass 1 (dS); d256 computes both in pass 0;

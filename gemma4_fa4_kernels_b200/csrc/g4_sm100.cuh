@@ -60,18 +60,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
 // Shared per-CTA abort word: once any role times out, every other wait returns
 // false promptly so that the CTA can reach its teardown (TMEM release).
 struct CtaAbort {
@@ -81,19 +69,69 @@ struct CtaAbort {
 
 // Wait until the phase with the given parity has completed.  Returns false
 // (after recording `code`) if the wait exceeds kWaitLimitNs or the CTA aborts.
+// The poll loop sits inside one PTX block, bounded by %globaltimer and by the
+// CTA abort word; the timer is read only after a failed first try.  Measured
+// with a tcgen05.mma issue probe (M128 N128 K16, a wait per 8 MMAs): an issuing
+// thread that polls through a C++ loop around try_wait issues an MMA every 135
+// cycles, a converged warp polling here every 70 (the tensor pipe needs 68).
+// Any caller may use it (one lane or a whole warp); lanes of a converged warp
+// all return the same value.
+#define G4_WAIT_ASM(TRY)                                                              \
+  asm volatile(                                                                       \
+      "{\n\t.reg .pred p;\n\t.reg .u64 t0, t1;\n\t.reg .u32 f;\n\t"                   \
+      TRY " p, [%1], %2;\n\t"                                                         \
+      "@p bra LAB_DONE;\n\t"                                                          \
+      "mov.u64 t0, %%globaltimer;\n"                                                  \
+      "LAB_WAIT:\n\t"                                                                 \
+      TRY " p, [%1], %2;\n\t"                                                         \
+      "@p bra LAB_DONE;\n\t"                                                          \
+      "ld.volatile.shared.u32 f, [%3];\n\t"                                           \
+      "setp.ne.u32 p, f, 0;\n\t"                                                      \
+      "@p bra LAB_FAIL;\n\t"                                                          \
+      "mov.u64 t1, %%globaltimer;\n\t"                                                \
+      "sub.u64 t1, t1, t0;\n\t"                                                       \
+      "setp.lt.u64 p, t1, %4;\n\t"                                                    \
+      "@p bra LAB_WAIT;\n"                                                            \
+      "LAB_FAIL:\n\t"                                                                 \
+      "setp.ne.u32 p, 0, 0;\n"                                                        \
+      "LAB_DONE:\n\t"                                                                 \
+      "selp.u32 %0, 1, 0, p;\n\t}"                                                    \
+      : "=r"(done)                                                                    \
+      : "r"(smem_addr(bar)), "r"(parity), "r"(smem_addr((const void*)ab.flag)),       \
+        "l"(kWaitLimitNs)                                                             \
+      : "memory")
+
+// One lane of a converged warp (elect.sync over the full mask): the lowest
+// active lane, so every call in a converged warp elects lane 0.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(e));
+  return e != 0;
+}
+
+__device__ __forceinline__ bool wait_fail(const CtaAbort& ab, int code) {
+  if (!*ab.flag) {  // this wait ran out of time (not an abort raised elsewhere)
+    *ab.flag = 1;
+    if (ab.error) atomicCAS(ab.error, 0, code);
+  }
+  return false;
+}
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const CtaAbort& ab,
                                           int code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*ab.flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      *ab.flag = 1;
-      if (ab.error) atomicCAS(ab.error, 0, code);
-      return false;
-    }
-  }
+  uint32_t done;
+  G4_WAIT_ASM("mbarrier.try_wait.parity.shared::cta.b64");
+  return done ? true : wait_fail(ab, code);
+}
+// The same with cluster-scope acquire (barriers that receive peer-CTA arrivals).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  const CtaAbort& ab, int code) {
+  uint32_t done;
+  G4_WAIT_ASM("mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64");
+  return done ? true : wait_fail(ab, code);
 }
 
 // ------------------------------------------------------------------------------------
@@ -126,99 +164,6 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cl_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr)
                : "memory");
 }
-// mbar_wait with cluster-scope acquire, for barriers that also receive
-// arrivals from the peer CTA.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
-                                                  const CtaAbort& ab, int code) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  while (true) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (*ab.flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      *ab.flag = 1;
-      if (ab.error) atomicCAS(ab.error, 0, code);
-      return false;
-    }
-  }
-}
-
-// Waits of the MMA-issuing warps.  The whole warp polls inside one PTX block,
-// bounded by %globaltimer (kWaitLimitNs) and by the CTA abort word; the timer
-// is read only after a failed first try.  Measured with a tcgen05.mma issue
-// probe (M128 N128 K16, a wait per 8 MMAs): one lane polling through a C++ loop
-// around try_wait issues an MMA every 135 cycles, the converged warp polling
-// here every 70 (the tensor pipe needs 68).
-#define G4_WAIT_WARP_ASM(TRY)                                                         \
-  asm volatile(                                                                       \
-      "{\n\t.reg .pred p;\n\t.reg .u64 t0, t1;\n\t.reg .u32 f;\n\t"                \
-      TRY " p, [%1], %2;\n\t"                                                        \
-      "@p bra LAB_DONE;\n\t"                                                         \
-      "mov.u64 t0, %%globaltimer;\n"                                                  \
-      "LAB_WAIT:\n\t"                                                                \
-      TRY " p, [%1], %2;\n\t"                                                        \
-      "@p bra LAB_DONE;\n\t"                                                         \
-      "ld.volatile.shared.u32 f, [%3];\n\t"                                          \
-      "setp.ne.u32 p, f, 0;\n\t"                                                     \
-      "@p bra LAB_FAIL;\n\t"                                                         \
-      "mov.u64 t1, %%globaltimer;\n\t"                                               \
-      "sub.u64 t1, t1, t0;\n\t"                                                      \
-      "setp.lt.u64 p, t1, %4;\n\t"                                                   \
-      "@p bra LAB_WAIT;\n"                                                            \
-      "LAB_FAIL:\n\t"                                                                \
-      "setp.ne.u32 p, 0, 0;\n"                                                        \
-      "LAB_DONE:\n\t"                                                                \
-      "selp.u32 %0, 1, 0, p;\n\t}"                                                   \
-      : "=r"(done)                                                                    \
-      : "r"(smem_addr(bar)), "r"(parity), "r"(smem_addr((const void*)ab.flag)),        \
-        "l"(kWaitLimitNs)                                                             \
-      : "memory")
-
-// One lane of a converged warp (elect.sync over the full mask): the lowest
-// active lane, so every call in a converged warp elects lane 0.
-__device__ __forceinline__ bool elect_one() {
-  uint32_t e;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
-      "elect.sync r|p, 0xffffffff;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(e));
-  return e != 0;
-}
-
-__device__ __forceinline__ bool wait_warp_fail(const CtaAbort& ab, int code) {
-  if (!*ab.flag) {  // this wait ran out of time (not an abort raised elsewhere)
-    *ab.flag = 1;
-    if (ab.error) atomicCAS(ab.error, 0, code);
-  }
-  return false;
-}
-// All 32 lanes of a converged warp; returns the same value in every lane.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const CtaAbort& ab,
-                                               int code) {
-  uint32_t done;
-  G4_WAIT_WARP_ASM("mbarrier.try_wait.parity.shared::cta.b64");
-  return done ? true : wait_warp_fail(ab, code);
-}
-// The same with cluster-scope acquire (barriers that receive peer-CTA arrivals).
-__device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t parity,
-                                                       const CtaAbort& ab, int code) {
-  uint32_t done;
-  G4_WAIT_WARP_ASM("mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64");
-  return done ? true : wait_warp_fail(ab, code);
-}
-
 // ------------------------------------------------------------------------------------
 // TMA: every load delivers into the issuing CTA's own shared memory
 // ------------------------------------------------------------------------------------

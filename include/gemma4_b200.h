@@ -168,6 +168,18 @@ int g4_attn_bwd_noalloc(const g4_attn_args* args, void* stream);
 int g4_read_device_error(const void* workspace, int* code, void* stream);
 
 /*
+ * Self-test of the bounded waits every kernel uses (no reference counterpart:
+ * the reference's kernels have no wait bound).  One CTA on the current device,
+ * synchronous.  mode 0: the awaited barrier completes; mode 1: nothing
+ * completes it and the wait expires after the library's 2 s bound; mode 2:
+ * another warp raises the CTA abort word first (recording device error 1) and
+ * the wait returns at once.  Outputs: *code the device error word, *completed
+ * 1 if the wait saw the barrier complete, *wait_ms the wait's duration.
+ * Nothing here faults or hangs the GPU.
+ */
+int g4_selftest_wait(int mode, int* code, int* completed, double* wait_ms);
+
+/*
  * Dense Gemma-4 mask builder: writes out[b][q][k] = 1 if allowed, else 0
  * (uint8, (B,Sq,Sk) contiguous).  Query row i sits at absolute position
  * q_start + i (q_start < 0 selects lower-right alignment, kv_len - q_len).
@@ -243,7 +255,7 @@ int g4_prep_bwd(const g4_prep_args* args, void* stream);
  * ranges), 5 mask builder, 6 backward P/dS scores, 7-9 backward dV / dK / dQ
  * tile GEMMs (materialised path), 10 two-pass forward softmax, 11 two-pass
  * forward O = P V, 12 decode, 13 decode combine, 14 preparation forward,
- * 15 preparation backward, 16 preparation dweight reduction.
+ * 15 preparation backward, 16 preparation dweight reduction, 17 wait self-test.
  *  - g4_launch_count: launches of `kernel_id` issued by this process so far.
  *  - g4_profile_enable(1): every later launch is bracketed by CUDA events on
  *    its own stream; g4_profile_read synchronises those events and returns the
