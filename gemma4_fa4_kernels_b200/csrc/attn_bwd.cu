@@ -224,6 +224,7 @@ __global__ void __launch_bounds__(192, 1)
   const int q_idx = qt * kTileM + tid;
   const bool row_valid = tid < kTileM && q_idx < si.len_q;
   const int q_abs = q_idx + q_off;
+  const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;  // text-only key range start
   int qvis = -1, qdoc = 0;
   float lse2_r = -INFINITY, delta_r = 0.f;
   if (row_valid) {
@@ -418,10 +419,10 @@ __global__ void __launch_bounds__(192, 1)
             const int col = c * 32 + i + u;
             const int k = k0 + col;
             bool keep = row_valid && lse2_r != -INFINITY && k < si.len_k;
-            if (cls != 1 && keep)
+            if (cls != 1 && keep)  // text only: the key range [k_lo, q_abs]
               keep = meta ? mask_allows(p.mask.window, q_abs, k, qvis, qdoc, misc->col_vis[col],
                                         misc->col_doc[col])
-                          : mask_allows(p.mask.window, q_abs, k, -1, 0, -1, 0);
+                          : (k >= k_lo && k <= q_abs);
             const float pr = keep ? ex2(fmaf(__uint_as_float(sr[i + u]), kLog2e, -lse2_r)) : 0.f;
             ds2[u] = keep ? pr * (__uint_as_float(dr[i + u]) - delta_r) : 0.f;
           }
@@ -558,6 +559,11 @@ __global__ void __launch_bounds__(192, 1)
 
   // ---- which query positions can see this key tile ----
   const int k = kt * kTileN + tid;  // this thread's key row (tid < 128)
+  // text only: the queries that see key k end at k + W - 1 (local) or never
+  const int q_hi = p.mask.window > 0
+                       ? static_cast<int>(min(static_cast<int64_t>(k) + p.mask.window - 1,
+                                              static_cast<int64_t>(0x7fffffff)))
+                       : 0x7fffffff;
   const bool row_valid = tid < kTileN && k < si.len_k;
   int kvis = -1, kdoc = 0;
   if (row_valid) {
@@ -782,10 +788,10 @@ __global__ void __launch_bounds__(192, 1)
             const int col = c * 32 + i + u;
             const float l2 = misc->col_lse2[col];
             bool keep = row_valid && l2 != -INFINITY;
-            if (cls != 1 && keep)
+            if (cls != 1 && keep)  // text only: the query range [k, q_hi]
               keep = meta ? mask_allows(p.mask.window, q0 + col + q_off, k, misc->col_vis[col],
                                         misc->col_doc[col], kvis, kdoc)
-                          : mask_allows(p.mask.window, q0 + col + q_off, k, -1, 0, -1, 0);
+                          : (q0 + col + q_off >= k && q0 + col + q_off <= q_hi);
             const float pr = keep ? ex2(fmaf(__uint_as_float(sr[i + u]), kLog2e, -l2)) : 0.f;
             pv[u] = pr;
             dv[u] = keep ? pr * (__uint_as_float(dr[i + u]) - misc->col_delta[col]) : 0.f;

@@ -143,9 +143,15 @@ struct ScoreCfg {
   static constexpr bool kStageDs = kTS && MODE == kScoreDs;
 };
 
+// The resident operand (Q, or dO in the dS pass) arrives in four quarters of
+// its K extent, each on its own barrier, and column group g of the math warps
+// moves quarter g into TMEM (TS variant): the first tile's MMAs start once
+// their quarter is in place instead of after the whole 64-128 KB operand.
+constexpr int kResParts = 4;
+
 struct ScoreMisc {
-  uint64_t res_full;
-  uint64_t a_ready;       // resident operand copied into TMEM (TS variant)
+  uint64_t res_full[kResParts];  // resident quarter landed (dO, when also resident, on the last)
+  uint64_t a_ready[kResParts];   // resident quarter copied into TMEM (TS / QT variants)
   uint64_t ring_full[8];
   uint64_t ring_empty[8];
   uint64_t s_full[2];
@@ -207,7 +213,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   const bool cap_ok = t_off + n_kt <= p.head_cap_tiles;
 
   if (tid == 0) {
-    mbar_init(&misc->res_full, 1);
+    for (int qp = 0; qp < kResParts; ++qp) {
+      mbar_init(&misc->res_full[qp], 1);
+      mbar_init(&misc->a_ready[qp], kScoreMathThreads / kResParts);
+    }
     for (int s = 0; s < Cfg::kRingStages; ++s) {
       mbar_init(&misc->ring_full[s], 1);
       mbar_init(&misc->ring_empty[s], 1);
@@ -217,7 +226,6 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       mbar_init(&misc->buf_free[b], kScoreMathThreads);
     }
     for (int s2 = 0; s2 < 4; ++s2) mbar_init(&misc->p_full[s2], 1);
-    mbar_init(&misc->a_ready, kScoreMathThreads);
     mbar_init(&misc->drain, 1);
     mbar_init(&misc->stg_free[0], 1);
     mbar_init(&misc->stg_free[1], 1);
@@ -226,6 +234,28 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     mbar_init(&misc->dp_free, kScoreMathThreads);
     misc->abort = 0;
     fence_mbar_init();
+    if (cap_ok && n_kt > 0) {
+      // the resident operand is requested before TMEM allocation and the CTA
+      // barrier: its 64-128 KB are the first thing every role waits for.
+      // Quarter qp of the TMEM-bound operand (Q, or dO in the dS pass) lands
+      // on res_full[qp]; a dO that stays in shared memory (S-and-dP pass)
+      // lands on the last quarter's barrier.
+      constexpr int kBpp = (D / 64) / kResParts;  // 64-element blocks per quarter
+      const int qrow = si.q_base + qt * kTileM;
+      const CUtensorMap* tr = Cfg::kS ? &tmQ : &tmDO;
+      uint8_t* rs = Cfg::kS ? q_s : do_s;
+      for (int qp = 0; qp < kResParts; ++qp) {
+        const bool do_too = Cfg::kS && Cfg::kDP && qp == kResParts - 1;
+        mbar_expect_tx(&misc->res_full[qp], kBpp * 16384 + (do_too ? Cfg::kDoBytes : 0));
+        for (int blk = qp * kBpp; blk < (qp + 1) * kBpp; ++blk)
+          tma_load_4d(rs + blk * 16384, tr, &misc->res_full[qp], blk * 64, head, qrow,
+                      si.b_coord);
+        if (do_too)
+          for (int blk = 0; blk < D / 64; ++blk)
+            tma_load_4d(do_s + blk * 16384, &tmDO, &misc->res_full[qp], blk * 64, head, qrow,
+                        si.b_coord);
+      }
+    }
   }
   if (warp == kProducerWarp) {
     tmem_alloc(&misc->tmem_base, 512);
@@ -260,19 +290,6 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   if (warp == kProducerWarp) {
     // whole warp: warp-uniform waits, copies issued by one elected lane
     if (work > 0) {
-      const int qrow = si.q_base + qt * kTileM;
-      if (elect_one()) {
-        mbar_expect_tx(&misc->res_full, Cfg::kQBytes + Cfg::kDoBytes);
-        if (Cfg::kS)
-          for (int blk = 0; blk < D / 64; ++blk)
-            tma_load_4d(q_s + blk * 16384, &tmQ, &misc->res_full, blk * 64, head, qrow,
-                        si.b_coord);
-        if (Cfg::kDP)
-          for (int blk = 0; blk < D / 64; ++blk)
-            tma_load_4d(do_s + blk * 16384, &tmDO, &misc->res_full, blk * 64, head, qrow,
-                        si.b_coord);
-      }
-      __syncwarp();
       uint32_t it = 0;
       bool ok = true;
       bool res_free = !Cfg::kTS;
@@ -282,7 +299,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
           if (st >= static_cast<uint32_t>(Cfg::kStages) && !res_free) {
-            if (!(ok = mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer))) break;
+            for (int qp = 0; qp < kResParts && ok; ++qp)
+              ok = mbar_wait(&misc->a_ready[qp], 0, ab, kDevTimeoutPeer);
+            if (!ok) break;
             res_free = true;
           }
           if (!(ok = mbar_wait(&misc->ring_empty[st], ph ^ 1, ab, kDevTimeoutMma))) break;
@@ -325,7 +344,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       };
       if (Cfg::kStageDs) {
         // the P slots sit in the resident area, free once dO is in TMEM
-        ok = mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer);
+        for (int qp = 0; qp < kResParts && ok; ++qp)
+          ok = mbar_wait(&misc->a_ready[qp], 0, ab, kDevTimeoutPeer);
         for (int j = 0; j < Cfg::kPStages && j < work && ok; ++j) load_p(j);
       }
       for (int j = 0; j < work && ok; ++j) {
@@ -354,8 +374,12 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       constexpr uint32_t kId = idesc_bf16(128, 128, false, false);
       const uint32_t qb = smem_addr(q_s), db = smem_addr(do_s);
       uint32_t it = 0;
-      bool ok = Cfg::kTS || Cfg::kQT ? mbar_wait(&misc->a_ready, 0, ab, kDevTimeoutPeer)
-                                     : mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
+      // SS variant: the whole resident area first; TS / QT: each quarter of
+      // the TMEM operand before the first tile's chunks that read it
+      bool ok = true;
+      if (!(Cfg::kTS || Cfg::kQT))
+        for (int qp = 0; qp < kResParts && ok; ++qp)
+          ok = mbar_wait(&misc->res_full[qp], 0, ab, kDevTimeoutTma);
       for (int j = 0; j < work && ok; ++j) {
         const int b = j & 1;
         if (j >= 2 &&
@@ -367,6 +391,15 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           ++it;
           if (!(ok = mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma))) break;
           const bool is_k = Cfg::kS && c < D / 128;
+          if ((Cfg::kTS || (Cfg::kQT && is_k)) && j == 0) {
+            // K elements [128 cc, +128) of the TMEM operand: quarters
+            // 2cc / kBpp .. (2cc + 1) / kBpp
+            constexpr int kBpp = (D / 64) / kResParts;
+            const int cq = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
+            for (int qp = (2 * cq) / kBpp; qp <= (2 * cq + 1) / kBpp && ok; ++qp)
+              ok = mbar_wait(&misc->a_ready[qp], 0, ab, kDevTimeoutPeer);
+            if (!ok) break;
+          }
           // single dP buffer: tile j's dP waits until every math thread read tile j-1's
           if (Cfg::kQT && c == D / 128 && j > 0 &&
               !(ok = mbar_wait(&misc->dp_free, (j - 1) & 1, ab, kDevTimeoutPeer)))
@@ -410,14 +443,17 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     const float delta_r =
         (row_valid && p.delta) ? p.delta[head * p.ws_head_stride + tok_base + q_idx] : 0.f;
     const bool row_ok = row_valid && lse2_r != -INFINITY;
+
     const int qdoc = (row_valid && p.mask.doc) ? p.mask.doc[si.meta_base + q_abs] : 0;
     const int qa0 = qt * kTileM + q_off;
     const int qa1 = min((qt + 1) * kTileM, si.len_q) - 1 + q_off;
     bool ok = true;
     if ((Cfg::kTS || Cfg::kQT) && work > 0) {
       // resident Q / dO (128-B swizzled rows) -> TMEM lane r, bf16 pairs from
-      // column 256; this warp copies K elements [D/4*(w/4), +D/4) of its rows.
-      ok = mbar_wait(&misc->res_full, 0, ab, kDevTimeoutTma);
+      // column 256; this warp copies K elements [D/4*(w/4), +D/4) of its rows
+      // (quarter w/4 of the operand).
+      static_assert(kScoreGroups == kResParts, "one resident quarter per column group");
+      ok = mbar_wait(&misc->res_full[grp], 0, ab, kDevTimeoutTma);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         const uint8_t* src = Cfg::kS ? q_s : do_s;
@@ -441,7 +477,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       }
       fence_proxy_async_smem();  // the area is refilled by bulk copies next
       tc_fence_before();
-      mbar_arrive(&misc->a_ready);
+      mbar_arrive(&misc->a_ready[grp]);
     }
     if constexpr (MODE == kScoreFwd) {
       // ---- forward pass 1: online softmax over the key tiles ----
@@ -483,15 +519,24 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         }
         const int kc = k0 + c_begin * 32;
         if (!(cls == 1 && kc + kCols <= si.len_k)) {
+          if (!p.mask.doc) {
+            // text only: the row's visible keys are one range (window bound,
+            // causal bound, end of the sequence)
+            const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
+            const int k_hi = min(q_abs, si.len_k - 1);
 #pragma unroll
-          for (int i = 0; i < kCols; ++i) {
-            const int k = kc + i;
-            bool keep = k < si.len_k;
-            if (cls != 1 && keep) {
-              const int kdoc = p.mask.doc ? p.mask.doc[si.meta_base + k] : 0;
-              keep = mask_allows(p.mask.window, q_abs, k, -1, qdoc, -1, kdoc);
+            for (int i = 0; i < kCols; ++i)
+              if (kc + i < k_lo || kc + i > k_hi) sv[i] = -INFINITY;
+          } else {
+#pragma unroll
+            for (int i = 0; i < kCols; ++i) {
+              const int k = kc + i;
+              bool keep = k < si.len_k;
+              if (cls != 1 && keep)
+                keep = mask_allows(p.mask.window, q_abs, k, -1, qdoc, -1,
+                                   p.mask.doc[si.meta_base + k]);
+              if (!keep) sv[i] = -INFINITY;
             }
-            if (!keep) sv[i] = -INFINITY;
           }
         }
         float mt = -INFINITY;
@@ -616,6 +661,17 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           if (cls == 1 && row_ok && kc + 32 <= si.len_k) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) pv[i] = ex2(fmaf(__uint_as_float(sr[i]), kLog2e, -lse2_r));
+          } else if (!p.mask.doc) {
+            // text only: the row's visible keys are one range (window bound,
+            // causal bound, end of the sequence); none for a row without keys
+            const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
+            const int k_hi = row_ok ? min(q_abs, si.len_k - 1) : -1;
+            const float sub = row_ok ? -lse2_r : 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float e = ex2(fmaf(__uint_as_float(sr[i]), kLog2e, sub));
+              pv[i] = (kc + i >= k_lo && kc + i <= k_hi) ? e : 0.f;
+            }
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {

@@ -339,19 +339,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
         for (int i = 0; i < 64; ++i) s[i] = -INFINITY;
       }
-      if (cls != 1) {
+      if (cls != 1 && !meta) {
+        // text only: the row's visible keys are one range (window bound,
+        // causal bound, end of the sequence)
+        const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
+        const int k_hi = min(q_abs, si.len_k - 1);
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (kh + i < k_lo || kh + i > k_hi) s[i] = -INFINITY;
+      } else if (cls != 1) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
           const int k = kh + i;
-          bool keep;
-          if (k >= si.len_k) {
-            keep = false;
-          } else if (meta) {
-            keep = mask_allows(p.mask.window, q_abs, k, qvis, qdoc, kvis[half * 64 + i],
-                               kdoc[half * 64 + i]);
-          } else {
-            keep = mask_allows(p.mask.window, q_abs, k, -1, 0, -1, 0);
-          }
+          const bool keep = k < si.len_k &&
+                            mask_allows(p.mask.window, q_abs, k, qvis, qdoc, kvis[half * 64 + i],
+                                        kdoc[half * 64 + i]);
           if (!keep) s[i] = -INFINITY;
         }
       }
