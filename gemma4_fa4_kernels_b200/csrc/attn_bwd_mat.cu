@@ -766,6 +766,8 @@ struct GemmCfg {
   static constexpr int kStages = kStageBytes > 64 * 1024 ? 2 : 4;
 };
 
+constexpr int kQListCap = 2048;  // query tiles of one sequence listed in shared memory
+
 struct GemmMisc {
   uint64_t full[4];
   uint64_t empty[4];
@@ -776,6 +778,10 @@ struct GemmMisc {
   uint32_t tmem_base;
   int abort;
   uint32_t flag_bits[64];  // forward: rescale flags of up to 2048 key tiles
+  // dV / dK: the query tiles that reach this CTA's key tile, in order:
+  // (query tile within the sequence, scratch slot of the key tile in its row)
+  int qlist_n;             // entries, or -1 when the sequence has more query tiles than fit
+  int2 qlist[kQListCap];
 };
 
 // One k-step of 64 (half a scratch tile): where A and B come from.
@@ -852,6 +858,17 @@ __global__ void __launch_bounds__(192, 1)
           return;
     } else {
       uint8_t* base = WHICH == kGemmDv ? p.p_tiles : p.ds_tiles;
+      const int nl = misc->qlist_n;
+      if (nl >= 0) {  // the listed query tiles
+        for (int gi = 0; gi < G; ++gi) {
+          const int qh = head * G + gi;
+          for (int i = 0; i < nl; ++i) {
+            const int2 e = misc->qlist[i];
+            if (!fn(scratch_tile(base, p, qh, e.y, 0), qh, si.q_base + e.x * kTileM)) return;
+          }
+        }
+        return;
+      }
       for (int gi = 0; gi < G; ++gi) {
         const int qh = head * G + gi;
         for (int qt = 0; qt < n_qt_seq; ++qt) {
@@ -865,6 +882,26 @@ __global__ void __launch_bounds__(192, 1)
     }
   };
 
+  if (!Cfg::kQMajor && warp == 1) {
+    // the query tiles that reach this key tile, gathered once by one warp
+    // (32 ranges per load round): every k-step of the producer and the MMA
+    // warp then reads shared memory instead of rescanning all the ranges
+    int cnt = 0;
+    const bool fits = n_qt_seq <= kQListCap;
+    for (int b0 = 0; b0 < n_qt_seq && fits; b0 += 32) {
+      const int qt = b0 + lane;
+      int4 rg = make_int4(0, 0, 0, 0);
+      bool hit = false;
+      if (qt < n_qt_seq) {
+        rg = p.ranges[first_qg + qt];
+        hit = tile >= rg.x && tile < rg.x + rg.y && rg.z + rg.y <= p.head_cap_tiles;
+      }
+      const uint32_t m = __ballot_sync(0xffffffffu, hit);
+      if (hit) misc->qlist[cnt + __popc(m & ((1u << lane) - 1u))] = make_int2(qt, rg.z + tile - rg.x);
+      cnt += __popc(m);
+    }
+    if (lane == 0) misc->qlist_n = fits ? cnt : -1;
+  }
   if (tid == 0) {
     for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&misc->full[s], 1);
@@ -898,17 +935,20 @@ __global__ void __launch_bounds__(192, 1)
   const CtaAbort ab{&misc->abort, p.err};
 
   // k-step count (two per scratch tile).  Whether a query tile reaches this
-  // key tile does not depend on the GQA head, so the KV-major count scans the
-  // query tiles once instead of once per head.
+  // key tile does not depend on the GQA head, so the KV-major count is the
+  // length of the query-tile list times the group size.
   int n_steps = 0;
   if (Cfg::kQMajor) {
     const int4 rg = p.ranges[qg];
     n_steps = rg.z + rg.y > p.head_cap_tiles ? 0 : 2 * rg.y;
   } else {
-    int n_qt = 0;
-    for (int qt = 0; qt < n_qt_seq; ++qt) {
-      const int4 rg = p.ranges[first_qg + qt];
-      n_qt += (tile >= rg.x && tile < rg.x + rg.y && rg.z + rg.y <= p.head_cap_tiles) ? 1 : 0;
+    int n_qt = misc->qlist_n;
+    if (n_qt < 0) {  // more query tiles than the list holds: count by scanning
+      n_qt = 0;
+      for (int qt = 0; qt < n_qt_seq; ++qt) {
+        const int4 rg = p.ranges[first_qg + qt];
+        n_qt += (tile >= rg.x && tile < rg.x + rg.y && rg.z + rg.y <= p.head_cap_tiles) ? 1 : 0;
+      }
     }
     n_steps = 2 * G * n_qt;
   }
