@@ -792,8 +792,15 @@ struct GemmStep {
   int b_row;         // TMA token coordinate for B (first of 64 rows)
 };
 
+// Warps: 4 producer, 5 MMA, 0-3 and 6-9 epilogue.  An epilogue warp reads the
+// TMEM lane quarter warp % 4 (rows 32 (warp % 4) ..), so each quarter has one
+// warp in each group: warps 0-3 take the accumulator's first column half,
+// warps 6-9 the second.
+constexpr int kGemmThreads = 320;
+constexpr int kGemmEpiThreads = 256;
+
 template <int D, int WHICH, bool PAIR>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     bwd_tile_gemm_kernel(const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmOut,
                          const __grid_constant__ CUtensorMap tmA, const MatParams p) {
@@ -909,7 +916,8 @@ __global__ void __launch_bounds__(192, 1)
     }
     mbar_init(&misc->acc_full, 1);
     mbar_init(&misc->o_done, 1);
-    mbar_init(&misc->o_ready, PAIR ? 8 : 128);  // pair: one arrival per correction warp of each CTA
+    // pair: one arrival per correction warp of each CTA; else one per epilogue thread
+    mbar_init(&misc->o_ready, PAIR ? 2 * kGemmEpiThreads / 32 : kGemmEpiThreads);
     mbar_init(&misc->drain, 1);
     misc->abort = 0;
     fence_mbar_init();
@@ -1102,8 +1110,12 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ---------------- epilogue: TMEM -> bf16 rows ----------------
+    // row er of the tile (TMEM lane quarter warp % 4); columns [c_lo, c_hi)
+    // in 32-column chunks: the first or second half of the accumulator
     bool ok = true;
-    const uint32_t lane_base0 = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int er = (warp & 3) * 32 + lane;
+    const int ehalf = warp < 4 ? 0 : 1;
+    const uint32_t lane_base0 = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     if (WHICH == kGemmO && n_steps > 0) {
       // correction: apply the forward's lazy rescale factors at flagged tiles
       const int4 rg = p.ranges[qg];
@@ -1116,10 +1128,10 @@ __global__ void __launch_bounds__(192, 1)
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        const float a = p.fwd_alpha[(tile_base + j) * 128 + tid];
+        const float a = p.fwd_alpha[(tile_base + j) * 128 + er];
         if (__any_sync(0xffffffffu, a != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; c += 2) {
+          for (int c = ehalf * (D / 64); c < (ehalf + 1) * (D / 64); c += 2) {
             uint32_t r0[32], r1[32];
             tmem_ld32(lane_base0 + c * 32, r0);
             tmem_ld32(lane_base0 + c * 32 + 32, r1);
@@ -1150,8 +1162,10 @@ __global__ void __launch_bounds__(192, 1)
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     const bool have = ok && n_steps > 0;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const int row = tile * 128 + tid;
+    const uint32_t lane_base = lane_base0;
+    const int row = tile * 128 + er;
+    constexpr int kHalfChunks = Cfg::kNB / 64;  // 32-column chunks per epilogue warp
+    const int c_lo = ehalf * kHalfChunks;
     const bool row_valid = Cfg::kQMajor ? row < si.len_q : row < si.len_k;
     float out_scale = 1.f;
     __nv_bfloat16* dst;
@@ -1179,37 +1193,45 @@ __global__ void __launch_bounds__(192, 1)
     const int seq_len = Cfg::kQMajor ? si.len_q : si.len_k;
     const bool via_tma = have && tile * 128 + 128 <= seq_len;
     if (via_tma) {
+      // two 32-column chunks per TMEM wait (one 64-column block of the
+      // 128-B swizzled staging layout)
 #pragma unroll 1
-      for (int c = 0; c < Cfg::kNB / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + c * 32, r);
+      for (int c = c_lo; c < c_lo + kHalfChunks; c += 2) {
+        uint32_t r[2][32];
+        tmem_ld32(lane_base + c * 32, r[0]);
+        tmem_ld32(lane_base + c * 32 + 32, r[1]);
         tmem_wait_ld();
-        reg_fence32(r);
-        uint8_t* rowp = smem + (c >> 1) * 16384 + tid * 128;
+        reg_fence32(r[0]);
+        reg_fence32(r[1]);
+        uint8_t* rowp = smem + (c >> 1) * 16384 + er * 128;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          *reinterpret_cast<uint4*>(rowp + ((((c & 1) * 4 + i) ^ (tid & 7)) << 4)) =
-              make_uint4(pack_bf16x2(__uint_as_float(r[8 * i + 0]) * out_scale,
-                                     __uint_as_float(r[8 * i + 1]) * out_scale),
-                         pack_bf16x2(__uint_as_float(r[8 * i + 2]) * out_scale,
-                                     __uint_as_float(r[8 * i + 3]) * out_scale),
-                         pack_bf16x2(__uint_as_float(r[8 * i + 4]) * out_scale,
-                                     __uint_as_float(r[8 * i + 5]) * out_scale),
-                         pack_bf16x2(__uint_as_float(r[8 * i + 6]) * out_scale,
-                                     __uint_as_float(r[8 * i + 7]) * out_scale));
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<uint4*>(rowp + (((hh * 4 + i) ^ (er & 7)) << 4)) =
+                make_uint4(pack_bf16x2(__uint_as_float(r[hh][8 * i + 0]) * out_scale,
+                                       __uint_as_float(r[hh][8 * i + 1]) * out_scale),
+                           pack_bf16x2(__uint_as_float(r[hh][8 * i + 2]) * out_scale,
+                                       __uint_as_float(r[hh][8 * i + 3]) * out_scale),
+                           pack_bf16x2(__uint_as_float(r[hh][8 * i + 4]) * out_scale,
+                                       __uint_as_float(r[hh][8 * i + 5]) * out_scale),
+                           pack_bf16x2(__uint_as_float(r[hh][8 * i + 6]) * out_scale,
+                                       __uint_as_float(r[hh][8 * i + 7]) * out_scale));
       }
       fence_proxy_async_smem();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(kGemmEpiThreads) : "memory");
       if (tid == 0) {
         const int tok0 = (Cfg::kQMajor ? si.q_base : si.k_base) + tile * 128;
         for (int cb = 0; cb < Cfg::kNB / 64; ++cb)
           tma_store_4d(&tmOut, smem + cb * 16384, half * 256 + cb * 64, head, tok0, si.b_coord);
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        bulk_store_wait_all();
+        // the staging area is read before the CTA's shared memory is released;
+        // the global writes complete with the grid
+        bulk_store_wait_read();
       }
     } else {
 #pragma unroll 1
-      for (int c = 0; c < Cfg::kNB / 32; ++c) {
+      for (int c = c_lo; c < c_lo + kHalfChunks; ++c) {
         uint32_t r[32];
         if (have) {
           tmem_ld32(lane_base + c * 32, r);
@@ -1293,7 +1315,7 @@ static int launch_gemm_impl(const CUtensorMap& tb, const CUtensorMap& tout, cons
   if (e != cudaSuccess) return static_cast<int>(e);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = Cfg::kQMajor ? dim3(grid_y, grid_x) : dim3(grid_x, grid_y);
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
