@@ -79,6 +79,7 @@ def flops_of(cfg) -> dict:
             # tile GEMM does one of dV, dK, dQ
             "bwd_score": 2.0 * h * p * (2 * d), "bwd_gemm_dv": 2.0 * h * p * d,
             "bwd_gemm_dk": 2.0 * h * p * d, "bwd_gemm_dq": 2.0 * h * p * d,
+            "bwd_gemm_dvdk": 2.0 * h * p * (2 * d),  # dV and dK in one launch
             # two-pass forward: S once, then O = P V
             "fwd_score": 2.0 * h * p * d, "fwd_pv": 2.0 * h * p * d}
 

@@ -743,7 +743,11 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
 // =====================================================================================
 // tile GEMM kernel: dV = P^T dO, dK = dS^T Q (KV-major) and dQ = dS K (Q-major)
 // =====================================================================================
-enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2, kGemmO = 3 };
+// kGemmDvDk: dV and dK in one launch.  Their KV-major CTAs have identical
+// sizes (the k-steps of a key tile), so interleaving the two products doubles
+// the number of CTAs of each size and evens out the end of the launch (the
+// largest CTA is a smaller share of each SM's work).
+enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2, kGemmO = 3, kGemmDvDk = 4 };
 
 // dQ CTAs produce all D output columns (A loaded once); dV / dK CTAs produce
 // one 256-column half each, which doubles the KV-major grid for load balance.
@@ -757,7 +761,7 @@ enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2, kGemmO = 3 };
 // arrive on the leader's o_ready.
 template <int D, int WHICH, bool PAIR = false>
 struct GemmCfg {
-  static constexpr bool kQMajor = WHICH >= 2;       // dQ and the forward O
+  static constexpr bool kQMajor = WHICH == kGemmDq || WHICH == kGemmO;  // dQ and the forward O
   static constexpr int kNB = kQMajor ? D : 256;     // output columns per CTA
   static constexpr int kHalves = D / kNB;
   static constexpr int kABytes = 16384;             // 128 rows x 64 deep
@@ -803,6 +807,8 @@ template <int D, int WHICH, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     bwd_tile_gemm_kernel(const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmOut,
+                         const __grid_constant__ CUtensorMap tmB2,    // kGemmDvDk: dK's B (Q)
+                         const __grid_constant__ CUtensorMap tmOut2,  // kGemmDvDk: dK
                          const __grid_constant__ CUtensorMap tmA, const MatParams p) {
   using Cfg = GemmCfg<D, WHICH, PAIR>;
   static_assert(!PAIR || (Cfg::kQMajor && D == 512), "CTA pairs serve the d512 Q-major GEMMs");
@@ -821,6 +827,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int seq, tile, head;  // tile: key tile (dV/dK) or query tile (dQ) within the sequence
   int qg = 0;           // dQ: global query-tile index
   int half = 0;         // dV/dK: which 256-column half
+  int which = WHICH;    // kGemmDvDk: this CTA's product (dV or dK)
   if (Cfg::kQMajor) {
     const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
     // grid (heads, query tiles), head fastest: longest-first over the whole grid
@@ -832,8 +839,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     const int hkv = p.num_q_heads / G;
     const int per_item = hkv * Cfg::kHalves;
-    const int item = blockIdx.x / per_item;
-    const int rest = blockIdx.x % per_item;
+    const int n_prod = WHICH == kGemmDvDk ? 2 : 1;  // kGemmDvDk: a dV item, then the same dK item
+    const int item = blockIdx.x / (per_item * n_prod);
+    const int r2 = blockIdx.x % (per_item * n_prod);
+    if (WHICH == kGemmDvDk) which = r2 < per_item ? kGemmDv : kGemmDk;
+    const int rest = r2 % per_item;
     head = rest / Cfg::kHalves;  // KV head
     half = rest % Cfg::kHalves;
     if (packed) {
@@ -864,7 +874,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!fn(scratch_tile(base, p, head, rg.z, j), kv_head, si.k_base + (rg.x + j) * kTileN))
           return;
     } else {
-      uint8_t* base = WHICH == kGemmDv ? p.p_tiles : p.ds_tiles;
+      uint8_t* base = which == kGemmDv ? p.p_tiles : p.ds_tiles;
       const int nl = misc->qlist_n;
       if (nl >= 0) {  // the listed query tiles
         for (int gi = 0; gi < G; ++gi) {
@@ -995,8 +1005,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 bulk_load(dst, t + h * 8192, 8192, &misc->full[st]);
                 bulk_load(dst + 8192, t + 16384 + h * 8192, 8192, &misc->full[st]);
               }
+              const CUtensorMap* mb = WHICH == kGemmDvDk && which == kGemmDk ? &tmB2 : &tmB;
               for (int blk = 0; blk < Cfg::kNB / 64; ++blk)
-                tma_load_4d(dst + Cfg::kABytes + blk * 8192, &tmB, &misc->full[st],
+                tma_load_4d(dst + Cfg::kABytes + blk * 8192, mb, &misc->full[st],
                             half * 256 + blk * 64, b_head, b_row + h * 64, si.b_coord);
             }
           }
@@ -1174,10 +1185,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       out_scale = row_valid ? p.fwd_inv_l[head * p.ws_head_stride + tok] : 0.f;
       dst = p.o + static_cast<int64_t>(si.b_coord) * p.o_stride[0] +
             static_cast<int64_t>(si.q_base + row) * p.o_stride[1] + static_cast<int64_t>(head) * p.o_stride[2];
-    } else if (WHICH == kGemmDq)
+    } else if (which == kGemmDq)
       dst = p.dq + static_cast<int64_t>(si.b_coord) * p.dq_stride[0] +
             static_cast<int64_t>(si.q_base + row) * p.dq_stride[1] + static_cast<int64_t>(head) * p.dq_stride[2];
-    else if (WHICH == kGemmDv)
+    else if (which == kGemmDv)
       dst = p.dv + static_cast<int64_t>(si.b_coord) * p.dv_stride[0] +
             static_cast<int64_t>(si.k_base + row) * p.dv_stride[1] + static_cast<int64_t>(head) * p.dv_stride[2];
     else
@@ -1222,8 +1233,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       asm volatile("bar.sync 1, %0;" ::"n"(kGemmEpiThreads) : "memory");
       if (tid == 0) {
         const int tok0 = (Cfg::kQMajor ? si.q_base : si.k_base) + tile * 128;
+        const CUtensorMap* mo = WHICH == kGemmDvDk && which == kGemmDk ? &tmOut2 : &tmOut;
         for (int cb = 0; cb < Cfg::kNB / 64; ++cb)
-          tma_store_4d(&tmOut, smem + cb * 16384, half * 256 + cb * 64, head, tok0, si.b_coord);
+          tma_store_4d(mo, smem + cb * 16384, half * 256 + cb * 64, head, tok0, si.b_coord);
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         // the staging area is read before the CTA's shared memory is released;
         // the global writes complete with the grid
@@ -1303,10 +1315,11 @@ int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& 
 
 template <int D, int WHICH, bool PAIR = false>
 static int launch_gemm_impl(const CUtensorMap& tb, const CUtensorMap& tout, const CUtensorMap& ta,
-                            const MatParams& p, int grid_x, int grid_y, cudaStream_t stream) {
+                            const CUtensorMap& tb2, const CUtensorMap& tout2, const MatParams& p,
+                            int grid_x, int grid_y, cudaStream_t stream) {
   using Cfg = GemmCfg<D, WHICH, PAIR>;
-  if (!Cfg::kQMajor) {  // KV-major: (key tile, KV head, half) all along x
-    grid_x *= grid_y * Cfg::kHalves;
+  if (!Cfg::kQMajor) {  // KV-major: (key tile, [product,] KV head, half) all along x
+    grid_x *= grid_y * Cfg::kHalves * (WHICH == kGemmDvDk ? 2 : 1);
     grid_y = 1;
   }
   const int smem = Cfg::kStages * Cfg::kStageBytes + sizeof(GemmMisc);
@@ -1327,7 +1340,7 @@ static int launch_gemm_impl(const CUtensorMap& tb, const CUtensorMap& tout, cons
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  e = cudaLaunchKernelEx(&cfg, kernel, tb, tout, ta, p);
+  e = cudaLaunchKernelEx(&cfg, kernel, tb, tout, tb2, tout2, ta, p);
   if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }
@@ -1342,20 +1355,34 @@ int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const CUtensor
                          cudaStream_t stream) {
   const CUtensorMap& a = ta ? *ta : tb;  // only read by the pair variant
   if (d == 256) {
-    if (which == kGemmDv) return launch_gemm_impl<256, kGemmDv>(tb, tout, a, p, grid_x, grid_y, stream);
-    if (which == kGemmDk) return launch_gemm_impl<256, kGemmDk>(tb, tout, a, p, grid_x, grid_y, stream);
-    return launch_gemm_impl<256, kGemmDq>(tb, tout, a, p, grid_x, grid_y, stream);
+    if (which == kGemmDv)
+      return launch_gemm_impl<256, kGemmDv>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
+    if (which == kGemmDk)
+      return launch_gemm_impl<256, kGemmDk>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
+    return launch_gemm_impl<256, kGemmDq>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
   }
-  if (which == kGemmDv) return launch_gemm_impl<512, kGemmDv>(tb, tout, a, p, grid_x, grid_y, stream);
-  if (which == kGemmDk) return launch_gemm_impl<512, kGemmDk>(tb, tout, a, p, grid_x, grid_y, stream);
+  if (which == kGemmDv)
+    return launch_gemm_impl<512, kGemmDv>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
+  if (which == kGemmDk)
+    return launch_gemm_impl<512, kGemmDk>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
   if (which == kGemmO) {
     if (ta && gemm_pairs_ok(d, which, p))
-      return launch_gemm_impl<512, kGemmO, true>(tb, tout, *ta, p, grid_x, grid_y, stream);
-    return launch_gemm_impl<512, kGemmO>(tb, tout, a, p, grid_x, grid_y, stream);
+      return launch_gemm_impl<512, kGemmO, true>(tb, tout, *ta, tb, tout, p, grid_x, grid_y,
+                                                 stream);
+    return launch_gemm_impl<512, kGemmO>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
   }
   if (ta && gemm_pairs_ok(d, which, p))
-    return launch_gemm_impl<512, kGemmDq, true>(tb, tout, *ta, p, grid_x, grid_y, stream);
-  return launch_gemm_impl<512, kGemmDq>(tb, tout, a, p, grid_x, grid_y, stream);
+    return launch_gemm_impl<512, kGemmDq, true>(tb, tout, *ta, tb, tout, p, grid_x, grid_y,
+                                                stream);
+  return launch_gemm_impl<512, kGemmDq>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
+}
+
+int launch_bwd_tile_gemm_dvdk(int d, const CUtensorMap& tdo, const CUtensorMap& tdv,
+                              const CUtensorMap& tq, const CUtensorMap& tdk, const MatParams& p,
+                              int grid_x, int grid_y, cudaStream_t stream) {
+  if (d == 256)
+    return launch_gemm_impl<256, kGemmDvDk>(tdo, tdv, tdo, tq, tdk, p, grid_x, grid_y, stream);
+  return launch_gemm_impl<512, kGemmDvDk>(tdo, tdv, tdo, tq, tdk, p, grid_x, grid_y, stream);
 }
 
 }  // namespace g4

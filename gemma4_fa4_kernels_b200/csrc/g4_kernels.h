@@ -169,6 +169,11 @@ int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const CUtensor
                          const CUtensorMap* ta, const MatParams& p, int grid_x, int grid_y,
                          cudaStream_t stream);
 bool gemm_pairs_ok(int d, int which, const MatParams& p);
+// dV = P^T dO and dK = dS^T Q in one launch (KV-major CTAs of the two products
+// interleaved): tdo / tq with 64-row boxes, tdv / tdk with 128-row boxes.
+int launch_bwd_tile_gemm_dvdk(int d, const CUtensorMap& tdo, const CUtensorMap& tdv,
+                              const CUtensorMap& tq, const CUtensorMap& tdk, const MatParams& p,
+                              int grid_x, int grid_y, cudaStream_t stream);
 
 template <int DQK>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,

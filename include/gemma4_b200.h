@@ -255,7 +255,9 @@ int g4_prep_bwd(const g4_prep_args* args, void* stream);
  * ranges), 5 mask builder, 6 backward P/dS scores, 7-9 backward dV / dK / dQ
  * tile GEMMs (materialised path), 10 two-pass forward softmax, 11 two-pass
  * forward O = P V, 12 decode, 13 decode combine, 14 preparation forward,
- * 15 preparation backward, 16 preparation dweight reduction, 17 wait self-test.
+ * 15 preparation backward, 16 preparation dweight reduction, 17 wait self-test,
+ * 18 backward dV and dK tile GEMMs in one launch (used instead of 7 and 8 when
+ * the dO and Q operands take at most 80 MiB together).
  *  - g4_launch_count: launches of `kernel_id` issued by this process so far.
  *  - g4_profile_enable(1): every later launch is bracketed by CUDA events on
  *    its own stream; g4_profile_read synchronises those events and returns the
