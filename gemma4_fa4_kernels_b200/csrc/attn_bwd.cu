@@ -44,6 +44,7 @@ namespace g4 {
 // the whole row in flight.
 template <int DV>
 __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const BwdParams p, int64_t tokens_q) {
+  pdl_enter();
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= tokens_q * p.num_q_heads) return;
@@ -97,10 +98,12 @@ int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int64_t tokens_q,
   const int threads = 256;
   const int64_t blocks = (rows * 32 + threads - 1) / threads;
   if (blocks == 0) return 0;
-  if (head_dim_v == 256)
-    bwd_preprocess_kernel<256><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p, tokens_q);
-  else
-    bwd_preprocess_kernel<512><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p, tokens_q);
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const cudaError_t e =
+      head_dim_v == 256
+          ? launch_chained(bwd_preprocess_kernel<256>, grid, dim3(threads), 0, stream, p, tokens_q)
+          : launch_chained(bwd_preprocess_kernel<512>, grid, dim3(threads), 0, stream, p, tokens_q);
+  if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }
 

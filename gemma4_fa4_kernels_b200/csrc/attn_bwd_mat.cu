@@ -57,6 +57,7 @@ __device__ __forceinline__ uint32_t tile_chunk_offset(int r, int c) {
 __global__ void plan_qtile_ranges_kernel(const MatParams p) {
   __shared__ int scan[1024];
   __shared__ int carry;
+  pdl_enter();
   const int tid = threadIdx.x;
   const bool packed = p.layout.packed();
   const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
@@ -184,6 +185,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
                      const __grid_constant__ CUtensorMap tmDO, const MatParams p) {
   using Cfg = ScoreCfg<D, MODE>;
   extern __shared__ __align__(1024) uint8_t smem[];
+  pdl_enter();
   if ((smem_addr(smem) & 1023u) != 0) {
     if (p.err) atomicCAS(p.err, 0, 5);
     return;
@@ -813,6 +815,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   using Cfg = GemmCfg<D, WHICH, PAIR>;
   static_assert(!PAIR || (Cfg::kQMajor && D == 512), "CTA pairs serve the d512 Q-major GEMMs");
   extern __shared__ __align__(1024) uint8_t smem[];
+  pdl_enter();
   if ((smem_addr(smem) & 1023u) != 0) {
     if (p.err) atomicCAS(p.err, 0, 5);
     return;
@@ -1286,7 +1289,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // launchers
 // =====================================================================================
 int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream) {
-  plan_qtile_ranges_kernel<<<1, 1024, 0, stream>>>(p);
+  cudaError_t e = launch_chained(plan_qtile_ranges_kernel, dim3(1), dim3(1024), 0, stream, p);
+  if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -1299,8 +1303,9 @@ static int launch_score_impl(const CUtensorMap& tq, const CUtensorMap& tk, const
   cudaError_t e = cudaFuncSetAttribute(bwd_score_kernel<D, MODE>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(p.num_q_heads, grid_x);
-  bwd_score_kernel<D, MODE><<<grid, kScoreThreads, smem, stream>>>(tq, tk, tv, tdo, p);
+  e = launch_chained(bwd_score_kernel<D, MODE>, dim3(p.num_q_heads, grid_x), dim3(kScoreThreads),
+                     smem, stream, tq, tk, tv, tdo, p);
+  if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -1331,14 +1336,17 @@ static int launch_gemm_impl(const CUtensorMap& tb, const CUtensorMap& tout, cons
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // chained: pdl_enter
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (PAIR) {  // query heads 2i, 2i+1 (grid x) form a cluster
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
   }
   e = cudaLaunchKernelEx(&cfg, kernel, tb, tout, tb2, tout2, ta, p);
   if (e != cudaSuccess) return static_cast<int>(e);

@@ -80,6 +80,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   using Cfg = FwdCfg<DQK>;
   extern __shared__ __align__(1024) uint8_t smem[];
+  pdl_enter();
   if ((smem_addr(smem) & 1023u) != 0) {  // the 128-B swizzle atoms need 1024-B alignment
     if (p.err) atomicCAS(p.err, 0, 5);
     return;
@@ -478,8 +479,9 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<DQK>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(num_q_heads, grid_x, slabs);
-  attn_fwd_kernel<DQK><<<grid, kFwdThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
+  e = launch_chained(attn_fwd_kernel<DQK>, dim3(num_q_heads, grid_x, slabs), dim3(kFwdThreads),
+                     Cfg::kSmemBytes, stream, tq, tk, tv, p);
+  if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }
 

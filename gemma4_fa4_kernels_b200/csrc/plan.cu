@@ -25,6 +25,7 @@ __global__ void plan_tiles_kernel(const int* __restrict__ cu, int nseg, int tile
                                   int* n_tiles, int* seg_first) {
   __shared__ int scan[1024];
   __shared__ int carry;
+  pdl_enter();
   const int tid = threadIdx.x;
   if (tid == 0) carry = 0;
   __syncthreads();
@@ -52,7 +53,9 @@ __global__ void plan_tiles_kernel(const int* __restrict__ cu, int nseg, int tile
 
 int launch_plan_tiles(const int* cu, int nseg, int tile, int2* tiles, int* n_tiles,
                       int* seg_first, cudaStream_t stream) {
-  plan_tiles_kernel<<<1, 1024, 0, stream>>>(cu, nseg, tile, tiles, n_tiles, seg_first);
+  cudaError_t e = launch_chained(plan_tiles_kernel, dim3(1), dim3(1024), 0, stream, cu, nseg,
+                                 tile, tiles, n_tiles, seg_first);
+  if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }
 
