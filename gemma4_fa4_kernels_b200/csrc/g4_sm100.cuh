@@ -298,36 +298,10 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// MMAs and commits are issued by a converged warp: elect.sync picks one lane
+// inside the asm block, so the issuing loop stays warp-uniform (operands in
+// uniform registers; see mbar_wait for the measured issue rates).
 // D[tmem] (+)= A[smem] * B[smem]^T
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// D[tmem] (+)= A[tmem] * B[smem]^T
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on `bar` when every MMA previously issued by this thread completes.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_addr(bar))
-      : "memory");
-}
-
-// Issued by a converged warp: elect.sync picks one lane inside the asm block,
-// so the issuing loop stays warp-uniform (operands in uniform registers).
 __device__ __forceinline__ void umma_ss_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -338,6 +312,7 @@ __device__ __forceinline__ void umma_ss_w(uint32_t d_tmem, uint64_t a_desc, uint
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]^T
 __device__ __forceinline__ void umma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -348,6 +323,7 @@ __device__ __forceinline__ void umma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Arrive once on `bar` when every MMA previously issued by this warp completes.
 __device__ __forceinline__ void umma_commit_w(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
@@ -373,34 +349,10 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
-// M = 256 across the pair (issued by the leader): each CTA's shared memory
-// holds its 128 rows of A at the A descriptor's address and half of B's N
-// columns at the B descriptor's address; each CTA's TMEM receives its 128 rows
-// of D at `d_tmem`.
-__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on `bar` in both CTAs of the pair when every pair MMA previously
-// issued by this thread completes (called by the leader: one commit on its own
-// barrier, one on the peer CTA's copy through its shared::cluster address).
-__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_addr(bar))
-      : "memory");
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          mapa_shared(bar, 1))
-      : "memory");
-}
-
-// Converged-warp forms of the pair MMA and commit (one lane elected inside the asm).
+// M = 256 across the pair (issued by the leader's converged MMA warp): each
+// CTA's shared memory holds its 128 rows of A at the A descriptor's address and
+// half of B's N columns at the B descriptor's address; each CTA's TMEM receives
+// its 128 rows of D at `d_tmem`.
 __device__ __forceinline__ void umma_ss_pair_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                                uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -411,6 +363,9 @@ __device__ __forceinline__ void umma_ss_pair_w(uint32_t d_tmem, uint64_t a_desc,
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Arrive once on `bar` in both CTAs of the pair when every pair MMA previously
+// issued by this warp completes (the leader: one commit on its own barrier,
+// one on the peer CTA's copy through its shared::cluster address).
 __device__ __forceinline__ void umma_commit_pair_both_w(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
