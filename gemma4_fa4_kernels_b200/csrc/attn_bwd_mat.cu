@@ -1208,7 +1208,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool via_tma = have && tile * 128 + 128 <= seq_len;
     if (via_tma) {
       // two 32-column chunks per TMEM wait (one 64-column block of the
-      // 128-B swizzled staging layout)
+      // 128-B swizzled staging layout); each group of four warps syncs on its
+      // own named barrier once a block holds all 128 rows, and its first warp
+      // stores that block at once, so the stores overlap the later blocks
+      const int tok0 = (Cfg::kQMajor ? si.q_base : si.k_base) + tile * 128;
+      const CUtensorMap* mo = WHICH == kGemmDvDk && which == kGemmDk ? &tmOut2 : &tmOut;
+      const bool issuer = lane == 0 && (warp & 3) == 0;  // warp 0 (first half), warp 8 (second)
 #pragma unroll 1
       for (int c = c_lo; c < c_lo + kHalfChunks; c += 2) {
         uint32_t r[2][32];
@@ -1231,19 +1236,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                        __uint_as_float(r[hh][8 * i + 5]) * out_scale),
                            pack_bf16x2(__uint_as_float(r[hh][8 * i + 6]) * out_scale,
                                        __uint_as_float(r[hh][8 * i + 7]) * out_scale));
+        fence_proxy_async_smem();
+        asm volatile("bar.sync %0, %1;" ::"r"(2 + ehalf), "n"(kGemmEpiThreads / 2) : "memory");
+        if (issuer) {
+          tma_store_4d(mo, smem + (c >> 1) * 16384, half * 256 + (c >> 1) * 64, head, tok0,
+                       si.b_coord);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
       }
-      fence_proxy_async_smem();
-      asm volatile("bar.sync 1, %0;" ::"n"(kGemmEpiThreads) : "memory");
-      if (tid == 0) {
-        const int tok0 = (Cfg::kQMajor ? si.q_base : si.k_base) + tile * 128;
-        const CUtensorMap* mo = WHICH == kGemmDvDk && which == kGemmDk ? &tmOut2 : &tmOut;
-        for (int cb = 0; cb < Cfg::kNB / 64; ++cb)
-          tma_store_4d(mo, smem + cb * 16384, half * 256 + cb * 64, head, tok0, si.b_coord);
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        // the staging area is read before the CTA's shared memory is released;
-        // the global writes complete with the grid
-        bulk_store_wait_read();
-      }
+      // the staging area is read before the CTA's shared memory is released;
+      // the global writes complete with the grid
+      if (issuer) bulk_store_wait_read();
     } else {
 #pragma unroll 1
       for (int c = c_lo; c < c_lo + kHalfChunks; ++c) {
