@@ -36,6 +36,7 @@ EXPORTED_SYMBOLS = (
     "g4_attn_bwd_min_workspace_bytes",
     "g4_attn_bwd",
     "g4_attn_bwd_noalloc",
+    "g4_attn_bwd_noalloc_device_error",
     "g4_read_device_error",
     "g4_selftest_wait",
     "g4_build_mask",
@@ -163,6 +164,9 @@ def load() -> ctypes.CDLL:
         lib.g4_read_device_error.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int),
                                              ctypes.c_void_p]
         lib.g4_read_device_error.restype = ctypes.c_int
+        lib.g4_attn_bwd_noalloc_device_error.argtypes = [ctypes.POINTER(ctypes.c_int),
+                                                         ctypes.c_void_p]
+        lib.g4_attn_bwd_noalloc_device_error.restype = ctypes.c_int
         lib.g4_selftest_wait.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                          ctypes.POINTER(ctypes.c_int),
                                          ctypes.POINTER(ctypes.c_double)]

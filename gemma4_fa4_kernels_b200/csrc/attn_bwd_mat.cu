@@ -1205,7 +1205,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // partial tile of a packed segment would spill into the next segment, so
     // partial tiles keep the direct stores.
     const int seq_len = Cfg::kQMajor ? si.len_q : si.len_k;
-    const bool via_tma = have && tile * 128 + 128 <= seq_len;
+    // The choice must be the same for all 128 threads of a column half: the
+    // TMA branch meets named barrier 2 + ehalf once per block, the direct
+    // branch never.  `have` is only warp-uniform (one warp's bounded wait may
+    // expire while another's passes), so the half takes the TMA branch only
+    // when every one of its threads has the accumulator (an AND-reduction on
+    // the same named barrier, which every epilogue thread reaches).
+    const bool via_tma =
+        bar_red_and(2 + ehalf, kGemmEpiThreads / 2, have && tile * 128 + 128 <= seq_len);
     if (via_tma) {
       // two 32-column chunks per TMEM wait (one 64-column block of the
       // 128-B swizzled staging layout); each group of four warps syncs on its

@@ -501,27 +501,18 @@ int run_decode(const g4_attn_args* a, cudaStream_t st) {
 }
 
 // Scratch for g4_attn_bwd_noalloc: a fixed-size static device array instead of
-// a caller-provided workspace.  Host code must not use the symbol itself as a
-// device address; noalloc_scratch() fetches the real address once per device.
+// a caller-provided workspace.  In host code the symbol is only a host-side
+// stand-in, never a device address; noalloc_scratch() asks the runtime for the
+// array's address on the current device.  The lookup runs on every call (it is
+// cheap), so an address never outlives the context it was taken in (a device
+// reset or a re-created primary context gets a fresh one).
 static __device__ __align__(256) uint8_t g_noalloc_scratch[G4_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kMaxDevices] = {};
-
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) return fail(G4_ERR_UNSUPPORTED, "device index out of range");
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+  *out = p;
   return G4_OK;
 }
 
@@ -844,20 +835,28 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
 
 int g4_attn_bwd_noalloc(const g4_attn_args* a, void* stream) {
   g_last_error.clear();
-  if (!a) return fail(G4_ERR_INVALID, "null argument block");
+  int rc = check_common(a);  // sizes are computed from validated arguments only
+  if (rc) return rc;
   const size_t need = plan_workspace(a, 1).total;
   if (need > G4_NOALLOC_SCRATCH_BYTES)
     return fail(G4_ERR_WORKSPACE,
-                "this backward needs %zu bytes of scratch; the allocation-free entry point has "
-                "%u bytes (use g4_attn_bwd with a caller workspace)",
+                "this backward needs at least %zu bytes of scratch; the allocation-free entry "
+                "point has %u bytes (use g4_attn_bwd with a caller workspace)",
                 need, G4_NOALLOC_SCRATCH_BYTES);
   void* scratch = nullptr;
-  int rc = noalloc_scratch(&scratch);
-  if (rc) return rc;
+  if ((rc = noalloc_scratch(&scratch))) return rc;
   g4_attn_args local = *a;
   local.workspace = scratch;
   local.workspace_bytes = G4_NOALLOC_SCRATCH_BYTES;
   return g4_attn_bwd(&local, stream);
+}
+
+int g4_attn_bwd_noalloc_device_error(int* code, void* stream) {
+  if (!code) return fail(G4_ERR_INVALID, "code is required");
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return g4_read_device_error(scratch, code, stream);
 }
 
 // ---------------------------------------------------------------------------------------

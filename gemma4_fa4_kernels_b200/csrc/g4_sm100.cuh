@@ -113,6 +113,22 @@ __device__ __forceinline__ bool elect_one() {
   return e != 0;
 }
 
+// AND of `pred` over the `count` threads that meet on named barrier `id`
+// (bar.red.and): every participant gets the same answer, so a branch on it is
+// uniform across them even when `pred` differs between their warps.
+__device__ __forceinline__ bool bar_red_and(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ bool wait_fail(const CtaAbort& ab, int code) {
   if (!*ab.flag) {  // this wait ran out of time (not an abort raised elsewhere)
     *ab.flag = 1;

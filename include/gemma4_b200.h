@@ -150,15 +150,28 @@ int g4_attn_bwd(const g4_attn_args* args, void* stream);
  * and results as g4_attn_bwd, except that `workspace`/`workspace_bytes` are
  * ignored: scratch comes from one static device array of
  * G4_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads the
- * library keeps until process exit.  A call whose scratch need
- * (g4_attn_bwd_workspace_bytes) exceeds that size fails with
- * G4_ERR_WORKSPACE before any launch.  The first call on a device looks the
- * array up for that device, so make it before any CUDA graph capture.  All
- * calls share the one array: calls that overlap on the GPU (other streams,
- * other threads) race and must be serialised by the caller.
+ * library keeps until process exit.  The arguments are checked first; then a
+ * call whose minimum scratch need (g4_attn_bwd_min_workspace_bytes) exceeds
+ * the array fails with G4_ERR_WORKSPACE before any launch.  Within the array
+ * the backward takes its fastest form that fits (see g4_attn_bwd).  Every call
+ * asks the runtime for the array's address on the current device; the first
+ * call on a device also loads the library's kernels there, so make it before
+ * any CUDA graph capture.  All calls share the one array and its contents
+ * persist between calls: calls that overlap on the GPU (other streams, other
+ * threads) race and must be serialised by the caller.  A bounded wait that
+ * expired inside such a call is read back with
+ * g4_attn_bwd_noalloc_device_error.
  */
 #define G4_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 int g4_attn_bwd_noalloc(const g4_attn_args* args, void* stream);
+
+/*
+ * Synchronise `stream` and read the device error word of the allocation-free
+ * backward's static array on the current device (the counterpart of
+ * g4_read_device_error for g4_attn_bwd_noalloc, whose scratch address callers
+ * never see).  *code receives 0 or a G4 device error as described there.
+ */
+int g4_attn_bwd_noalloc_device_error(int* code, void* stream);
 
 /*
  * Synchronise `stream` and read the device error word of a workspace used by

@@ -258,7 +258,9 @@ def main(reference_src: str) -> None:
 
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    src = args[0] if args else "/root/reference/src"
+    if len(args) != 1:
+        sys.exit("usage: python tests/golden/make_golden.py <reference src dir> [--prep-only]")
+    src = args[0]
     if "--prep-only" in sys.argv:
         sys.path.insert(0, src)
         prep_cases()

@@ -8,8 +8,9 @@ GPU) and this entry point uses it instead of a caller workspace.
 
 These tests call it through the C ABI and check that two calls in a row give
 the same gradients as ``g4_attn_bwd`` with a caller workspace, within the
-parity tolerance, and that a call needing more scratch than the array holds is
-refused before any launch.  The file is named so that pytest collects it last.
+parity tolerance, with the array's device error word still 0 after each call,
+and that a call whose minimum scratch exceeds the array is refused before any
+launch.  The file is named so that pytest collects it last.
 """
 
 import ctypes
@@ -51,9 +52,14 @@ def test_noalloc_backward_matches_workspace_backward_twice(shape):
     q, k, v, dout = make_inputs((b, s, hq, d), (b, s, hkv, d), (b, s, hkv, d), seed=77)
     out, lse = ops.attn_fwd(q, k, v, window=window)
     ref = ops.attn_bwd(q, k, v, out, lse, dout, window=window)
+    lib = _lib.load()
     for _ in range(2):
         got = _noalloc_bwd(q, k, v, out, lse, dout, window)
-        torch.cuda.synchronize()
+        code = ctypes.c_int(-1)
+        rc = lib.g4_attn_bwd_noalloc_device_error(ctypes.byref(code),
+                                                  torch.cuda.current_stream().cuda_stream)
+        assert rc == _lib.G4_OK, _lib.last_error()
+        assert code.value == 0
         for g, r in zip(got, ref):
             assert rel_l2(g.float().cpu().numpy(), r.float().cpu().numpy()) <= REL_L2_TOL
 
@@ -61,7 +67,8 @@ def test_noalloc_backward_matches_workspace_backward_twice(shape):
 def test_noalloc_backward_refuses_oversized_scratch_before_launch():
     lib = _lib.load()
     a = _lib.G4AttnArgs()
-    # 32 heads x 131072 tokens needs ~32 MiB of scratch: more than the array holds.
+    # 32 heads x 131072 tokens needs at least 32 MiB of scratch (the per-row
+    # delta and log2 LSE): more than the array holds.
     tokens = 131072
     a.q, a.k, a.v, a.o, a.lse = 0x1000, 0x2000, 0x3000, 0x4000, 0x5000
     a.dout, a.dq, a.dk, a.dv = 0x6000, 0x7000, 0x8000, 0x9000
@@ -71,7 +78,7 @@ def test_noalloc_backward_refuses_oversized_scratch_before_launch():
     a.lse_stride[:] = [32 * tokens, tokens]
     a.batch, a.seqlen_q, a.seqlen_k = 1, tokens, tokens
     a.num_q_heads, a.num_kv_heads, a.head_dim_qk, a.head_dim_v = 32, 4, 512, 512
-    assert lib.g4_attn_bwd_workspace_bytes(ctypes.byref(a)) > _lib.NOALLOC_SCRATCH_BYTES
+    assert lib.g4_attn_bwd_min_workspace_bytes(ctypes.byref(a)) > _lib.NOALLOC_SCRATCH_BYTES
     rc = lib.g4_attn_bwd_noalloc(ctypes.byref(a), None)
     assert rc == _lib.G4_ERR_WORKSPACE
     assert "scratch" in _lib.last_error()
