@@ -13,7 +13,7 @@ import threading
 _PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG_DIR, "libgemma4_b200.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 G4_OK = 0
 G4_ERR_INVALID = 1
@@ -95,6 +95,8 @@ class G4AttnArgs(ctypes.Structure):
         ("document_ids", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("causal_shift", ctypes.c_int32),
+        ("grad_accumulate", ctypes.c_int32),
     ]
 
 

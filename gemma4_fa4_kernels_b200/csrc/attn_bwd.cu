@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(192, 1)
     qt = nqt - 1 - static_cast<int>(blockIdx.x % nqt);
   }
   const SeqInfo si = p.layout.seq(seq);
-  const int q_off = si.len_k - si.len_q;
+  const int q_off = si.q_off;
   const int64_t tok_base = p.layout.packed() ? si.q_base : static_cast<int64_t>(seq) * p.layout.seqlen_q;
 
   if (tid == 0) {
@@ -536,7 +536,7 @@ __global__ void __launch_bounds__(192, 1)
     kt = static_cast<int>(blockIdx.x % nkt);
   }
   const SeqInfo si = p.layout.seq(seq);
-  const int q_off = si.len_k - si.len_q;
+  const int q_off = si.q_off;
   const int64_t tok_base = p.layout.packed() ? si.q_base : static_cast<int64_t>(seq) * p.layout.seqlen_q;
 
   if (tid == 0) {

@@ -32,6 +32,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "g4_attn.cuh"
 #include "g4_kernels.h"
 #include "g4_sm100.cuh"
@@ -40,9 +42,71 @@ namespace g4 {
 
 constexpr int kTileBytes = 32768;  // one 128x128 bf16 scratch tile
 
+// Scratch tiles of a band: [query head of the band][band slot], 32 KB each.
+__device__ __forceinline__ int64_t band_tile_index(const MatParams& p, int head, int slot) {
+  return static_cast<int64_t>(head - p.band_h0 * p.group) * p.head_cap_tiles + slot;
+}
 __device__ __forceinline__ uint8_t* scratch_tile(uint8_t* base, const MatParams& p, int head,
                                                  int offset, int slot) {
-  return base + ((static_cast<int64_t>(head) * p.head_cap_tiles + offset + slot) * kTileBytes);
+  return base + band_tile_index(p, head, offset + slot) * kTileBytes;
+}
+
+// The flattened query tile of band row y: the band's second range first, then
+// its first, each from its last tile (the longest causal rows first), or -1.
+__device__ __forceinline__ int band_qtile(const MatParams& p, int y) {
+  const int n1 = p.band_g[3] - p.band_g[2];
+  const int n0 = p.band_g[1] - p.band_g[0];
+  if (y < n1) return p.band_g[3] - 1 - y;
+  if (y < n1 + n0) return p.band_g[1] - 1 - (y - n1);
+  return -1;
+}
+__device__ __forceinline__ int band_rows(const MatParams& p) {
+  return (p.band_g[1] - p.band_g[0]) + (p.band_g[3] - p.band_g[2]);
+}
+__device__ __forceinline__ bool in_band(const MatParams& p, int g) {
+  return (g >= p.band_g[0] && g < p.band_g[1]) || (g >= p.band_g[2] && g < p.band_g[3]);
+}
+// Band slots: the key tiles of the band's first range come first, those of
+// the second follow.  `prefix` is a query tile's offset in the problem-wide
+// prefix sum (ranges[g].z).
+struct BandSlots {
+  int off0, len0, off1;
+  __device__ __forceinline__ BandSlots(const MatParams& p) {
+    off0 = 0;
+    len0 = 0;
+    off1 = 0;
+    if (p.band_g[1] > p.band_g[0]) {
+      off0 = p.ranges[p.band_g[0]].z;
+      const int4 l = p.ranges[p.band_g[1] - 1];
+      len0 = l.z + l.y - off0;
+    }
+    if (p.band_g[3] > p.band_g[2]) off1 = p.ranges[p.band_g[2]].z;
+  }
+  __device__ __forceinline__ int slot(const MatParams& p, int g, int prefix) const {
+    return (g >= p.band_g[0] && g < p.band_g[1]) ? prefix - off0 : len0 + prefix - off1;
+  }
+};
+
+// Key tile j of query tile g (range rg): the j-th listed tile for metadata
+// masks, else kt_lo + j.
+__device__ __forceinline__ int qtile_key(const MatParams& p, int g, const int4& rg, int j) {
+  return p.klist ? p.klist[static_cast<int64_t>(g) * p.klist_stride + j] : rg.x + j;
+}
+// Position of key tile kt among query tile g's key tiles, or -1 (lists are
+// sorted ascending and start at rg.x).
+__device__ __forceinline__ int qtile_key_pos(const MatParams& p, int g, const int4& rg, int kt) {
+  if (kt < rg.x) return -1;
+  if (!p.klist) return kt < rg.x + rg.y ? kt - rg.x : -1;
+  const int* l = p.klist + static_cast<int64_t>(g) * p.klist_stride;
+  int lo = 0, hi = rg.y - 1;
+  while (lo <= hi) {
+    const int mid = (lo + hi) >> 1;
+    const int v = l[mid];
+    if (v == kt) return mid;
+    if (v < kt) lo = mid + 1;
+    else hi = mid - 1;
+  }
+  return -1;
 }
 
 // byte offset of the 16-B chunk holding columns [8c, 8c+8) of row r
@@ -77,7 +141,7 @@ __global__ void plan_qtile_ranges_kernel(const MatParams p) {
         qt = g % p.n_qt_fixed;
       }
       const SeqInfo si = p.layout.seq(seq);
-      const int q_off = si.len_k - si.len_q;
+      const int q_off = si.q_off;
       const int qa0 = qt * kTileM + q_off;
       const int qa1 = min((qt + 1) * kTileM, si.len_q) - 1 + q_off;
       const int lo = p.mask.window > 0 ? max(0, qa0 - p.mask.window + 1) : 0;
@@ -100,7 +164,6 @@ __global__ void plan_qtile_ranges_kernel(const MatParams p) {
     if (tid == 1023) carry += scan[1023];
     __syncthreads();
   }
-  if (tid == 0 && carry > p.head_cap_tiles && p.err) atomicCAS(p.err, 0, 6);
 }
 
 // =====================================================================================
@@ -200,19 +263,20 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   // grid (heads, query tiles): the head index varies fastest in launch order, so
   // every head's longest causal rows are dispatched first (longest-first over
   // the whole grid, which keeps the tail of the launch short)
-  const int head = blockIdx.x;
+  const int head = p.band_h0 * p.group + static_cast<int>(blockIdx.x);
   const int kv_head = head / p.group;
   const bool packed = p.layout.packed();
   const int n_tiles = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
-  if (static_cast<int>(blockIdx.y) >= n_tiles) return;
-  const int g = n_tiles - 1 - static_cast<int>(blockIdx.y);  // longest causal rows first
+  const int g = band_qtile(p, static_cast<int>(blockIdx.y));  // longest causal rows first
+  if (g < 0 || g >= n_tiles) return;
   const int4 rg = p.ranges[g];
-  const int kt_lo = rg.x, n_kt = rg.y, t_off = rg.z, seq = rg.w;
+  const int n_kt = rg.y, seq = rg.w;
+  const int t_off = BandSlots(p).slot(p, g, rg.z);
   const int qt = packed ? p.q_tiles[g].y : g % p.n_qt_fixed;
   const SeqInfo si = p.layout.seq(seq);
-  const int q_off = si.len_k - si.len_q;
+  const int q_off = si.q_off;
   const int64_t tok_base = packed ? si.q_base : static_cast<int64_t>(seq) * p.layout.seqlen_q;
-  const bool cap_ok = t_off + n_kt <= p.head_cap_tiles;
+  const bool cap_ok = t_off >= 0 && t_off + n_kt <= p.head_cap_tiles;
 
   if (tid == 0) {
     for (int qp = 0; qp < kResParts; ++qp) {
@@ -296,7 +360,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       bool ok = true;
       bool res_free = !Cfg::kTS;
       for (int j = 0; j < work && ok; ++j) {
-        const int krow = si.k_base + (kt_lo + j) * kTileN;
+        const int krow = si.k_base + qtile_key(p, g, rg, j) * kTileN;
         for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
           const uint32_t st = it % Cfg::kRingStages, ph = (it / Cfg::kRingStages) & 1;
           ++it;
@@ -490,13 +554,13 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       // once Q is in TMEM; every math thread passed that point before use)
       float* pmax = reinterpret_cast<float*>(res_area + (Cfg::kExtraStages + 2) * 32768);
       float* lsum = pmax + 2 * kScoreGroups * 128;      // [group][128]
-      const int64_t tile_base = static_cast<int64_t>(head) * p.head_cap_tiles + t_off;
+      const int64_t tile_base = band_tile_index(p, head, t_off);
       for (int j = tid; j < work; j += kScoreMathThreads) p.fwd_flags[tile_base + j] = 0;
       asm volatile("bar.sync 2, %0;" ::"n"(kScoreMathThreads) : "memory");
       float m_run = -INFINITY, l_half = 0.f;
       for (int j = 0; j < work; ++j) {
         const int b = j & 1;
-        const int k0 = (kt_lo + j) * kTileN;
+        const int k0 = qtile_key(p, g, rg, j) * kTileN;
         const int cls = p.mask.doc ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
         if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
         ok = __all_sync(0xffffffffu, ok);
@@ -603,7 +667,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     } else
     for (int j = 0; j < work; ++j) {
       const int b = j & 1;
-      const int k0 = (kt_lo + j) * kTileN;
+      const int k0 = qtile_key(p, g, rg, j) * kTileN;
       const int cls = p.mask.doc ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
       if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
       if (ok && Cfg::kTS && MODE == kScoreDs)
@@ -833,21 +897,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int which = WHICH;    // kGemmDvDk: this CTA's product (dV or dK)
   if (Cfg::kQMajor) {
     const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
-    // grid (heads, query tiles), head fastest: longest-first over the whole grid
-    if (static_cast<int>(blockIdx.y) >= n) return;
-    qg = n - 1 - static_cast<int>(blockIdx.y);
-    head = blockIdx.x;
+    // grid (band heads, band query tiles), head fastest: longest-first over the band
+    qg = band_qtile(p, static_cast<int>(blockIdx.y));
+    if (qg < 0 || qg >= n) return;
+    head = p.band_h0 * G + static_cast<int>(blockIdx.x);
     seq = p.ranges[qg].w;
     tile = packed ? p.q_tiles[qg].y : qg % p.n_qt_fixed;
   } else {
-    const int hkv = p.num_q_heads / G;
-    const int per_item = hkv * Cfg::kHalves;
+    const int per_item = p.band_nh * Cfg::kHalves;
     const int n_prod = WHICH == kGemmDvDk ? 2 : 1;  // kGemmDvDk: a dV item, then the same dK item
-    const int item = blockIdx.x / (per_item * n_prod);
+    const int item = p.kv_item0 + static_cast<int>(blockIdx.x) / (per_item * n_prod);
     const int r2 = blockIdx.x % (per_item * n_prod);
     if (WHICH == kGemmDvDk) which = r2 < per_item ? kGemmDv : kGemmDk;
     const int rest = r2 % per_item;
-    head = rest / Cfg::kHalves;  // KV head
+    head = p.band_h0 + rest / Cfg::kHalves;  // KV head
     half = rest % Cfg::kHalves;
     if (packed) {
       if (item >= *p.n_k_tiles) return;
@@ -867,14 +930,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // producer and the MMA thread.
   const int n_qt_seq = (si.len_q + kTileM - 1) / kTileM;
   const int first_qg = packed ? (n_qt_seq > 0 ? p.seg_first_qtile[seq] : 0) : seq * p.n_qt_fixed;
+  const BandSlots bslots(p);
+  // KV-major: the band's query tiles of this sequence that reach this key tile,
+  // in a fixed order (first range, then second): fn(query tile in the sequence,
+  // band slot of the key tile in that query tile's row); stops when fn is false.
+  auto for_each_band_qtile = [&](auto&& fn) {
+    for (int r = 0; r < 2; ++r) {
+      const int ga = max(p.band_g[2 * r], first_qg);
+      const int gb = min(p.band_g[2 * r + 1], first_qg + n_qt_seq);
+      for (int gq = ga; gq < gb; ++gq) {
+        const int4 rg = p.ranges[gq];
+        const int pos = qtile_key_pos(p, gq, rg, tile);
+        if (pos < 0) continue;
+        const int t_off = bslots.slot(p, gq, rg.z);
+        if (t_off < 0 || t_off + rg.y > p.head_cap_tiles) continue;  // not planned into the band
+        if (!fn(gq - first_qg, t_off + pos)) return;
+      }
+    }
+  };
   auto for_each_tile = [&](auto&& fn) {
     if (Cfg::kQMajor) {
       const int4 rg = p.ranges[qg];
       const int kv_head = head / G;
-      if (rg.z + rg.y > p.head_cap_tiles) return;  // planner flagged an overflow
+      const int t_off = bslots.slot(p, qg, rg.z);
+      if (t_off < 0 || t_off + rg.y > p.head_cap_tiles) return;  // not planned into the band
       uint8_t* base = WHICH == kGemmO ? p.p_tiles : p.ds_tiles;
       for (int j = 0; j < rg.y; ++j)
-        if (!fn(scratch_tile(base, p, head, rg.z, j), kv_head, si.k_base + (rg.x + j) * kTileN))
+        if (!fn(scratch_tile(base, p, head, t_off, j), kv_head,
+                si.k_base + qtile_key(p, qg, rg, j) * kTileN))
           return;
     } else {
       uint8_t* base = which == kGemmDv ? p.p_tiles : p.ds_tiles;
@@ -891,34 +974,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       for (int gi = 0; gi < G; ++gi) {
         const int qh = head * G + gi;
-        for (int qt = 0; qt < n_qt_seq; ++qt) {
-          const int4 rg = p.ranges[first_qg + qt];
-          if (tile < rg.x || tile >= rg.x + rg.y) continue;
-          if (rg.z + rg.y > p.head_cap_tiles) continue;  // planner flagged an overflow
-          if (!fn(scratch_tile(base, p, qh, rg.z, tile - rg.x), qh, si.q_base + qt * kTileM))
-            return;
-        }
+        bool go = true;
+        for_each_band_qtile([&](int qt, int slot) {
+          go = fn(scratch_tile(base, p, qh, slot, 0), qh, si.q_base + qt * kTileM);
+          return go;
+        });
+        if (!go) return;
       }
     }
   };
 
   if (!Cfg::kQMajor && warp == 1) {
     // the query tiles that reach this key tile, gathered once by one warp
-    // (32 ranges per load round): every k-step of the producer and the MMA
-    // warp then reads shared memory instead of rescanning all the ranges
+    // (32 candidates per load round): every k-step of the producer and the MMA
+    // warp then reads shared memory instead of rescanning the ranges
     int cnt = 0;
-    const bool fits = n_qt_seq <= kQListCap;
-    for (int b0 = 0; b0 < n_qt_seq && fits; b0 += 32) {
-      const int qt = b0 + lane;
-      int4 rg = make_int4(0, 0, 0, 0);
-      bool hit = false;
-      if (qt < n_qt_seq) {
-        rg = p.ranges[first_qg + qt];
-        hit = tile >= rg.x && tile < rg.x + rg.y && rg.z + rg.y <= p.head_cap_tiles;
+    bool fits = true;
+    for (int r = 0; r < 2 && fits; ++r) {
+      const int ga = max(p.band_g[2 * r], first_qg);
+      const int gb = min(p.band_g[2 * r + 1], first_qg + n_qt_seq);
+      for (int b0 = ga; b0 < gb; b0 += 32) {
+        const int gq = b0 + lane;
+        bool hit = false;
+        int slot = 0;
+        if (gq < gb) {
+          const int4 rg = p.ranges[gq];
+          const int pos = qtile_key_pos(p, gq, rg, tile);
+          if (pos >= 0) {
+            const int t_off = bslots.slot(p, gq, rg.z);
+            hit = t_off >= 0 && t_off + rg.y <= p.head_cap_tiles;
+            slot = t_off + pos;
+          }
+        }
+        const uint32_t m = __ballot_sync(0xffffffffu, hit);
+        if (cnt + __popc(m) > kQListCap) {
+          fits = false;
+          break;
+        }
+        if (hit) misc->qlist[cnt + __popc(m & ((1u << lane) - 1u))] = make_int2(gq - first_qg, slot);
+        cnt += __popc(m);
       }
-      const uint32_t m = __ballot_sync(0xffffffffu, hit);
-      if (hit) misc->qlist[cnt + __popc(m & ((1u << lane) - 1u))] = make_int2(qt, rg.z + tile - rg.x);
-      cnt += __popc(m);
     }
     if (lane == 0) misc->qlist_n = fits ? cnt : -1;
   }
@@ -961,15 +1056,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int n_steps = 0;
   if (Cfg::kQMajor) {
     const int4 rg = p.ranges[qg];
-    n_steps = rg.z + rg.y > p.head_cap_tiles ? 0 : 2 * rg.y;
+    const int t_off = bslots.slot(p, qg, rg.z);
+    n_steps = (t_off < 0 || t_off + rg.y > p.head_cap_tiles) ? 0 : 2 * rg.y;
   } else {
     int n_qt = misc->qlist_n;
     if (n_qt < 0) {  // more query tiles than the list holds: count by scanning
       n_qt = 0;
-      for (int qt = 0; qt < n_qt_seq; ++qt) {
-        const int4 rg = p.ranges[first_qg + qt];
-        n_qt += (tile >= rg.x && tile < rg.x + rg.y && rg.z + rg.y <= p.head_cap_tiles) ? 1 : 0;
-      }
+      for_each_band_qtile([&](int, int) {
+        ++n_qt;
+        return true;
+      });
     }
     n_steps = 2 * G * n_qt;
   }
@@ -1025,8 +1121,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // gather the rescale flags into a bitmask first: a dependent global load
       // per tile on the MMA issue path would stall the tensor pipe
       const int4 rg = p.ranges[qg];
-      const int64_t flag_base = static_cast<int64_t>(head) * p.head_cap_tiles + rg.z;
-      const int64_t peer_base = static_cast<int64_t>(head ^ 1) * p.head_cap_tiles + rg.z;
+      const int t_off = bslots.slot(p, qg, rg.z);
+      const int64_t flag_base = band_tile_index(p, head, t_off);
+      const int64_t peer_base = band_tile_index(p, head ^ 1, t_off);
       for (int w0 = 0; w0 < (rg.y + 31) / 32 && w0 < 64; ++w0) {
         const int j = w0 * 32 + lane;
         const bool f = j < rg.y && (p.fwd_flags[flag_base + j] != 0 ||
@@ -1133,8 +1230,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (WHICH == kGemmO && n_steps > 0) {
       // correction: apply the forward's lazy rescale factors at flagged tiles
       const int4 rg = p.ranges[qg];
-      const int64_t tile_base = static_cast<int64_t>(head) * p.head_cap_tiles + rg.z;
-      const int64_t peer_base = static_cast<int64_t>(head ^ 1) * p.head_cap_tiles + rg.z;
+      const int t_off = bslots.slot(p, qg, rg.z);
+      const int64_t tile_base = band_tile_index(p, head, t_off);
+      const int64_t peer_base = band_tile_index(p, head ^ 1, t_off);
       int events = 0;
       for (int j = 1; j < rg.y && ok; ++j) {
         if (!p.fwd_flags[tile_base + j] && !(PAIR && p.fwd_flags[peer_base + j])) continue;
@@ -1181,6 +1279,81 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr int kHalfChunks = Cfg::kNB / 64;  // 32-column chunks per epilogue warp
     const int c_lo = ehalf * kHalfChunks;
     const bool row_valid = Cfg::kQMajor ? row < si.len_q : row < si.len_k;
+    const bool acc = Cfg::kQMajor ? (WHICH == kGemmDq && p.acc_q != 0) : p.acc_kv != 0;
+    if (acc) {
+      // fp32 accumulation: this CTA's product is added into an fp32 tensor (a
+      // band's partial dV / dK, or a caller's gradient accumulator).  A CTA
+      // without k-steps adds nothing: no query tile of the band reaches it.
+      if (n_steps > 0) {
+        const int len_a = Cfg::kQMajor ? si.len_q : si.len_k;
+        // uniform over the column half, as for the bf16 stores below
+        const bool via_red =
+            bar_red_and(2 + ehalf, kGemmEpiThreads / 2, have && tile * 128 + 128 <= len_a);
+        if (via_red) {
+          const int tok0 = (Cfg::kQMajor ? si.q_base : si.k_base) + tile * 128;
+          const CUtensorMap* mo = WHICH == kGemmDvDk && which == kGemmDk ? &tmOut2 : &tmOut;
+          const bool issuer = lane == 0 && (warp & 3) == 0;
+          // 32 fp32 columns (128 B per row, 16 KB per chunk) staged at a time,
+          // four chunks per half in flight before the staging area is reused
+          constexpr int kRound = 4;
+          uint8_t* stg_half = smem + ehalf * kRound * 16384;
+#pragma unroll 1
+          for (int c0 = 0; c0 < kHalfChunks; c0 += kRound) {
+            if (c0 > 0) {  // the previous round's reduces have read the staging area
+              if (issuer) bulk_store_wait_read();
+              asm volatile("bar.sync %0, %1;" ::"r"(2 + ehalf), "n"(kGemmEpiThreads / 2) : "memory");
+            }
+#pragma unroll 1
+            for (int cc = 0; cc < kRound && c0 + cc < kHalfChunks; ++cc) {
+              const int c = c_lo + c0 + cc;
+              uint32_t r[32];
+              tmem_ld32(lane_base + c * 32, r);
+              tmem_wait_ld();
+              reg_fence32(r);
+              uint8_t* rowp = stg_half + cc * 16384 + er * 128;
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                *reinterpret_cast<uint4*>(rowp + ((i ^ (er & 7)) << 4)) =
+                    make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+              fence_proxy_async_smem();
+              asm volatile("bar.sync %0, %1;" ::"r"(2 + ehalf), "n"(kGemmEpiThreads / 2) : "memory");
+              if (issuer) {
+                tma_reduce_add_4d(mo, stg_half + cc * 16384, half * 256 + c * 32, head, tok0,
+                                  si.b_coord);
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+              }
+            }
+          }
+          if (issuer) bulk_store_wait_read();
+        } else if (have) {
+          // a partial tile of a packed segment: element atomics on valid rows
+          float* adst;
+          if (which == kGemmDq)
+            adst = p.dq_acc + static_cast<int64_t>(si.b_coord) * p.dq_acc_stride[0] +
+                   static_cast<int64_t>(si.q_base + row) * p.dq_acc_stride[1] +
+                   static_cast<int64_t>(head) * p.dq_acc_stride[2];
+          else if (which == kGemmDv)
+            adst = p.dv_acc + static_cast<int64_t>(si.b_coord) * p.dv_acc_stride[0] +
+                   static_cast<int64_t>(si.k_base + row) * p.dv_acc_stride[1] +
+                   static_cast<int64_t>(head) * p.dv_acc_stride[2];
+          else
+            adst = p.dk_acc + static_cast<int64_t>(si.b_coord) * p.dk_acc_stride[0] +
+                   static_cast<int64_t>(si.k_base + row) * p.dk_acc_stride[1] +
+                   static_cast<int64_t>(head) * p.dk_acc_stride[2];
+          adst += half * 256;
+#pragma unroll 1
+          for (int c = c_lo; c < c_lo + kHalfChunks; ++c) {
+            uint32_t r[32];
+            tmem_ld32(lane_base + c * 32, r);
+            tmem_wait_ld();
+            reg_fence32(r);
+            if (row_valid)
+#pragma unroll
+              for (int i = 0; i < 32; ++i) atomicAdd(adst + c * 32 + i, __uint_as_float(r[i]));
+          }
+        }
+      }
+    } else {
     float out_scale = 1.f;
     __nv_bfloat16* dst;
     if (WHICH == kGemmO) {
@@ -1281,6 +1454,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
+    }  // bf16 outputs
   }
 
   tc_fence_before();
@@ -1296,8 +1470,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // =====================================================================================
+// fp32 -> bf16 rows: the final dV / dK of a multi-band backward
+// =====================================================================================
+// src: [row][head][d] fp32, contiguous (row = batch * rows_per_batch + token);
+// dst: bf16 with element strides (batch, token, head).  Eight values per step.
+__global__ void cast_f32_bf16_kernel(const float* __restrict__ src, int64_t rows, int heads, int d,
+                                     __nv_bfloat16* dst, int64_t s0, int64_t s1, int64_t s2,
+                                     int64_t rows_per_batch) {
+  pdl_enter();
+  const int64_t n8 = rows * heads * (d / 8);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = i * 8;
+    const int c = static_cast<int>(e % d);
+    const int64_t rh = e / d;
+    const int h = static_cast<int>(rh % heads);
+    const int64_t row = rh / heads;
+    const int64_t b = row / rows_per_batch, t = row % rows_per_batch;
+    const float4 x0 = reinterpret_cast<const float4*>(src + e)[0];
+    const float4 x1 = reinterpret_cast<const float4*>(src + e)[1];
+    *reinterpret_cast<uint4*>(dst + b * s0 + t * s1 + h * s2 + c) =
+        make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w), pack_bf16x2(x1.x, x1.y),
+                   pack_bf16x2(x1.z, x1.w));
+  }
+}
+
+// =====================================================================================
 // launchers
 // =====================================================================================
+int launch_cast_f32_bf16(const float* src, int64_t rows, int heads, int d, __nv_bfloat16* dst,
+                         const int64_t* dst_stride, int batch, int64_t rows_per_batch,
+                         cudaStream_t stream) {
+  (void)batch;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t n8 = rows * heads * (d / 8);
+  const int64_t blocks = std::min<int64_t>((n8 + 255) / 256, int64_t(sms) * 8);
+  if (blocks <= 0) return 0;
+  cudaError_t e = launch_chained(cast_f32_bf16_kernel, dim3(static_cast<unsigned>(blocks)),
+                                 dim3(256), 0, stream, src, rows, heads, d, dst, dst_stride[0],
+                                 dst_stride[1], dst_stride[2], rows_per_batch);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  return static_cast<int>(cudaGetLastError());
+}
+
 int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream) {
   cudaError_t e = launch_chained(plan_qtile_ranges_kernel, dim3(1), dim3(1024), 0, stream, p);
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -1313,8 +1530,8 @@ static int launch_score_impl(const CUtensorMap& tq, const CUtensorMap& tk, const
   cudaError_t e = cudaFuncSetAttribute(bwd_score_kernel<D, MODE>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
-  e = launch_chained(bwd_score_kernel<D, MODE>, dim3(p.num_q_heads, grid_x), dim3(kScoreThreads),
-                     smem, stream, tq, tk, tv, tdo, p);
+  e = launch_chained(bwd_score_kernel<D, MODE>, dim3(p.band_nh * p.group, grid_x),
+                     dim3(kScoreThreads), smem, stream, tq, tk, tv, tdo, p);
   if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }

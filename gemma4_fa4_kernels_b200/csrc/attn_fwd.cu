@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     qt = nqt - 1 - item / p.layout.batch;  // longest causal rows first
   }
   const SeqInfo si = p.layout.seq(seq);
-  const int q_off = si.len_k - si.len_q;
+  const int q_off = si.q_off;
 
   if (tid == 0) {
     mbar_init(&misc->q_full, 1);

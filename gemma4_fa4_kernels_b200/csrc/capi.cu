@@ -58,6 +58,7 @@ enum KernelId {
   kKPrepDw,
   kKSelftest,
   kKGemmDvDk,
+  kKCast,
   kKCount
 };
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
@@ -65,7 +66,8 @@ const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq
                                            "bwd_gemm_dv", "bwd_gemm_dk", "bwd_gemm_dq",
                                            "fwd_score",   "fwd_pv",      "decode",
                                            "decode_combine", "prep_fwd",  "prep_bwd",
-                                           "prep_dw_reduce", "selftest_wait", "bwd_gemm_dvdk"};
+                                           "prep_dw_reduce", "selftest_wait", "bwd_gemm_dvdk",
+                                           "cast_f32_bf16"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -191,6 +193,11 @@ int check_common(const g4_attn_args* a) {
   if (a->window < 0) return fail(G4_ERR_INVALID, "window must be >= 0");
   if (a->window == 0 && (a->vision_ids || a->document_ids))
     return fail(G4_ERR_UNSUPPORTED, "vision/document metadata applies to local layers only");
+  if (a->causal_shift < 0) return fail(G4_ERR_INVALID, "causal_shift must be >= 0");
+  if (a->causal_shift != 0 && a->window != 0)
+    return fail(G4_ERR_UNSUPPORTED, "causal_shift applies to global layers only");
+  if (a->grad_accumulate != 0 && a->grad_accumulate != 1)
+    return fail(G4_ERR_INVALID, "grad_accumulate must be 0 or 1");
   int rc;
   if ((rc = check_strides(a->q_stride, "q", packed))) return rc;
   if ((rc = check_strides(a->k_stride, "k", packed))) return rc;
@@ -278,36 +285,14 @@ int decode_splits(const g4_attn_args* a) {
   return static_cast<int>((max_tiles + tps - 1) / tps);
 }
 
-// Upper bound of scratch tiles per query head for the materialised backward:
-// exact band sizes for fixed layouts, a per-tile bound for packed layouts.
-int64_t mat_head_cap_tiles(const g4_attn_args* a, int n_qt_total) {
-  const bool packed = a->cu_seqlens_q != nullptr;
-  const int W = a->window;
-  if (packed) {
-    const int64_t kmax = (a->max_seqlen_k + g4::kTileN - 1) / g4::kTileN;
-    int64_t per = kmax;
-    if (W > 0) per = std::min<int64_t>(per, (W + 126) / g4::kTileN + 2);
-    return per * n_qt_total;
-  }
-  const int n_qt = (a->seqlen_q + g4::kTileM - 1) / g4::kTileM;
-  const int q_off = a->seqlen_k - a->seqlen_q;
-  int64_t total = 0;
-  for (int qt = 0; qt < n_qt; ++qt) {
-    const int qa0 = qt * g4::kTileM + q_off;
-    const int qa1 = std::min((qt + 1) * g4::kTileM, a->seqlen_q) - 1 + q_off;
-    const int lo = W > 0 ? std::max(0, qa0 - W + 1) : 0;
-    const int hi = std::min(qa1, a->seqlen_k - 1);
-    if (hi >= lo) total += hi / g4::kTileN - lo / g4::kTileN + 1;
-  }
-  return total * a->batch;
-}
-
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 // Workspace modes: 0 single-kernel forward, 1 backward with recompute kernels,
 // 2 backward with materialised P/dS tiles, 3 two-pass forward (d512, P tiles).
-// Modes 2 and 3 fall back to 1 / 0 when the call is not eligible (vision
-// metadata needs data-dependent key ranges; the two-pass forward is d512 only).
+// plan_workspace lays out the regions every mode shares (and, for modes 2/3,
+// the problem-wide tile plan); the band scratch of modes 2/3 follows
+// w.total (see plan_bands).  Vision metadata keeps modes 2/3 on their
+// fallbacks (1 / 0): its key ranges are data-dependent.
 Workspace plan_workspace(const g4_attn_args* a, int mode) {
   Workspace w;
   const bool packed = a->cu_seqlens_q != nullptr;
@@ -339,7 +324,7 @@ Workspace plan_workspace(const g4_attn_args* a, int mode) {
       off = align256(off + sizeof(int2) * w.max_k_tiles);
     }
   }
-  if (a->vision_ids && a->window > 0) {
+  if (vision) {
     const int64_t meta_len = packed ? a->seqlen_k : int64_t(a->batch) * a->seqlen_k;
     w.pair_last = off;
     off = align256(off + sizeof(int) * meta_len);
@@ -348,47 +333,27 @@ Workspace plan_workspace(const g4_attn_args* a, int mode) {
       off = align256(off + sizeof(int) * meta_len);
     }
   }
+  w.tokens_q = packed ? a->seqlen_q : int64_t(a->batch) * a->seqlen_q;
   if (backward) {
-    w.tokens_q = packed ? a->seqlen_q : int64_t(a->batch) * a->seqlen_q;
     w.delta = off;
     off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
     w.lse2 = off;
     off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
-    if (backward == 2 && !(a->vision_ids && a->window > 0)) {
-      w.materialized = true;
-      w.n_qt_total = packed ? w.max_q_tiles
-                            : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
-      if (packed) {
-        w.seg_first = off;
-        off = align256(off + sizeof(int) * a->batch);
-      }
-      w.ranges = off;
-      off = align256(off + sizeof(int4) * w.n_qt_total);
-      w.head_cap_tiles = mat_head_cap_tiles(a, w.n_qt_total);
-      const size_t tiles = size_t(a->num_q_heads) * size_t(w.head_cap_tiles) * 32768;
-      w.p_tiles = off;
-      off = align256(off + tiles);
-      w.ds_tiles = off;
-      off = align256(off + tiles);
-    }
   }
-  if (two_pass_fwd) {
+  if ((backward == 2 && !vision) || two_pass_fwd) {
     w.materialized = true;
-    w.tokens_q = packed ? a->seqlen_q : int64_t(a->batch) * a->seqlen_q;
     w.n_qt_total = packed ? w.max_q_tiles
                           : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
+    if (packed) {
+      w.seg_first = off;
+      off = align256(off + sizeof(int) * a->batch);
+    }
     w.ranges = off;
     off = align256(off + sizeof(int4) * w.n_qt_total);
-    w.head_cap_tiles = mat_head_cap_tiles(a, w.n_qt_total);
-    const size_t tiles = size_t(a->num_q_heads) * size_t(w.head_cap_tiles);
-    w.p_tiles = off;
-    off = align256(off + tiles * 32768);
-    w.fwd_alpha = off;
-    off = align256(off + tiles * 128 * sizeof(float));
-    w.fwd_flags = off;
-    off = align256(off + tiles * sizeof(int));
-    w.fwd_inv_l = off;
-    off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
+    if (two_pass_fwd) {
+      w.fwd_inv_l = off;
+      off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
+    }
   }
   w.total = off;
   return w;
@@ -407,7 +372,304 @@ g4::SeqLayout make_layout(const g4_attn_args* a) {
   l.cu_q = a->cu_seqlens_q;
   l.cu_k = a->cu_seqlens_k;
   l.meta_stride = a->seqlen_k;
+  l.causal_shift = a->window == 0 ? a->causal_shift : 0;
   return l;
+}
+
+// ---------------------------------------------------------------------------------------
+// materialised path: bands
+// ---------------------------------------------------------------------------------------
+// A band is a set of KV heads and up to two ranges of the flattened query-tile
+// list whose P (and dS) tiles fit the scratch at once.  One launch set runs per
+// band.  Plans, in order of preference:
+//   1. one band (the whole problem; the common case);
+//   2. bands of KV heads over all query tiles (every dV / dK still complete);
+//   3. bands of query tiles over all heads: a band takes tiles from the end of
+//      the list (long causal rows) and from its start (short rows), so every
+//      band is a mix that keeps the SMs evenly loaded; dV / dK are partial per
+//      band and summed in fp32 (TMA reduce-add), then converted once.
+struct Band {
+  int g[4];
+  int h0, nh;          // KV heads
+  int kv_item0, kv_items;  // key-major grid (items are key tiles)
+  int rows;            // query tiles in the band
+};
+
+struct MatPlan {
+  bool ok = false;
+  bool acc_kv = false;   // the dV / dK products add fp32 (caller accumulators or own_acc)
+  bool own_acc = false;  // fp32 dV / dK buffers in the workspace, cast to bf16 at the end
+  int64_t cap = 0;     // scratch tiles per query head of a band
+  int nh_max = 0;
+  size_t p_off = 0, ds_off = 0, alpha_off = 0, flags_off = 0, dk_acc_off = 0, dv_acc_off = 0;
+  size_t total = 0;
+  std::vector<Band> bands;
+};
+
+// Per query tile of the problem: key-tile range, count and sequence; per
+// sequence: the key-major index of its first key tile.
+struct TileTable {
+  std::vector<int> kt_lo, n_kt, seq;
+  std::vector<int> kfirst;  // packed: first key-tile list index of each segment
+  int nk_per_seq = 0;       // fixed: key tiles per sequence
+  bool exact = false;
+};
+
+int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+// Key-tile range of one query tile (text masks; the planner kernel's rule).
+void qtile_range(int len_q, int len_k, int qt, int window, int shift, int* kt_lo, int* n_kt) {
+  const int q_off = len_k - len_q + shift;
+  const int qa0 = qt * g4::kTileM + q_off;
+  const int qa1 = std::min((qt + 1) * g4::kTileM, len_q) - 1 + q_off;
+  const int lo = window > 0 ? std::max(0, qa0 - window + 1) : 0;
+  const int hi = std::min(qa1, len_k - 1);
+  *kt_lo = hi >= lo ? lo / g4::kTileN : 0;
+  *n_kt = hi >= lo ? hi / g4::kTileN - lo / g4::kTileN + 1 : 0;
+}
+
+// Exact table from the sequence lengths (host copies).
+void table_from_lengths(const g4_attn_args* a, const std::vector<int>& len_q,
+                        const std::vector<int>& len_k, TileTable* t) {
+  const int shift = a->window == 0 ? a->causal_shift : 0;
+  const bool packed = a->cu_seqlens_q != nullptr;
+  t->kt_lo.clear();
+  t->n_kt.clear();
+  t->seq.clear();
+  t->kfirst.assign(len_q.size() + 1, 0);
+  for (size_t s = 0; s < len_q.size(); ++s) {
+    const int nqt = ceil_div(len_q[s], g4::kTileM);
+    for (int qt = 0; qt < nqt; ++qt) {
+      int lo, n;
+      qtile_range(len_q[s], len_k[s], qt, a->window, shift, &lo, &n);
+      t->kt_lo.push_back(lo);
+      t->n_kt.push_back(n);
+      t->seq.push_back(static_cast<int>(s));
+    }
+    t->kfirst[s + 1] = t->kfirst[s] + ceil_div(len_k[s], g4::kTileN);
+  }
+  t->nk_per_seq = packed ? 0 : ceil_div(a->seqlen_k, g4::kTileN);
+  t->exact = true;
+}
+
+// Upper bound of the problem's scratch tiles per query head, from arguments
+// alone (no device access): exact for fixed layouts.
+int64_t bound_tiles(const g4_attn_args* a, int n_qt_total) {
+  const bool packed = a->cu_seqlens_q != nullptr;
+  if (packed) {
+    const int64_t kmax = ceil_div(a->max_seqlen_k, g4::kTileN);
+    int64_t per = kmax;
+    if (a->window > 0) per = std::min<int64_t>(per, (a->window + 126) / g4::kTileN + 2);
+    return per * n_qt_total;
+  }
+  TileTable t;
+  std::vector<int> lq(1, a->seqlen_q), lk(1, a->seqlen_k);
+  table_from_lengths(a, lq, lk, &t);
+  int64_t total = 0;
+  for (int n : t.n_kt) total += n;
+  return total * a->batch;
+}
+
+// Bytes per scratch tile and query head: P + dS (backward) or P + its row
+// rescale factors + the tile flag (two-pass forward).
+size_t tile_bytes(bool backward) {
+  return backward ? 2 * 32768 : 32768 + 128 * sizeof(float) + sizeof(int);
+}
+
+// Places a band plan's regions after the shared prefix.
+void place(const g4_attn_args* a, const Workspace& w, bool backward, MatPlan* m) {
+  const int G = a->num_q_heads / a->num_kv_heads;
+  const size_t heads = size_t(m->nh_max) * G;
+  const size_t tiles = heads * size_t(m->cap);
+  size_t off = w.total;
+  if (m->own_acc) {
+    const int64_t tok_k = a->cu_seqlens_q ? a->seqlen_k : int64_t(a->batch) * a->seqlen_k;
+    const size_t acc = size_t(tok_k) * a->num_kv_heads * a->head_dim_qk * sizeof(float);
+    m->dk_acc_off = off;
+    off = align256(off + acc);
+    m->dv_acc_off = off;
+    off = align256(off + acc);
+  }
+  m->p_off = off;
+  off = align256(off + tiles * 32768);
+  if (backward) {
+    m->ds_off = off;
+    off = align256(off + tiles * 32768);
+  } else {
+    m->alpha_off = off;
+    off = align256(off + tiles * 128 * sizeof(float));
+    m->flags_off = off;
+    off = align256(off + tiles * sizeof(int));
+  }
+  m->total = off;
+}
+
+// Single-band size (the *_workspace_bytes queries): every tile of the bound.
+size_t single_band_bytes(const g4_attn_args* a, const Workspace& w, bool backward) {
+  MatPlan m;
+  m.nh_max = a->num_kv_heads;
+  m.cap = bound_tiles(a, w.n_qt_total);
+  place(a, w, backward, &m);
+  return m.total;
+}
+
+// Key-major grid of a band: the key tiles its query tiles reach.
+void band_kv_items(const g4_attn_args* a, const TileTable& t, Band* b) {
+  const bool packed = a->cu_seqlens_q != nullptr;
+  int lo = INT32_MAX, hi = -1;
+  for (int r = 0; r < 2; ++r)
+    for (int g = b->g[2 * r]; g < b->g[2 * r + 1]; ++g) {
+      if (t.n_kt[g] <= 0) continue;
+      const int s = t.seq[g];
+      const int first = packed ? t.kfirst[s] + t.kt_lo[g] : t.kt_lo[g];
+      const int last = packed ? t.kfirst[s] + t.kt_lo[g] + t.n_kt[g] - 1
+                              : t.kt_lo[g] + t.n_kt[g] - 1;
+      lo = std::min(lo, first);
+      hi = std::max(hi, last);
+    }
+  if (hi < lo) {
+    b->kv_item0 = 0;
+    b->kv_items = 0;
+  } else if (packed) {
+    b->kv_item0 = lo;
+    b->kv_items = hi - lo + 1;
+  } else {  // fixed items run key tile major: item = tile * B + sequence
+    b->kv_item0 = lo * a->batch;
+    b->kv_items = (hi - lo + 1) * a->batch;
+  }
+}
+
+// Query-tile bands of capacity `cap` tiles per head (see the comment above).
+std::vector<Band> qtile_bands(const TileTable& t, int64_t cap, int h0, int nh) {
+  std::vector<Band> out;
+  const int n = static_cast<int>(t.n_kt.size());
+  int lo = 0, hi = n - 1;
+  while (lo <= hi) {
+    Band b;
+    b.h0 = h0;
+    b.nh = nh;
+    b.g[0] = b.g[1] = lo;
+    b.g[2] = b.g[3] = hi + 1;
+    int64_t sum = 0;
+    // long rows from the end (at least one tile), up to half the capacity
+    while (hi >= lo && (b.g[2] == b.g[3] || sum + t.n_kt[hi] <= cap / 2)) {
+      sum += t.n_kt[hi];
+      --hi;
+      b.g[2] = hi + 1;
+    }
+    while (lo <= hi && sum + t.n_kt[lo] <= cap) {  // short rows from the start
+      sum += t.n_kt[lo];
+      ++lo;
+      b.g[1] = lo;
+    }
+    while (hi >= lo && sum + t.n_kt[hi] <= cap) {  // room left: more from the end
+      sum += t.n_kt[hi];
+      --hi;
+      b.g[2] = hi + 1;
+    }
+    out.push_back(b);
+  }
+  return out;
+}
+
+// Band plan for a workspace of `ws_bytes`; `t` must be exact unless one band
+// of the bound fits.  Returns false when no band fits (then the compact
+// kernels run).
+bool plan_bands(const g4_attn_args* a, const Workspace& w, bool backward, size_t ws_bytes,
+                const TileTable* t, bool accumulate, MatPlan* m) {
+  const int G = a->num_q_heads / a->num_kv_heads;
+  const int Hkv = a->num_kv_heads;
+  const size_t per = tile_bytes(backward);
+  const size_t avail = ws_bytes > w.total ? ws_bytes - w.total : 0;
+  m->bands.clear();
+  m->ok = false;
+  m->acc_kv = accumulate;
+  auto full_band = [&](int h0, int nh) {
+    Band b;
+    b.g[0] = 0;
+    b.g[1] = w.n_qt_total;
+    b.g[2] = b.g[3] = w.n_qt_total;
+    b.h0 = h0;
+    b.nh = nh;
+    b.rows = w.n_qt_total;
+    // every key tile (zeros for keys no query reaches)
+    const int nk = a->cu_seqlens_q ? w.max_k_tiles
+                                   : a->batch * ceil_div(a->seqlen_k, g4::kTileN);
+    b.kv_item0 = 0;
+    b.kv_items = nk;
+    return b;
+  };
+  // 1. one band over the bound
+  const int64_t bound = bound_tiles(a, w.n_qt_total);
+  {
+    MatPlan c;
+    c.acc_kv = accumulate;
+    c.nh_max = Hkv;
+    c.cap = bound;
+    place(a, w, backward, &c);
+    if (c.total <= ws_bytes && bound > 0) {
+      *m = c;
+      m->bands.push_back(full_band(0, Hkv));
+      m->ok = true;
+      return true;
+    }
+  }
+  if (!t || !t->exact) return false;
+  int64_t total = 0, widest = 0;
+  for (int n : t->n_kt) {
+    total += n;
+    widest = std::max<int64_t>(widest, n);
+  }
+  if (total == 0) return false;
+  // 2. bands of KV heads
+  {
+    const int nh = static_cast<int>(
+        std::min<int64_t>(Hkv, avail / std::max<size_t>(1, size_t(G) * size_t(total) * per)));
+    if (nh >= 1) {
+      MatPlan c;
+      c.acc_kv = accumulate;
+      c.nh_max = nh;
+      c.cap = total;
+      place(a, w, backward, &c);
+      if (c.total <= ws_bytes) {
+        *m = c;
+        for (int h0 = 0; h0 < Hkv; h0 += nh) {
+          Band b = full_band(h0, std::min(nh, Hkv - h0));
+          if (accumulate) band_kv_items(a, *t, &b);
+          m->bands.push_back(b);
+        }
+        m->ok = true;
+        return true;
+      }
+    }
+  }
+  // 3. bands of query tiles (dV / dK summed in fp32: into the caller's
+  // accumulators, or into workspace buffers converted at the end)
+  MatPlan c;
+  c.acc_kv = backward;
+  c.own_acc = backward && !accumulate;
+  for (int nh = Hkv; nh >= 1; nh = nh > 1 ? nh / 2 : 0) {
+    if (Hkv % nh) continue;
+    c.nh_max = nh;
+    c.cap = 0;
+    place(a, w, backward, &c);  // fixed regions (accumulators) with an empty scratch
+    const size_t left = ws_bytes > c.total ? ws_bytes - c.total : 0;
+    const int64_t cap = static_cast<int64_t>(left / (size_t(nh) * G * per)) - 2;  // alignment slack
+    if (cap < widest) continue;
+    c.cap = cap;
+    place(a, w, backward, &c);
+    if (c.total > ws_bytes) continue;
+    *m = c;
+    for (int h0 = 0; h0 < Hkv; h0 += nh)
+      for (Band b : qtile_bands(*t, cap, h0, nh)) {
+        b.rows = (b.g[1] - b.g[0]) + (b.g[3] - b.g[2]);
+        band_kv_items(a, *t, &b);
+        m->bands.push_back(b);
+      }
+    m->ok = true;
+    return true;
+  }
+  return false;
 }
 
 // Common prologue: zero the header, plan packed tiles and metadata bounds.
@@ -446,6 +708,69 @@ int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream
     mask->pair_last = pl;
     mask->pair_first = pf;
   }
+  return G4_OK;
+}
+
+// Exact tile table for a band plan.  Fixed layouts: from the arguments.
+// Packed layouts: the segment lengths are read back from the device (one
+// stream synchronisation, as the reference's host-side schedule also reads
+// cu_seqlens); not possible while the stream is being captured.
+int exact_table(const g4_attn_args* a, cudaStream_t st, TileTable* t) {
+  if (!a->cu_seqlens_q) {
+    std::vector<int> lq(a->batch, a->seqlen_q), lk(a->batch, a->seqlen_k);
+    table_from_lengths(a, lq, lk, t);
+    return G4_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    t->exact = false;
+    return G4_OK;
+  }
+  std::vector<int> cq(a->batch + 1), ck(a->batch + 1);
+  cudaError_t e = cudaMemcpyAsync(cq.data(), a->cu_seqlens_q, sizeof(int) * cq.size(),
+                                  cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(ck.data(), a->cu_seqlens_k, sizeof(int) * ck.size(),
+                        cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "cu_seqlens read-back");
+  std::vector<int> lq(a->batch), lk(a->batch);
+  for (int s = 0; s < a->batch; ++s) {
+    lq[s] = cq[s + 1] - cq[s];
+    lk[s] = ck[s + 1] - ck[s];
+    if (lq[s] < 0 || lk[s] < 0 || lq[s] > lk[s])
+      return fail(G4_ERR_INVALID, "cu_seqlens must be non-decreasing with Sq <= Sk per segment");
+  }
+  table_from_lengths(a, lq, lk, t);
+  return G4_OK;
+}
+
+g4::MatParams mat_band(g4::MatParams m, const Band& b) {
+  for (int i = 0; i < 4; ++i) m.band_g[i] = b.g[i];
+  m.band_h0 = b.h0;
+  m.band_nh = b.nh;
+  m.kv_item0 = b.kv_item0;
+  return m;
+}
+
+// fp32 (D, H, S, B) view for the accumulators, (32, 1, 128, 1) boxes, 128-B swizzle.
+int make_map_f32(CUtensorMap* map, const void* ptr, int64_t d, int64_t h, int64_t s, int64_t b,
+                 int64_t stride_h, int64_t stride_s, int64_t stride_b) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(G4_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (b <= 1) stride_b = stride_s * (s > 0 ? s : 1);
+  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)h, (cuuint64_t)(s > 0 ? s : 1),
+                        (cuuint64_t)(b > 0 ? b : 1)};
+  cuuint64_t strides[3] = {(cuuint64_t)(stride_h * 4), (cuuint64_t)(stride_s * 4),
+                           (cuuint64_t)(stride_b * 4)};
+  cuuint32_t box[4] = {32, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(G4_ERR_INVALID, "fp32 tensor map encoding failed (CUresult %d)", (int)r);
   return G4_OK;
 }
 
@@ -526,7 +851,8 @@ const char* g4_last_error(void) { return g_last_error.c_str(); }
 
 size_t g4_attn_fwd_workspace_bytes(const g4_attn_args* args) {
   if (!args) return 0;
-  return plan_workspace(args, 3).total;
+  const Workspace w = plan_workspace(args, 3);
+  return w.materialized ? single_band_bytes(args, w, false) : w.total;
 }
 
 size_t g4_attn_fwd_min_workspace_bytes(const g4_attn_args* args) {
@@ -536,7 +862,8 @@ size_t g4_attn_fwd_min_workspace_bytes(const g4_attn_args* args) {
 
 size_t g4_attn_bwd_workspace_bytes(const g4_attn_args* args) {
   if (!args) return 0;
-  return plan_workspace(args, 2).total;
+  const Workspace w = plan_workspace(args, 2);
+  return w.materialized ? single_band_bytes(args, w, true) : w.total;
 }
 
 size_t g4_attn_bwd_min_workspace_bytes(const g4_attn_args* args) {
@@ -553,11 +880,19 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
     return fail(G4_ERR_INVALID, "lse strides must be positive");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (decode_eligible(a)) return run_decode(a, st);
-  // Two-pass d512 forward (P tiles in HBM, no QK^T recomputation) when the
-  // workspace holds its scratch; otherwise the single-kernel forward.
+  // Two-pass d512 forward (P tiles in HBM, no QK^T recomputation), one launch
+  // pair per band, when the workspace holds one band's scratch; otherwise the
+  // single-kernel forward.
   const Workspace w3 = plan_workspace(a, 3);
-  const Workspace w =
-      (w3.materialized && a->workspace && a->workspace_bytes >= w3.total) ? w3 : plan_workspace(a, 0);
+  MatPlan mp;
+  if (w3.materialized && a->workspace && a->workspace_bytes >= w3.total) {
+    if (!plan_bands(a, w3, false, a->workspace_bytes, nullptr, false, &mp)) {
+      TileTable t;
+      if ((rc = exact_table(a, st, &t))) return rc;
+      plan_bands(a, w3, false, a->workspace_bytes, &t, false, &mp);
+    }
+  }
+  const Workspace w = mp.ok ? w3 : plan_workspace(a, 0);
   g4::FwdParams p;
   memset(&p, 0, sizeof(p));
   if ((rc = prepare(a, w, false, st, &p.mask))) return rc;
@@ -587,7 +922,7 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
     return rc;
   const int grid_x = packed ? w.max_q_tiles
                             : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
-  if (w.materialized) {
+  if (mp.ok) {
     g4::MatParams m;
     memset(&m, 0, sizeof(m));
     m.layout = p.layout;
@@ -598,10 +933,10 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
     m.q_tiles = p.tiles;
     m.n_q_tiles = p.n_tiles;
     m.ranges = ws_ptr<int4>(a, w.ranges);
-    m.head_cap_tiles = w.head_cap_tiles;
-    m.p_tiles = ws_ptr<uint8_t>(a, w.p_tiles);
-    m.fwd_alpha = ws_ptr<float>(a, w.fwd_alpha);
-    m.fwd_flags = ws_ptr<int>(a, w.fwd_flags);
+    m.head_cap_tiles = mp.cap;
+    m.p_tiles = ws_ptr<uint8_t>(a, mp.p_off);
+    m.fwd_alpha = ws_ptr<float>(a, mp.alpha_off);
+    m.fwd_flags = ws_ptr<int>(a, mp.flags_off);
     m.fwd_inv_l = ws_ptr<float>(a, w.fwd_inv_l);
     m.ws_head_stride = w.tokens_q;
     m.lse_out = a->lse;
@@ -614,30 +949,31 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
     if ((rc = make_map(&tv64, a->v, a->head_dim_v, a->num_kv_heads, a->seqlen_k, bq,
                        a->v_stride[2], a->v_stride[1], a->v_stride[0], 64)))
       return rc;
+    CUtensorMap to128;  // O, written by TMA stores in 128-row tiles
+    if ((rc = make_map(&to128, a->o, a->head_dim_v, a->num_q_heads, a->seqlen_q, bq,
+                       a->o_stride[2], a->o_stride[1], a->o_stride[0], 128)))
+      return rc;
+    CUtensorMap tp;  // the P scratch as bytes: the d512 O = P V GEMM runs as CTA pairs
+    const bool pairs = g4::gemm_pairs_ok(D, 3, m);
+    if (pairs && (rc = make_scratch_map(&tp, m.p_tiles,
+                                        2 * int64_t(mp.nh_max) * p.group * mp.cap)))
+      return rc;
     int e;
     {
       LaunchScope ls(kKPlan, st);
       e = g4::launch_plan_qtile_ranges(m, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "query-tile range planning");
     }
-    {
-      LaunchScope ls(kKFwdScore, st);
-      e = g4::launch_bwd_score(D, 2, tq, tk, tv, tq, m, w.n_qt_total, st);
-      if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward score launch");
-    }
-    CUtensorMap to128;  // O, written by TMA stores in 128-row tiles
-    if ((rc = make_map(&to128, a->o, a->head_dim_v, a->num_q_heads, a->seqlen_q, bq,
-                       a->o_stride[2], a->o_stride[1], a->o_stride[0], 128)))
-      return rc;
-    {
+    for (const Band& b : mp.bands) {
+      const g4::MatParams mb = mat_band(m, b);
+      {
+        LaunchScope ls(kKFwdScore, st);
+        e = g4::launch_bwd_score(D, 2, tq, tk, tv, tq, mb, b.rows, st);
+        if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward score launch");
+      }
       LaunchScope ls(kKFwdPv, st);
-      CUtensorMap tp;  // the P scratch as bytes: the d512 O = P V GEMM runs as CTA pairs
-      const bool pairs = g4::gemm_pairs_ok(D, 3, m);
-      if (pairs && (rc = make_scratch_map(&tp, m.p_tiles,
-                                          2 * int64_t(a->num_q_heads) * w.head_cap_tiles)))
-        return rc;
-      e = g4::launch_bwd_tile_gemm(D, 3, tv64, to128, pairs ? &tp : nullptr, m, w.n_qt_total,
-                                   a->num_q_heads, st);
+      e = g4::launch_bwd_tile_gemm(D, 3, tv64, to128, pairs ? &tp : nullptr, mb, b.rows,
+                                   b.nh * p.group, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward PV launch");
     }
     return G4_OK;
@@ -666,11 +1002,25 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
   if (!packed && (a->lse_stride[0] <= 0 || a->lse_stride[1] <= 0))
     return fail(G4_ERR_INVALID, "lse strides must be positive");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Materialised P/dS when eligible and the workspace holds the scratch,
-  // otherwise the recompute kernels (small workspaces, vision metadata).
+  const bool accumulate = a->grad_accumulate != 0;
+  // Materialised P/dS, band by band, when eligible and the workspace holds one
+  // band's scratch; otherwise the recompute kernels (small workspaces, vision
+  // metadata).
   const Workspace wm = plan_workspace(a, 2);
-  const Workspace w =
-      (wm.materialized && a->workspace && a->workspace_bytes >= wm.total) ? wm : plan_workspace(a, 1);
+  MatPlan mp;
+  if (wm.materialized && a->workspace && a->workspace_bytes >= wm.total) {
+    if (!plan_bands(a, wm, true, a->workspace_bytes, nullptr, accumulate, &mp)) {
+      TileTable t;
+      if ((rc = exact_table(a, st, &t))) return rc;
+      plan_bands(a, wm, true, a->workspace_bytes, &t, accumulate, &mp);
+    }
+  }
+  if (accumulate && !mp.ok)
+    return fail(G4_ERR_WORKSPACE,
+                "gradient accumulation runs on the materialised backward only; the workspace "
+                "(%zu bytes) holds no band of its scratch",
+                a->workspace_bytes);
+  const Workspace w = mp.ok ? wm : plan_workspace(a, 1);
   g4::BwdParams p;
   memset(&p, 0, sizeof(p));
   if ((rc = prepare(a, w, true, st, &p.mask))) return rc;
@@ -729,7 +1079,7 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     return rc;
   const int gq = packed ? w.max_q_tiles : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
   const int gk = packed ? w.max_k_tiles : a->batch * ((a->seqlen_k + g4::kTileN - 1) / g4::kTileN);
-  if (w.materialized) {
+  if (mp.ok) {
     g4::MatParams m;
     memset(&m, 0, sizeof(m));
     m.layout = p.layout;
@@ -743,9 +1093,9 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     m.n_k_tiles = p.n_k_tiles;
     m.seg_first_qtile = packed ? ws_ptr<int>(a, w.seg_first) : nullptr;
     m.ranges = ws_ptr<int4>(a, w.ranges);
-    m.head_cap_tiles = w.head_cap_tiles;
-    m.p_tiles = ws_ptr<uint8_t>(a, w.p_tiles);
-    m.ds_tiles = ws_ptr<uint8_t>(a, w.ds_tiles);
+    m.head_cap_tiles = mp.cap;
+    m.p_tiles = ws_ptr<uint8_t>(a, mp.p_off);
+    m.ds_tiles = ws_ptr<uint8_t>(a, mp.ds_off);
     m.lse2 = p.lse2;
     m.delta = p.delta;
     m.ws_head_stride = p.ws_head_stride;
@@ -758,6 +1108,26 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
       m.dv_stride[i] = p.dv_stride[i];
     }
     m.err = p.err;
+    const int Hkv = a->num_kv_heads;
+    const int64_t tok_k = packed ? a->seqlen_k : int64_t(a->batch) * a->seqlen_k;
+    // fp32 destinations: the caller's accumulators, or the band sums of dV / dK
+    m.acc_q = accumulate ? 1 : 0;
+    m.acc_kv = mp.acc_kv ? 1 : 0;
+    if (accumulate) {
+      m.dq_acc = static_cast<float*>(a->dq);
+      m.dk_acc = static_cast<float*>(a->dk);
+      m.dv_acc = static_cast<float*>(a->dv);
+      for (int i = 0; i < 3; ++i) {
+        m.dq_acc_stride[i] = a->dq_stride[i];
+        m.dk_acc_stride[i] = a->dk_stride[i];
+        m.dv_acc_stride[i] = a->dv_stride[i];
+      }
+    } else if (mp.own_acc) {
+      m.dk_acc = ws_ptr<float>(a, mp.dk_acc_off);
+      m.dv_acc = ws_ptr<float>(a, mp.dv_acc_off);
+      const int64_t st_acc[3] = {packed ? 0 : int64_t(a->seqlen_k) * Hkv * D, int64_t(Hkv) * D, D};
+      for (int i = 0; i < 3; ++i) m.dk_acc_stride[i] = m.dv_acc_stride[i] = st_acc[i];
+    }
     CUtensorMap tq64, tdo64;
     if ((rc = make_map(&tq64, a->q, D, a->num_q_heads, a->seqlen_q, bq, a->q_stride[2],
                        a->q_stride[1], a->q_stride[0], 64)))
@@ -765,56 +1135,92 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     if ((rc = make_map(&tdo64, a->dout, a->head_dim_v, a->num_q_heads, a->seqlen_q, bq,
                        a->do_stride[2], a->do_stride[1], a->do_stride[0], 64)))
       return rc;
-    CUtensorMap tdq128, tdk128, tdv128;  // gradients, written by TMA stores in 128-row tiles
-    if ((rc = make_map(&tdq128, a->dq, D, a->num_q_heads, a->seqlen_q, bq, a->dq_stride[2],
-                       a->dq_stride[1], a->dq_stride[0], 128)))
+    // gradients: bf16 TMA stores in 128-row tiles, or fp32 reduce-adds
+    CUtensorMap tdq, tdk, tdv;
+    if (accumulate) {
+      if ((rc = make_map_f32(&tdq, a->dq, D, a->num_q_heads, a->seqlen_q, bq, a->dq_stride[2],
+                             a->dq_stride[1], a->dq_stride[0])))
+        return rc;
+    } else if ((rc = make_map(&tdq, a->dq, D, a->num_q_heads, a->seqlen_q, bq, a->dq_stride[2],
+                              a->dq_stride[1], a->dq_stride[0], 128))) {
       return rc;
-    if ((rc = make_map(&tdk128, a->dk, D, a->num_kv_heads, a->seqlen_k, bq, a->dk_stride[2],
-                       a->dk_stride[1], a->dk_stride[0], 128)))
-      return rc;
-    if ((rc = make_map(&tdv128, a->dv, a->head_dim_v, a->num_kv_heads, a->seqlen_k, bq,
-                       a->dv_stride[2], a->dv_stride[1], a->dv_stride[0], 128)))
+    }
+    if (mp.acc_kv) {
+      if ((rc = make_map_f32(&tdk, m.dk_acc, D, Hkv, a->seqlen_k, bq, m.dk_acc_stride[2],
+                             m.dk_acc_stride[1], m.dk_acc_stride[0])))
+        return rc;
+      if ((rc = make_map_f32(&tdv, m.dv_acc, a->head_dim_v, Hkv, a->seqlen_k, bq,
+                             m.dv_acc_stride[2], m.dv_acc_stride[1], m.dv_acc_stride[0])))
+        return rc;
+    } else {
+      if ((rc = make_map(&tdk, a->dk, D, Hkv, a->seqlen_k, bq, a->dk_stride[2], a->dk_stride[1],
+                         a->dk_stride[0], 128)))
+        return rc;
+      if ((rc = make_map(&tdv, a->dv, a->head_dim_v, Hkv, a->seqlen_k, bq, a->dv_stride[2],
+                         a->dv_stride[1], a->dv_stride[0], 128)))
+        return rc;
+    }
+    CUtensorMap tds;  // the dS scratch as bytes: the d512 dQ GEMM runs as CTA pairs
+    const bool pairs = g4::gemm_pairs_ok(D, 2, m);
+    if (pairs && (rc = make_scratch_map(&tds, m.ds_tiles,
+                                        2 * int64_t(mp.nh_max) * p.group * mp.cap)))
       return rc;
     {
       LaunchScope ls(kKPlan, st);
       e = g4::launch_plan_qtile_ranges(m, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "query-tile range planning");
     }
-    for (int pass = 0; pass < (D == 512 ? 2 : 1); ++pass) {
-      LaunchScope ls(kKScore, st);
-      e = g4::launch_bwd_score(D, pass, tq, tk, tv, tdo, m, w.n_qt_total, st);
-      if (e) return cuda_fail(static_cast<cudaError_t>(e), "score launch");
+    if (mp.own_acc) {
+      const size_t acc = size_t(tok_k) * Hkv * D * sizeof(float);
+      cudaError_t ce = cudaMemsetAsync(m.dk_acc, 0, acc, st);
+      if (ce == cudaSuccess) ce = cudaMemsetAsync(m.dv_acc, 0, acc, st);
+      if (ce != cudaSuccess) return cuda_fail(ce, "accumulator reset");
     }
     // dV and dK in one launch evens out the end of the KV-major grid, but it
     // streams both B operands (dO and Q) at once: only when together they take
     // at most 80 MiB of the 126 MB L2 (measured: 64 MiB, -12%; 256 MiB, no gain).
     const int64_t b_bytes =
         int64_t(w.tokens_q) * a->num_q_heads * (int64_t(D) + a->head_dim_v) * 2;
-    if (b_bytes <= (int64_t(80) << 20)) {
-      LaunchScope ls(kKGemmDvDk, st);
-      e = g4::launch_bwd_tile_gemm_dvdk(D, tdo64, tdv128, tq64, tdk128, m, gk, a->num_kv_heads,
-                                        st);
-      if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV/dK launch");
-    } else {
-      {
-        LaunchScope ls(kKGemmDv, st);
-        e = g4::launch_bwd_tile_gemm(D, 0, tdo64, tdv128, nullptr, m, gk, a->num_kv_heads, st);
-        if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV launch");
+    for (const Band& b : mp.bands) {
+      const g4::MatParams mb = mat_band(m, b);
+      for (int pass = 0; pass < (D == 512 ? 2 : 1); ++pass) {
+        LaunchScope ls(kKScore, st);
+        e = g4::launch_bwd_score(D, pass, tq, tk, tv, tdo, mb, b.rows, st);
+        if (e) return cuda_fail(static_cast<cudaError_t>(e), "score launch");
       }
-      LaunchScope ls(kKGemmDk, st);
-      e = g4::launch_bwd_tile_gemm(D, 1, tq64, tdk128, nullptr, m, gk, a->num_kv_heads, st);
-      if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK launch");
-    }
-    {
+      if (b.kv_items > 0) {
+        if (b_bytes <= (int64_t(80) << 20)) {
+          LaunchScope ls(kKGemmDvDk, st);
+          e = g4::launch_bwd_tile_gemm_dvdk(D, tdo64, tdv, tq64, tdk, mb, b.kv_items, b.nh, st);
+          if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV/dK launch");
+        } else {
+          {
+            LaunchScope ls(kKGemmDv, st);
+            e = g4::launch_bwd_tile_gemm(D, 0, tdo64, tdv, nullptr, mb, b.kv_items, b.nh, st);
+            if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV launch");
+          }
+          LaunchScope ls(kKGemmDk, st);
+          e = g4::launch_bwd_tile_gemm(D, 1, tq64, tdk, nullptr, mb, b.kv_items, b.nh, st);
+          if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK launch");
+        }
+      }
       LaunchScope ls(kKGemmDq, st);
-      CUtensorMap tds;  // the dS scratch as bytes: the d512 dQ GEMM runs as CTA pairs
-      const bool pairs = g4::gemm_pairs_ok(D, 2, m);
-      if (pairs && (rc = make_scratch_map(&tds, m.ds_tiles,
-                                          2 * int64_t(a->num_q_heads) * w.head_cap_tiles)))
-        return rc;
-      e = g4::launch_bwd_tile_gemm(D, 2, tk64, tdq128, pairs ? &tds : nullptr, m, w.n_qt_total,
-                                   a->num_q_heads, st);
+      e = g4::launch_bwd_tile_gemm(D, 2, tk64, tdq, pairs ? &tds : nullptr, mb, b.rows,
+                                   b.nh * p.group, st);
       if (e) return cuda_fail(static_cast<cudaError_t>(e), "dQ launch");
+    }
+    if (mp.own_acc) {
+      const int64_t rows_b = a->seqlen_k;  // packed: one "batch" of Tk rows
+      {
+        LaunchScope ls(kKCast, st);
+        e = g4::launch_cast_f32_bf16(m.dk_acc, tok_k, Hkv, D, p.dk, a->dk_stride, a->batch,
+                                     rows_b, st);
+        if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK cast launch");
+      }
+      LaunchScope ls(kKCast, st);
+      e = g4::launch_cast_f32_bf16(m.dv_acc, tok_k, Hkv, a->head_dim_v, p.dv, a->dv_stride,
+                                   a->batch, rows_b, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV cast launch");
     }
     return G4_OK;
   }

@@ -3,7 +3,10 @@
 // predicate, and the per-Q-tile key-tile range.
 //
 // Mask (reference masks.py:8-80, h100_masks.py:27-152), with q_abs the query's
-// absolute position in its K stream (lower-right alignment, q_abs = q + Sk - Sq):
+// absolute position in its K stream (lower-right alignment, q_abs = q + Sk - Sq,
+// plus an optional non-negative causal shift for global layers that ring
+// context parallelism uses for blocks of keys that lie wholly before the
+// queries; the reference contract has shift 0):
 //   window == 0 (global layer):  k <= q_abs
 //   window  > 0 (local layer) :  k > q_abs - W
 //                                AND (k <= q_abs OR (vis[q_abs] >= 0 AND vis[k] == vis[q_abs]))
@@ -26,6 +29,7 @@ struct SeqInfo {
   int k_base;   // first K token of this sequence along the token axis
   int len_q;
   int len_k;
+  int q_off;          // q_abs - q: len_k - len_q + causal shift
   int64_t meta_base;  // index of key 0 of this sequence in the metadata arrays
 };
 
@@ -36,6 +40,7 @@ struct SeqLayout {
   const int* cu_q; // packed only
   const int* cu_k; // packed only
   int64_t meta_stride;  // fixed: per-batch stride of vis/doc; packed: unused
+  int causal_shift;     // added to every query's absolute position (global layers)
 
   __device__ __forceinline__ bool packed() const { return cu_q != nullptr; }
 
@@ -57,6 +62,7 @@ struct SeqLayout {
       si.len_k = seqlen_k;
       si.meta_base = static_cast<int64_t>(s) * meta_stride;
     }
+    si.q_off = si.len_k - si.len_q + causal_shift;
     return si;
   }
 };

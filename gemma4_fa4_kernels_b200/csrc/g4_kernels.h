@@ -83,7 +83,16 @@ struct BwdParams {
   int* err;
 };
 
-// Backward with materialised P / dS scratch tiles (attn_bwd_mat.cu).
+// Backward with materialised P / dS scratch tiles (attn_bwd_mat.cu), and the
+// two-pass d512 forward that shares its kernels.
+//
+// Work is cut into bands: a band is a set of KV heads (with all their query
+// heads) and up to two ranges of the flattened query-tile list.  One band's
+// P / dS tiles fit the scratch, so any problem size runs the same kernels, one
+// launch set per band.  A band that holds every query tile writes dV / dK as
+// bf16 like the query-major products; with several query bands the dV / dK
+// partial sums of each band are added in fp32 (TMA reduce-add) into a buffer
+// that a final kernel converts.
 struct MatParams {
   SeqLayout layout;
   MaskSpec mask;                   // window and documents only (no vision)
@@ -95,8 +104,25 @@ struct MatParams {
   const int2* k_tiles;
   const int* n_k_tiles;
   const int* seg_first_qtile;      // packed: list index of each segment's first q tile
-  int4* ranges;                    // per query tile: kt_lo, n_kt, scratch offset, sequence
-  int64_t head_cap_tiles;          // scratch tiles reserved per query head
+  int4* ranges;                    // per query tile: kt_lo, n_kt, scratch prefix, sequence
+  const int* klist;                // nullable: per query tile its key tiles (metadata masks)
+  int klist_stride;                // entries reserved per query tile in klist
+  int64_t head_cap_tiles;          // scratch tiles reserved per query head of a band
+  // this launch set's band
+  int band_g[4];                   // query tiles [band_g[0], band_g[1]) and [band_g[2], band_g[3])
+  int band_h0;                     // first KV head
+  int band_nh;                     // KV heads
+  int kv_item0;                    // key-major grids: first work item (key tile) of the band
+  // fp32 accumulation: the product adds into an fp32 tensor (TMA reduce-add;
+  // direct atomics for partial tiles of packed segments) instead of storing bf16
+  int acc_kv;                      // dV / dK
+  int acc_q;                       // dQ
+  float* dq_acc;
+  int64_t dq_acc_stride[3];
+  float* dk_acc;
+  int64_t dk_acc_stride[3];
+  float* dv_acc;
+  int64_t dv_acc_stride[3];
   uint8_t* p_tiles;
   uint8_t* ds_tiles;
   const float* lse2;
@@ -111,8 +137,8 @@ struct MatParams {
   // two-pass forward (d512): pass 1 writes P (in p_tiles, relative to the
   // running row max), the per-row rescale factor of every tile, a per-tile
   // "some row rescaled" flag, 1/rowsum and the LSE; pass 2 forms O = P V.
-  float* fwd_alpha;                // [head][tile][128]
-  int* fwd_flags;                  // [head][tile]
+  float* fwd_alpha;                // [band head][tile][128]
+  int* fwd_flags;                  // [band head][tile]
   float* fwd_inv_l;                // [head][token]
   float* lse_out;
   int64_t lse_stride[2];
@@ -187,6 +213,11 @@ int launch_prep_dw_reduce(const float* part, int n_parts, int d, float* dw, cuda
 int launch_selftest_wait(int mode, int* err, unsigned long long* out, cudaStream_t stream);
 
 int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream);
+// fp32 [token][head][d] (contiguous) -> bf16 with strides: the final dV / dK of
+// a multi-band backward (or any fp32 gradient accumulator)
+int launch_cast_f32_bf16(const float* src, int64_t rows, int heads, int d,
+                         __nv_bfloat16* dst, const int64_t* dst_stride, int batch,
+                         int64_t rows_per_batch, cudaStream_t stream);
 // pass: d512 runs pass 0 (P) then pass 1 (dS); d256 computes both in pass 0;
 // pass 2 is the forward's first pass (online softmax, d512 only).
 int launch_bwd_score(int d, int pass, const CUtensorMap& tq, const CUtensorMap& tk,

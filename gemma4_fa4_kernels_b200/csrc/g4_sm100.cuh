@@ -232,6 +232,18 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
       : "memory");
 }
 
+// 4-D tiled reduce-add shared -> global: the box is added element-wise into
+// the tensor (fp32 maps: the fp32 accumulators), performed atomically in L2.
+// Same coordinate rules as tma_store_4d; tracked as one bulk async-group.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* smem_src,
+                                                  int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3, %4, %5}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_addr(smem_src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // Order this thread's generic shared-memory accesses before later async-proxy
 // (TMA / bulk copy) accesses to the same bytes, e.g. before a buffer that was
 // read with ordinary loads is handed back to a bulk-copy producer.

@@ -79,12 +79,13 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
-# The materialised-P/dS backward is used when its scratch fits this budget
-# (the smaller of 24 GiB and a quarter of the device's memory); otherwise the
-# recompute kernels run with a small workspace.  The budget is fixed per
-# device: querying free memory on every call costs more than a whole
-# backward at the benchmark sizes.
-_SCRATCH_CAP = 24 * 1024**3
+# The materialised-P/dS backward and the two-pass forward run band by band:
+# each band's tiles fit the workspace.  The workspace is the whole problem's
+# scratch when that fits this budget (the smaller of 64 GiB and a third of the
+# device's memory), else the budget itself, which the library cuts into bands.
+# The budget is fixed per device: querying free memory on every call costs more
+# than a whole backward at the benchmark sizes.
+_SCRATCH_CAP = 64 * 1024**3
 _budget_cache: dict[int, int] = {}
 
 
@@ -92,17 +93,20 @@ def _scratch_budget(device) -> int:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     if idx not in _budget_cache:
         total = torch.cuda.get_device_properties(idx).total_memory
-        _budget_cache[idx] = min(_SCRATCH_CAP, total // 4)
+        _budget_cache[idx] = min(_SCRATCH_CAP, total // 3)
     return _budget_cache[idx]
 
 
-def _pick_workspace(full: int, small: int, force_small: bool, device) -> torch.Tensor:
-    """Workspace for the fast (scratch-backed) path when it fits the budget and
-    the allocator, else the minimum workspace of the compact path."""
-    if force_small or full > _scratch_budget(device):
+def _pick_workspace(full: int, small: int, force_small: bool, device,
+                    budget: int | None = None) -> torch.Tensor:
+    """Workspace for the fast (scratch-backed) path: the whole problem's
+    scratch, or the budget when that is smaller (the library then runs bands);
+    the minimum workspace of the compact path when forced or out of memory."""
+    if force_small:
         return _workspace(small, device)
+    size = max(min(full, _scratch_budget(device) if budget is None else int(budget)), small)
     try:
-        return _workspace(full, device)
+        return _workspace(size, device)
     except torch.cuda.OutOfMemoryError:
         return _workspace(small, device)
 
@@ -113,12 +117,15 @@ def _stream(device) -> int:
 
 def attn_fwd(q, k, v, *, window=0, vision_ids=None, document_ids=None, cu_seqlens_q=None,
              cu_seqlens_k=None, max_seqlen_q=None, max_seqlen_k=None, out=None,
-             algorithm="auto"):
+             algorithm="auto", causal_shift=0, workspace_bytes=None):
     """Forward through ``g4_attn_fwd``.  Fixed BSHD (4-D) or packed THD (3-D)
     inputs; returns ``(out, lse)`` with LSE ``(B,Hq,Sq)`` or ``(Hq,Tq)``.
 
-    ``algorithm``: "auto" lets global d512 run the two-pass forward when its
-    scratch fits the budget; "single" forces the single-kernel forward."""
+    ``algorithm``: "auto" lets global d512 run the two-pass forward (in bands
+    when its scratch exceeds the budget); "single" forces the single-kernel
+    forward.  ``causal_shift`` (global layers) moves every query ``shift``
+    positions to the right of its lower-right position; ``workspace_bytes``
+    overrides the budget (tests use it to force several bands)."""
     lib = _lib.load()
     packed = cu_seqlens_q is not None
     dev = q.device
@@ -132,9 +139,10 @@ def attn_fwd(q, k, v, *, window=0, vision_ids=None, document_ids=None, cu_seqlen
     a = _build_args(q, k, v, out, lse, window=window, vision_ids=vis, document_ids=doc,
                     cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
                     max_seqlen_q=max_seqlen_q, max_seqlen_k=max_seqlen_k)
+    a.causal_shift = int(causal_shift)
     ws = _pick_workspace(lib.g4_attn_fwd_workspace_bytes(ctypes.byref(a)),
                          lib.g4_attn_fwd_min_workspace_bytes(ctypes.byref(a)),
-                         algorithm in ("single", "recompute"), dev)
+                         algorithm in ("single", "recompute"), dev, workspace_bytes)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _raise_for(lib.g4_attn_fwd(ctypes.byref(a), _stream(dev)), "g4_attn_fwd")
     return out, lse
@@ -142,14 +150,22 @@ def attn_fwd(q, k, v, *, window=0, vision_ids=None, document_ids=None, cu_seqlen
 
 def attn_bwd(q, k, v, out, lse, dout, *, dlse=None, window=0, vision_ids=None,
              document_ids=None, cu_seqlens_q=None, cu_seqlens_k=None, max_seqlen_q=None,
-             max_seqlen_k=None, dq=None, dk=None, dv=None, algorithm="auto"):
+             max_seqlen_k=None, dq=None, dk=None, dv=None, algorithm="auto", causal_shift=0,
+             accumulate=False, workspace_bytes=None):
     """Backward through ``g4_attn_bwd``; returns ``(dq, dk, dv)``.
 
-    ``algorithm``: "auto" materialises P/dS when the scratch fits the budget,
-    "recompute" always passes the minimum workspace (recompute kernels)."""
+    ``algorithm``: "auto" materialises P/dS (in bands when the scratch exceeds
+    the budget), "recompute" always passes the minimum workspace (recompute
+    kernels).  ``accumulate``: ``dq``/``dk``/``dv`` are fp32 tensors and the
+    gradients are added to them (ring partial sums).  ``causal_shift`` and
+    ``workspace_bytes`` as in :func:`attn_fwd`."""
     lib = _lib.load()
     packed = cu_seqlens_q is not None
     dev = q.device
+    if accumulate and (dq is None or dk is None or dv is None):
+        raise ValueError("accumulate=True needs fp32 dq, dk and dv to add into")
+    if accumulate and any(t.dtype != torch.float32 for t in (dq, dk, dv)):
+        raise ValueError("accumulated gradients must be float32")
     dq = torch.empty_like(q) if dq is None else dq
     dk = torch.empty_like(k) if dk is None else dk
     dv = torch.empty_like(v) if dv is None else dv
@@ -172,9 +188,11 @@ def attn_bwd(q, k, v, out, lse, dout, *, dlse=None, window=0, vision_ids=None,
     a.dv_stride = _strides3(dv, packed)
     if algorithm not in ("auto", "materialized", "recompute"):
         raise ValueError(f"unknown backward algorithm {algorithm!r}")
+    a.causal_shift = int(causal_shift)
+    a.grad_accumulate = 1 if accumulate else 0
     ws = _pick_workspace(lib.g4_attn_bwd_workspace_bytes(ctypes.byref(a)),
                          lib.g4_attn_bwd_min_workspace_bytes(ctypes.byref(a)),
-                         algorithm == "recompute", dev)
+                         algorithm == "recompute", dev, workspace_bytes)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _raise_for(lib.g4_attn_bwd(ctypes.byref(a), _stream(dev)), "g4_attn_bwd")
     return dq, dk, dv

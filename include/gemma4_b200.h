@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define G4_ABI_VERSION 1
+#define G4_ABI_VERSION 2
 
 enum g4_status {
   G4_OK = 0,
@@ -89,6 +89,14 @@ typedef struct g4_attn_args {
   /* scratch */
   void* workspace;
   size_t workspace_bytes;
+  /* ABI 2 */
+  int32_t causal_shift;    /* global layers (window == 0) only: added to every query's
+                              position, q_abs = q + Sk - Sq + shift, shift >= 0 (the reference
+                              contract is 0).  shift >= Sq makes every key visible: ring context
+                              parallelism's blocks of keys that precede the queries. */
+  int32_t grad_accumulate; /* backward: 0 = dq/dk/dv are bf16 and overwritten; 1 = they are fp32
+                              (strides in fp32 elements, multiples of 8) and the gradients are
+                              added to their contents (partial sums over ring steps) */
 } g4_attn_args;
 
 /* ABI version of the loaded library (G4_ABI_VERSION). */

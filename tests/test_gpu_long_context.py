@@ -8,9 +8,10 @@ With Q = 0 every visible score is 0, so every visible key gets weight 1:
   delta), so dQ = dK = 0 up to rounding, and
   dV[k] = sum over the query heads of the group and over the queries q that
   see k of dO[q] / (visible keys of q).
-At these sizes the scratch-backed algorithms exceed their budget, so the
-launches also exercise the compact fallbacks (single-kernel forward,
-recompute backward)."""
+At these sizes the scratch of the materialised algorithms (two-pass forward,
+P/dS backward) exceeds any workspace, so they run in bands; the global case
+also runs once more on the compact kernels (single-kernel forward, recompute
+backward)."""
 
 import math
 
@@ -35,16 +36,22 @@ def _operands(shape_q, shape_kv, seed):
     return q, k, v, do
 
 
-def test_global_d512_maximum_length_forward_and_backward():
+@pytest.mark.parametrize("algorithm", ["bands", "compact"])
+def test_global_d512_maximum_length_forward_and_backward(algorithm):
     s, hq, hkv, d = 262144, 4, 1, 512
     q, k, v, do = _operands((1, s, hq, d), (1, s, hkv, d), seed=5)
     n0 = _lib.launch_counts()
-    out, lse = ops.attn_fwd(q, k, v, window=0)
-    dq, dk, dv = ops.attn_bwd(q, k, v, out, lse, do, window=0)
+    fwd_alg, bwd_alg = ("auto", "auto") if algorithm == "bands" else ("single", "recompute")
+    out, lse = ops.attn_fwd(q, k, v, window=0, algorithm=fwd_alg)
+    dq, dk, dv = ops.attn_bwd(q, k, v, out, lse, do, window=0, algorithm=bwd_alg)
     torch.cuda.synchronize()
     n1 = _lib.launch_counts()
-    assert n1["attn_fwd"] > n0["attn_fwd"]  # the two-pass scratch (TBs) does not fit
-    assert n1["bwd_dq"] > n0["bwd_dq"] and n1["bwd_dkv"] > n0["bwd_dkv"]  # recompute backward
+    if algorithm == "bands":  # several bands of the two-pass forward and the P/dS backward
+        assert n1["fwd_score"] - n0["fwd_score"] >= 2 and n1["attn_fwd"] == n0["attn_fwd"]
+        assert n1["bwd_score"] - n0["bwd_score"] >= 4 and n1["bwd_dq"] == n0["bwd_dq"]
+    else:
+        assert n1["attn_fwd"] > n0["attn_fwd"]
+        assert n1["bwd_dq"] > n0["bwd_dq"] and n1["bwd_dkv"] > n0["bwd_dkv"]
     assert torch.all(out == 0.25)
     cnt = torch.arange(1, s + 1, device="cuda", dtype=torch.float64)  # causal: q+1 keys
     ref_lse = torch.log(cnt)[None, None, :].expand(1, hq, s)
