@@ -39,6 +39,8 @@ EXPORTED_SYMBOLS = (
     "g4_attn_bwd_noalloc_device_error",
     "g4_read_device_error",
     "g4_selftest_wait",
+    "g4_tile_schedule_workspace_bytes",
+    "g4_tile_schedule",
     "g4_build_mask",
     "g4_prep_bwd_workspace_bytes",
     "g4_prep_fwd",
@@ -173,6 +175,11 @@ def load() -> ctypes.CDLL:
                                          ctypes.POINTER(ctypes.c_int),
                                          ctypes.POINTER(ctypes.c_double)]
         lib.g4_selftest_wait.restype = ctypes.c_int
+        lib.g4_tile_schedule_workspace_bytes.argtypes = [P]
+        lib.g4_tile_schedule_workspace_bytes.restype = ctypes.c_size_t
+        lib.g4_tile_schedule.argtypes = [P, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                         ctypes.c_void_p]
+        lib.g4_tile_schedule.restype = ctypes.c_int
         lib.g4_build_mask.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                       ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,

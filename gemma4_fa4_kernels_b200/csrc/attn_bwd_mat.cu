@@ -88,9 +88,14 @@ struct BandSlots {
 };
 
 // Key tile j of query tile g (range rg): the j-th listed tile for metadata
-// masks, else kt_lo + j.
-__device__ __forceinline__ int qtile_key(const MatParams& p, int g, const int4& rg, int j) {
+// masks, else kt_lo + j.  List entries carry kFullTile when every pair of the
+// tile is allowed (the kernels then skip the mask).
+constexpr int kFullTile = static_cast<int>(0x80000000u);
+__device__ __forceinline__ int qtile_entry(const MatParams& p, int g, const int4& rg, int j) {
   return p.klist ? p.klist[static_cast<int64_t>(g) * p.klist_stride + j] : rg.x + j;
+}
+__device__ __forceinline__ int qtile_key(const MatParams& p, int g, const int4& rg, int j) {
+  return qtile_entry(p, g, rg, j) & 0x7fffffff;
 }
 // Position of key tile kt among query tile g's key tiles, or -1 (lists are
 // sorted ascending and start at rg.x).
@@ -101,7 +106,7 @@ __device__ __forceinline__ int qtile_key_pos(const MatParams& p, int g, const in
   int lo = 0, hi = rg.y - 1;
   while (lo <= hi) {
     const int mid = (lo + hi) >> 1;
-    const int v = l[mid];
+    const int v = l[mid] & 0x7fffffff;
     if (v == kt) return mid;
     if (v < kt) lo = mid + 1;
     else hi = mid - 1;
@@ -113,6 +118,92 @@ __device__ __forceinline__ int qtile_key_pos(const MatParams& p, int g, const in
 __device__ __forceinline__ uint32_t tile_chunk_offset(int r, int c) {
   const int blk = c >> 3, ch = c & 7;
   return blk * 16384 + r * 128 + ((ch ^ (r & 7)) << 4);
+}
+
+// =====================================================================================
+// plan (metadata masks): per query tile the exact list of key tiles that hold
+// at least one allowed pair, each tagged kFullTile when all its pairs (of valid
+// rows and keys) are allowed.  One CTA per query tile, one thread per row: the
+// row's key bound is [q - W + 1, max(q, pair_last)] (the vision exception has no
+// right window cap, masks.py:55-66); every key tile under the tile's bound is
+// tested against the exact predicate with its metadata staged in shared
+// memory.  Writes ranges[g] = (first listed tile, count, -, sequence); the
+// scratch prefix follows in plan_qtile_ranges_kernel.  The reference builds
+// the same incidence on the host (sparse_schedule.py:181-374).
+// =====================================================================================
+__global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParams p) {
+  __shared__ int kvis[kTileN], kdoc[kTileN];
+  __shared__ int lo_s, hi_s;
+  pdl_enter();
+  const int g = blockIdx.x;
+  const bool packed = p.layout.packed();
+  const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
+  if (g >= n) return;
+  int seq, qt;
+  if (packed) {
+    const int2 t = p.q_tiles[g];
+    seq = t.x;
+    qt = t.y;
+  } else {
+    seq = g / p.n_qt_fixed;
+    qt = g % p.n_qt_fixed;
+  }
+  const SeqInfo si = p.layout.seq(seq);
+  const int r = threadIdx.x;
+  const int W = p.mask.window;
+  const int q_idx = qt * kTileM + r;
+  const bool valid = q_idx < si.len_q;
+  const int q_abs = q_idx + si.q_off;
+  int qvis = -1, qdoc = 0, lo = 0x7fffffff, hi = -1;
+  if (valid) {
+    if (p.mask.vis) qvis = p.mask.vis[si.meta_base + q_abs];
+    if (p.mask.doc) qdoc = p.mask.doc[si.meta_base + q_abs];
+    lo = W > 0 ? max(0, q_abs - W + 1) : 0;
+    hi = q_abs;
+    if (W > 0 && qvis >= 0)
+      hi = p.mask.pair_last ? max(hi, p.mask.pair_last[si.meta_base + q_abs]) : si.len_k - 1;
+    hi = min(hi, si.len_k - 1);
+  }
+  if (r == 0) {
+    lo_s = 0x7fffffff;
+    hi_s = -1;
+  }
+  __syncthreads();
+  if (valid && hi >= lo) {
+    atomicMin(&lo_s, lo);
+    atomicMax(&hi_s, hi);
+  }
+  __syncthreads();
+  int* out = const_cast<int*>(p.klist) + static_cast<int64_t>(g) * p.klist_stride;
+  int cnt = 0, first = 0;
+  const int kt_end = hi_s >= 0 ? hi_s / kTileN : -1;
+  for (int kt = hi_s >= 0 ? lo_s / kTileN : 0; kt <= kt_end; ++kt) {
+    const int k0 = kt * kTileN;
+    const int kk = k0 + r;
+    const bool kin = kk < si.len_k;
+    __syncthreads();  // the previous tile's metadata is no longer read
+    kvis[r] = (p.mask.vis && kin) ? p.mask.vis[si.meta_base + kk] : -1;
+    kdoc[r] = (p.mask.doc && kin) ? p.mask.doc[si.meta_base + kk] : 0;
+    __syncthreads();
+    bool any = false, all = valid;
+    if (valid) {
+      for (int j = 0; j < kTileN; ++j) {
+        const int k = k0 + j;
+        const bool ok = k < si.len_k && k >= lo && k <= hi &&
+                        mask_allows(W, q_abs, k, qvis, qdoc, kvis[j], kdoc[j]);
+        any |= ok;
+        all &= ok;
+      }
+    }
+    const int any_t = __syncthreads_or(any);
+    const int all_t = __syncthreads_and(all || !valid);
+    if (any_t) {
+      if (r == 0 && cnt < p.klist_stride) out[cnt] = kt | (all_t ? kFullTile : 0);
+      if (cnt == 0) first = kt;
+      ++cnt;
+    }
+  }
+  if (r == 0) p.ranges[g] = make_int4(first, min(cnt, p.klist_stride), 0, seq);
 }
 
 // =====================================================================================
@@ -130,7 +221,12 @@ __global__ void plan_qtile_ranges_kernel(const MatParams p) {
   for (int base = 0; base < n; base += 1024) {
     const int g = base + tid;
     int cnt = 0, kt_lo = 0, seq = 0;
-    if (g < n) {
+    if (g < n && p.klist) {  // metadata: counts from plan_qtile_lists_kernel
+      const int4 rg = p.ranges[g];
+      kt_lo = rg.x;
+      cnt = rg.y;
+      seq = rg.w;
+    } else if (g < n) {
       int qt;
       if (packed) {
         const int2 t = p.q_tiles[g];
@@ -511,6 +607,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     const bool row_ok = row_valid && lse2_r != -INFINITY;
 
     const int qdoc = (row_valid && p.mask.doc) ? p.mask.doc[si.meta_base + q_abs] : 0;
+    const int qvis = (row_valid && p.mask.vis) ? p.mask.vis[si.meta_base + q_abs] : -1;
+    const bool meta = p.mask.has_meta();
     const int qa0 = qt * kTileM + q_off;
     const int qa1 = min((qt + 1) * kTileM, si.len_q) - 1 + q_off;
     bool ok = true;
@@ -560,8 +658,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       float m_run = -INFINITY, l_half = 0.f;
       for (int j = 0; j < work; ++j) {
         const int b = j & 1;
-        const int k0 = qtile_key(p, g, rg, j) * kTileN;
-        const int cls = p.mask.doc ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
+        const int ent = qtile_entry(p, g, rg, j);
+        const int k0 = (ent & 0x7fffffff) * kTileN;
+        const int cls = p.klist ? ((ent & kFullTile) ? 1 : 2)
+                                : (meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k));
         if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
         ok = __all_sync(0xffffffffu, ok);
         constexpr int kCols = 32 * kChunksPerWarp;
@@ -585,7 +685,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         }
         const int kc = k0 + c_begin * 32;
         if (!(cls == 1 && kc + kCols <= si.len_k)) {
-          if (!p.mask.doc) {
+          if (!meta) {
             // text only: the row's visible keys are one range (window bound,
             // causal bound, end of the sequence)
             const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
@@ -599,8 +699,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
               const int k = kc + i;
               bool keep = k < si.len_k;
               if (cls != 1 && keep)
-                keep = mask_allows(p.mask.window, q_abs, k, -1, qdoc, -1,
-                                   p.mask.doc[si.meta_base + k]);
+                keep = mask_allows(p.mask.window, q_abs, k, qvis, qdoc,
+                                   p.mask.vis ? p.mask.vis[si.meta_base + k] : -1,
+                                   p.mask.doc ? p.mask.doc[si.meta_base + k] : 0);
               if (!keep) sv[i] = -INFINITY;
             }
           }
@@ -667,8 +768,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     } else
     for (int j = 0; j < work; ++j) {
       const int b = j & 1;
-      const int k0 = qtile_key(p, g, rg, j) * kTileN;
-      const int cls = p.mask.doc ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
+      const int ent = qtile_entry(p, g, rg, j);
+      const int k0 = (ent & 0x7fffffff) * kTileN;
+      const int cls = p.klist ? ((ent & kFullTile) ? 1 : 2)
+                              : (meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k));
       if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
       if (ok && Cfg::kTS && MODE == kScoreDs)
         ok = mbar_wait(&misc->p_full[j % Cfg::kPStages], (j / Cfg::kPStages) & 1, ab,
@@ -727,7 +830,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           if (cls == 1 && row_ok && kc + 32 <= si.len_k) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) pv[i] = ex2(fmaf(__uint_as_float(sr[i]), kLog2e, -lse2_r));
-          } else if (!p.mask.doc) {
+          } else if (!meta) {
             // text only: the row's visible keys are one range (window bound,
             // causal bound, end of the sequence); none for a row without keys
             const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
@@ -743,9 +846,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             for (int i = 0; i < 32; ++i) {
               const int k = kc + i;
               bool keep = row_ok && k < si.len_k;
-              if (cls != 1) {
-                const int kdoc = (p.mask.doc && k < si.len_k) ? p.mask.doc[si.meta_base + k] : 0;
-                keep = keep && mask_allows(p.mask.window, q_abs, k, -1, qdoc, -1, kdoc);
+              if (cls != 1 && keep) {
+                const int kdoc = p.mask.doc ? p.mask.doc[si.meta_base + k] : 0;
+                const int kvis = p.mask.vis ? p.mask.vis[si.meta_base + k] : -1;
+                keep = mask_allows(p.mask.window, q_abs, k, qvis, qdoc, kvis, kdoc);
               }
               const float e = ex2(fmaf(__uint_as_float(sr[i]), kLog2e, row_ok ? -lse2_r : 0.f));
               pv[i] = keep ? e : 0.f;
@@ -1511,6 +1615,14 @@ int launch_cast_f32_bf16(const float* src, int64_t rows, int heads, int d, __nv_
   cudaError_t e = launch_chained(cast_f32_bf16_kernel, dim3(static_cast<unsigned>(blocks)),
                                  dim3(256), 0, stream, src, rows, heads, d, dst, dst_stride[0],
                                  dst_stride[1], dst_stride[2], rows_per_batch);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_plan_qtile_lists(const MatParams& p, int n_qt_total, cudaStream_t stream) {
+  if (n_qt_total <= 0) return 0;
+  cudaError_t e = launch_chained(plan_qtile_lists_kernel, dim3(n_qt_total), dim3(kTileM), 0,
+                                 stream, p);
   if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }

@@ -161,8 +161,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   tc_fence_after();
 
   const uint32_t tmem = misc->tmem_base;
-  const int kt_lo = misc->k_hi >= 0 ? misc->k_lo / kTileN : 0;
-  const int n_kt = misc->k_hi >= 0 ? misc->k_hi / kTileN - kt_lo + 1 : 0;
+  // metadata masks: the planner's exact key-tile list of this query tile (each
+  // listed tile holds an allowed pair; tiles outside the list are never loaded)
+  const int* klist = nullptr;
+  int kt_lo, n_kt;
+  if (p.klist) {
+    const int g = p.tiles ? item : seq * ((p.layout.seqlen_q + kTileM - 1) / kTileM) + qt;
+    klist = p.klist + static_cast<int64_t>(g) * p.klist_stride;
+    kt_lo = 0;
+    n_kt = p.ranges[g].y;
+  } else {
+    kt_lo = misc->k_hi >= 0 ? misc->k_lo / kTileN : 0;
+    n_kt = misc->k_hi >= 0 ? misc->k_hi / kTileN - kt_lo + 1 : 0;
+  }
+  // key tile of step j, and whether the planner found every pair of it allowed
+  auto ktile = [&](int j) { return klist ? (klist[j] & 0x7fffffff) : kt_lo + j; };
+  auto kfull = [&](int j) { return klist != nullptr && (klist[j] & 0x80000000) != 0; };
   const CtaAbort ab{&misc->abort, p.err};
 
   if (warp == kFwdProducerWarp) {
@@ -216,10 +230,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           ++it;
         }
       };
-      load_k(kt_lo);
+      load_k(ktile(0));
       for (int j = 0; j < n_kt && ok; ++j) {
-        if (j + 1 < n_kt) load_k(kt_lo + j + 1);
-        load_v(kt_lo + j);
+        if (j + 1 < n_kt) load_k(ktile(j + 1));
+        load_v(ktile(j));
       }
     }
     __syncwarp();
@@ -304,9 +318,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     float l_half = 0.f;       // this half's share of the row sum
     bool ok = true;
     for (int j = 0; j < n_kt; ++j) {
-      const int k0 = (kt_lo + j) * kTileN;
+      const int k0 = ktile(j) * kTileN;
       const int kh = k0 + half * 64;  // first key of this thread's half
-      const int cls = meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k);
+      const int cls = klist ? (kfull(j) ? 1 : 2)
+                            : (meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k));
       int* kvis = reinterpret_cast<int*>(misc->xbuf[(j + 1) & 1]);
       int* kdoc = kvis + kTileN;
       if (meta) {

@@ -222,6 +222,8 @@ struct Workspace {
   // materialised-P/dS backward only
   size_t seg_first = 0;    // int[B] (packed)
   size_t ranges = 0;       // int4[n_qt_total]
+  size_t klist = 0;        // metadata masks: int[n_qt_total * klist_stride] key-tile lists
+  int klist_stride = 0;
   size_t p_tiles = 0;      // Hq * head_cap tiles of 32 KB
   size_t ds_tiles = 0;
   size_t fwd_alpha = 0;    // two-pass forward: float[Hq * head_cap * 128]
@@ -287,12 +289,14 @@ int decode_splits(const g4_attn_args* a) {
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
 // Workspace modes: 0 single-kernel forward, 1 backward with recompute kernels,
 // 2 backward with materialised P/dS tiles, 3 two-pass forward (d512, P tiles).
 // plan_workspace lays out the regions every mode shares (and, for modes 2/3,
 // the problem-wide tile plan); the band scratch of modes 2/3 follows
-// w.total (see plan_bands).  Vision metadata keeps modes 2/3 on their
-// fallbacks (1 / 0): its key ranges are data-dependent.
+// w.total (see plan_bands).  With vision / document metadata, modes 0 and 2
+// also hold the exact key-tile list of every query tile (klist).
 Workspace plan_workspace(const g4_attn_args* a, int mode) {
   Workspace w;
   const bool packed = a->cu_seqlens_q != nullptr;
@@ -311,6 +315,7 @@ Workspace plan_workspace(const g4_attn_args* a, int mode) {
     return w;
   }
   const bool vision = a->vision_ids && a->window > 0;
+  const bool lists = a->window > 0 && (a->vision_ids || a->document_ids);
   const bool two_pass_fwd = mode == 3 && !vision && a->head_dim_qk == 512;
   const int backward = (mode == 1 || mode == 2) ? mode : 0;
   size_t off = 256;
@@ -340,8 +345,9 @@ Workspace plan_workspace(const g4_attn_args* a, int mode) {
     w.lse2 = off;
     off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
   }
-  if ((backward == 2 && !vision) || two_pass_fwd) {
-    w.materialized = true;
+  const bool fwd_lists = mode == 0 && lists;  // the single-kernel forward reads the lists
+  if (backward == 2 || two_pass_fwd || fwd_lists) {
+    w.materialized = !fwd_lists;
     w.n_qt_total = packed ? w.max_q_tiles
                           : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
     if (packed) {
@@ -350,6 +356,11 @@ Workspace plan_workspace(const g4_attn_args* a, int mode) {
     }
     w.ranges = off;
     off = align256(off + sizeof(int4) * w.n_qt_total);
+    if (lists) {
+      w.klist_stride = ceil_div(packed ? a->max_seqlen_k : a->seqlen_k, g4::kTileN);
+      w.klist = off;
+      off = align256(off + sizeof(int) * size_t(w.n_qt_total) * w.klist_stride);
+    }
     if (two_pass_fwd) {
       w.fwd_inv_l = off;
       off = align256(off + sizeof(float) * a->num_q_heads * w.tokens_q);
@@ -410,12 +421,11 @@ struct MatPlan {
 // sequence: the key-major index of its first key tile.
 struct TileTable {
   std::vector<int> kt_lo, n_kt, seq;
-  std::vector<int> kfirst;  // packed: first key-tile list index of each segment
+  std::vector<int> kfirst;  // packed: first key-tile list index of each segment (+ end)
   int nk_per_seq = 0;       // fixed: key tiles per sequence
+  bool lists = false;       // counts of listed key tiles (not ranges): kt_lo + n_kt - 1 is no bound
   bool exact = false;
 };
-
-int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
 // Key-tile range of one query tile (text masks; the planner kernel's rule).
 void qtile_range(int len_q, int len_k, int qt, int window, int shift, int* kt_lo, int* n_kt) {
@@ -456,6 +466,8 @@ void table_from_lengths(const g4_attn_args* a, const std::vector<int>& len_q,
 // alone (no device access): exact for fixed layouts.
 int64_t bound_tiles(const g4_attn_args* a, int n_qt_total) {
   const bool packed = a->cu_seqlens_q != nullptr;
+  if (a->window > 0 && (a->vision_ids || a->document_ids))  // listed tiles: up to every key tile
+    return int64_t(ceil_div(packed ? a->max_seqlen_k : a->seqlen_k, g4::kTileN)) * n_qt_total;
   if (packed) {
     const int64_t kmax = ceil_div(a->max_seqlen_k, g4::kTileN);
     int64_t per = kmax;
@@ -522,8 +534,8 @@ void band_kv_items(const g4_attn_args* a, const TileTable& t, Band* b) {
       if (t.n_kt[g] <= 0) continue;
       const int s = t.seq[g];
       const int first = packed ? t.kfirst[s] + t.kt_lo[g] : t.kt_lo[g];
-      const int last = packed ? t.kfirst[s] + t.kt_lo[g] + t.n_kt[g] - 1
-                              : t.kt_lo[g] + t.n_kt[g] - 1;
+      int last = packed ? t.kfirst[s] + t.kt_lo[g] + t.n_kt[g] - 1 : t.kt_lo[g] + t.n_kt[g] - 1;
+      if (t.lists) last = packed ? t.kfirst[s + 1] - 1 : t.nk_per_seq - 1;
       lo = std::min(lo, first);
       hi = std::max(hi, last);
     }
@@ -743,6 +755,51 @@ int exact_table(const g4_attn_args* a, cudaStream_t st, TileTable* t) {
       return fail(G4_ERR_INVALID, "cu_seqlens must be non-decreasing with Sq <= Sk per segment");
   }
   table_from_lengths(a, lq, lk, t);
+  return G4_OK;
+}
+
+// Exact table from the device plan (metadata masks: listed key tiles per query
+// tile): the ranges written by the planners and, for packed layouts, the key
+// lengths are read back (one stream synchronisation, as the reference's
+// host-side schedule also builds its lists on the host); not possible while
+// the stream is being captured.
+int table_from_device(const g4_attn_args* a, const Workspace& w, cudaStream_t st, TileTable* t) {
+  t->exact = false;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return G4_OK;
+  }
+  const bool packed = a->cu_seqlens_q != nullptr;
+  int hdr[4] = {0, 0, 0, 0};
+  std::vector<int4> rg(w.n_qt_total);
+  std::vector<int> ck(packed ? a->batch + 1 : 0);
+  cudaError_t e = cudaMemcpyAsync(hdr, a->workspace, sizeof(hdr), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(rg.data(), ws_ptr<int4>(a, w.ranges), sizeof(int4) * rg.size(),
+                        cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess && packed)
+    e = cudaMemcpyAsync(ck.data(), a->cu_seqlens_k, sizeof(int) * ck.size(),
+                        cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "tile plan read-back");
+  const int n = packed ? std::min(hdr[1], w.n_qt_total) : w.n_qt_total;
+  t->kt_lo.resize(n);
+  t->n_kt.resize(n);
+  t->seq.resize(n);
+  for (int g = 0; g < n; ++g) {
+    t->kt_lo[g] = rg[g].x;
+    t->n_kt[g] = rg[g].y;
+    t->seq[g] = rg[g].w;
+  }
+  if (packed) {
+    t->kfirst.assign(a->batch + 1, 0);
+    for (int s2 = 0; s2 < a->batch; ++s2)
+      t->kfirst[s2 + 1] = t->kfirst[s2] + ceil_div(std::max(0, ck[s2 + 1] - ck[s2]), g4::kTileN);
+  }
+  t->nk_per_seq = packed ? 0 : ceil_div(a->seqlen_k, g4::kTileN);
+  t->lists = true;
+  t->exact = true;
   return G4_OK;
 }
 
@@ -978,6 +1035,27 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
     }
     return G4_OK;
   }
+  if (w.klist) {
+    // metadata masks: the exact key-tile list of every query tile first
+    g4::MatParams m;
+    memset(&m, 0, sizeof(m));
+    m.layout = p.layout;
+    m.mask = p.mask;
+    m.group = p.group;
+    m.num_q_heads = a->num_q_heads;
+    m.n_qt_fixed = packed ? 0 : (a->seqlen_q + g4::kTileM - 1) / g4::kTileM;
+    m.q_tiles = p.tiles;
+    m.n_q_tiles = p.n_tiles;
+    m.ranges = ws_ptr<int4>(a, w.ranges);
+    m.klist = ws_ptr<int>(a, w.klist);
+    m.klist_stride = w.klist_stride;
+    LaunchScope ls(kKPlan, st);
+    const int e = g4::launch_plan_qtile_lists(m, w.n_qt_total, st);
+    if (e) return cuda_fail(static_cast<cudaError_t>(e), "key-tile list planning");
+    p.ranges = m.ranges;
+    p.klist = m.klist;
+    p.klist_stride = m.klist_stride;
+  }
   const int slabs = a->head_dim_v / 256;
   LaunchScope ls(kKFwd, st);
   int e = D == 256 ? g4::launch_fwd<256>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st)
@@ -1003,24 +1081,34 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     return fail(G4_ERR_INVALID, "lse strides must be positive");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool accumulate = a->grad_accumulate != 0;
-  // Materialised P/dS, band by band, when eligible and the workspace holds one
-  // band's scratch; otherwise the recompute kernels (small workspaces, vision
-  // metadata).
+  // Materialised P/dS, band by band, when the workspace holds one band's
+  // scratch; otherwise the recompute kernels (small workspaces).  With
+  // vision / document metadata the tile counts are data-dependent: when the
+  // bound does not fit one band, the plan is made after the device planners
+  // have listed the tiles (`defer`).
+  const bool lists = a->window > 0 && (a->vision_ids || a->document_ids);
   const Workspace wm = plan_workspace(a, 2);
   MatPlan mp;
+  bool defer = false;
   if (wm.materialized && a->workspace && a->workspace_bytes >= wm.total) {
     if (!plan_bands(a, wm, true, a->workspace_bytes, nullptr, accumulate, &mp)) {
-      TileTable t;
-      if ((rc = exact_table(a, st, &t))) return rc;
-      plan_bands(a, wm, true, a->workspace_bytes, &t, accumulate, &mp);
+      if (lists) {
+        defer = true;
+      } else {
+        TileTable t;
+        if ((rc = exact_table(a, st, &t))) return rc;
+        plan_bands(a, wm, true, a->workspace_bytes, &t, accumulate, &mp);
+      }
     }
   }
-  if (accumulate && !mp.ok)
+  if (accumulate && !mp.ok && !defer)
     return fail(G4_ERR_WORKSPACE,
                 "gradient accumulation runs on the materialised backward only; the workspace "
                 "(%zu bytes) holds no band of its scratch",
                 a->workspace_bytes);
-  const Workspace w = mp.ok ? wm : plan_workspace(a, 1);
+  // the recompute kernels use the same leading regions (tile lists, vision
+  // pairs, delta, log2 LSE), so a deferred plan that fails can still fall back
+  const Workspace w = (mp.ok || defer) ? wm : plan_workspace(a, 1);
   g4::BwdParams p;
   memset(&p, 0, sizeof(p));
   if ((rc = prepare(a, w, true, st, &p.mask))) return rc;
@@ -1079,6 +1167,43 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     return rc;
   const int gq = packed ? w.max_q_tiles : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
   const int gk = packed ? w.max_k_tiles : a->batch * ((a->seqlen_k + g4::kTileN - 1) / g4::kTileN);
+  if (mp.ok || defer) {
+    g4::MatParams m;
+    memset(&m, 0, sizeof(m));
+    m.layout = p.layout;
+    m.mask = p.mask;
+    m.group = p.group;
+    m.num_q_heads = a->num_q_heads;
+    m.n_qt_fixed = packed ? 0 : (a->seqlen_q + g4::kTileM - 1) / g4::kTileM;
+    m.q_tiles = p.q_tiles;
+    m.n_q_tiles = p.n_q_tiles;
+    m.k_tiles = p.k_tiles;
+    m.n_k_tiles = p.n_k_tiles;
+    m.seg_first_qtile = packed ? ws_ptr<int>(a, w.seg_first) : nullptr;
+    m.ranges = ws_ptr<int4>(a, w.ranges);
+    m.klist = lists ? ws_ptr<int>(a, w.klist) : nullptr;
+    m.klist_stride = w.klist_stride;
+    {
+      if (lists) {
+        LaunchScope ls(kKPlan, st);
+        e = g4::launch_plan_qtile_lists(m, w.n_qt_total, st);
+        if (e) return cuda_fail(static_cast<cudaError_t>(e), "key-tile list planning");
+      }
+      LaunchScope ls(kKPlan, st);
+      e = g4::launch_plan_qtile_ranges(m, st);
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "query-tile range planning");
+    }
+    if (defer) {
+      TileTable t;
+      if ((rc = table_from_device(a, w, st, &t))) return rc;
+      if (t.exact) plan_bands(a, wm, true, a->workspace_bytes, &t, accumulate, &mp);
+      if (!mp.ok && accumulate)
+        return fail(G4_ERR_WORKSPACE,
+                    "gradient accumulation runs on the materialised backward only; the "
+                    "workspace (%zu bytes) holds no band of its scratch",
+                    a->workspace_bytes);
+    }
+  }
   if (mp.ok) {
     g4::MatParams m;
     memset(&m, 0, sizeof(m));
@@ -1093,6 +1218,8 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     m.n_k_tiles = p.n_k_tiles;
     m.seg_first_qtile = packed ? ws_ptr<int>(a, w.seg_first) : nullptr;
     m.ranges = ws_ptr<int4>(a, w.ranges);
+    m.klist = lists ? ws_ptr<int>(a, w.klist) : nullptr;
+    m.klist_stride = w.klist_stride;
     m.head_cap_tiles = mp.cap;
     m.p_tiles = ws_ptr<uint8_t>(a, mp.p_off);
     m.ds_tiles = ws_ptr<uint8_t>(a, mp.ds_off);
@@ -1165,11 +1292,6 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
     if (pairs && (rc = make_scratch_map(&tds, m.ds_tiles,
                                         2 * int64_t(mp.nh_max) * p.group * mp.cap)))
       return rc;
-    {
-      LaunchScope ls(kKPlan, st);
-      e = g4::launch_plan_qtile_ranges(m, st);
-      if (e) return cuda_fail(static_cast<cudaError_t>(e), "query-tile range planning");
-    }
     if (mp.own_acc) {
       const size_t acc = size_t(tok_k) * Hkv * D * sizeof(float);
       cudaError_t ce = cudaMemsetAsync(m.dk_acc, 0, acc, st);
@@ -1236,6 +1358,80 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
                  : g4::launch_bwd_dkv<512>(tq, tk, tv, tdo, p, gk, st);
   }
   if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK/dV launch");
+  return G4_OK;
+}
+
+// Key-tile schedule of a local layer: the lists the attention kernels iterate.
+namespace {
+Workspace schedule_workspace(const g4_attn_args* a) {
+  Workspace w = plan_workspace(a, 0);
+  if (!w.klist) {  // text masks: the kernels use ranges; list them the same way here
+    const bool packed = a->cu_seqlens_q != nullptr;
+    w.n_qt_total = packed ? w.max_q_tiles
+                          : a->batch * ((a->seqlen_q + g4::kTileM - 1) / g4::kTileM);
+    size_t off = w.total;
+    w.ranges = off;
+    off = align256(off + sizeof(int4) * w.n_qt_total);
+    w.klist_stride = ceil_div(packed ? a->max_seqlen_k : a->seqlen_k, g4::kTileN);
+    w.klist = off;
+    off = align256(off + sizeof(int) * size_t(w.n_qt_total) * w.klist_stride);
+    w.total = off;
+  }
+  return w;
+}
+}  // namespace
+
+size_t g4_tile_schedule_workspace_bytes(const g4_attn_args* args) {
+  if (!args) return 0;
+  return schedule_workspace(args).total;
+}
+
+int g4_tile_schedule(const g4_attn_args* a, int32_t* counts, int32_t* key_tiles, int32_t stride,
+                     void* stream) {
+  g_last_error.clear();
+  // geometry only: the schedule depends on lengths and metadata, not on operands
+  if (!a) return fail(G4_ERR_INVALID, "null argument block");
+  const bool pk = a->cu_seqlens_q != nullptr;
+  if ((a->cu_seqlens_k != nullptr) != pk)
+    return fail(G4_ERR_INVALID, "cu_seqlens_q and cu_seqlens_k must both be set or both be null");
+  if (a->batch <= 0 || a->seqlen_q <= 0 || a->seqlen_k <= 0)
+    return fail(G4_ERR_INVALID, "batch and sequence lengths must be positive");
+  if (!pk && a->seqlen_q > a->seqlen_k)
+    return fail(G4_ERR_UNSUPPORTED, "fixed layout requires Sq <= Sk");
+  if (pk && (a->max_seqlen_q <= 0 || a->max_seqlen_k <= 0 || a->max_seqlen_q > a->max_seqlen_k))
+    return fail(G4_ERR_UNSUPPORTED, "packed maxima must satisfy 1 <= max Sq <= max Sk");
+  if (a->window <= 0) return fail(G4_ERR_UNSUPPORTED, "tile schedules describe local layers");
+  int rc;
+  if (!counts || !key_tiles) return fail(G4_ERR_INVALID, "counts and key_tiles are required");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Workspace w = schedule_workspace(a);
+  if (stride < w.klist_stride)
+    return fail(G4_ERR_INVALID, "stride must be at least %d (key tiles of the longest sequence)",
+                w.klist_stride);
+  g4::MaskSpec mask;
+  if ((rc = prepare(a, w, false, st, &mask))) return rc;
+  const bool packed = a->cu_seqlens_q != nullptr;
+  g4::MatParams m;
+  memset(&m, 0, sizeof(m));
+  m.layout = make_layout(a);
+  m.mask = mask;
+  m.group = a->num_q_heads / a->num_kv_heads;
+  m.num_q_heads = a->num_q_heads;
+  m.n_qt_fixed = packed ? 0 : (a->seqlen_q + g4::kTileM - 1) / g4::kTileM;
+  m.q_tiles = packed ? ws_ptr<int2>(a, w.q_tiles) : nullptr;
+  m.n_q_tiles = packed ? ws_ptr<int>(a, 0) + 1 : nullptr;
+  m.ranges = ws_ptr<int4>(a, w.ranges);
+  m.klist = key_tiles;
+  m.klist_stride = stride;
+  {
+    LaunchScope ls(kKPlan, st);
+    const int e = g4::launch_plan_qtile_lists(m, w.n_qt_total, st);
+    if (e) return cuda_fail(static_cast<cudaError_t>(e), "key-tile list planning");
+  }
+  cudaError_t e = cudaMemcpy2DAsync(counts, sizeof(int32_t), &ws_ptr<int4>(a, w.ranges)->y,
+                                    sizeof(int4), sizeof(int32_t), w.n_qt_total,
+                                    cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return cuda_fail(e, "schedule count copy");
   return G4_OK;
 }
 

@@ -52,6 +52,12 @@ struct FwdParams {
   int64_t lse_stride[2];           // batch, head (floats); token stride 1
   const int2* tiles;               // packed: (segment, q tile) work list, else null
   const int* n_tiles;
+  // metadata masks: per query tile (flattened index) the exact key-tile list
+  // from plan_qtile_lists_kernel (entries tagged 0x80000000 when every pair is
+  // allowed) and its count in ranges[g].y; null for text masks
+  const int4* ranges;
+  const int* klist;
+  int klist_stride;
   int* err;                        // device error word
 };
 
@@ -213,6 +219,9 @@ int launch_prep_dw_reduce(const float* part, int n_parts, int d, float* dw, cuda
 int launch_selftest_wait(int mode, int* err, unsigned long long* out, cudaStream_t stream);
 
 int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream);
+// metadata masks: exact key-tile lists per query tile into p.klist (and the
+// counts into p.ranges); run before launch_plan_qtile_ranges
+int launch_plan_qtile_lists(const MatParams& p, int n_qt_total, cudaStream_t stream);
 // fp32 [token][head][d] (contiguous) -> bf16 with strides: the final dV / dK of
 // a multi-band backward (or any fp32 gradient accumulator)
 int launch_cast_f32_bf16(const float* src, int64_t rows, int heads, int d,

@@ -201,6 +201,24 @@ int g4_read_device_error(const void* workspace, int* code, void* stream);
 int g4_selftest_wait(int mode, int* code, int* completed, double* wait_ms);
 
 /*
+ * Block-sparse tile schedule of a local layer (window > 0): for every query
+ * tile of 128 rows (flattened over sequences / segments), the key tiles of 128
+ * keys that hold at least one allowed (query, key) pair, ascending.  This is
+ * the exact incidence the kernels iterate: tiles outside a list are never
+ * loaded.  Bit 31 of an entry is set when every pair of the tile (valid rows
+ * and keys) is allowed, which lets the kernels skip the mask there.
+ * Replaces build_gemma4_local_sparse_schedule / SparseTileRows
+ * (src/gemma4_fa4/sparse_schedule.py:181-374, host Python in the reference;
+ * built on the device here).  Outputs (device int32): counts[n_q_tiles] and
+ * key_tiles[n_q_tiles * stride], stride >= ceil(max Sk / 128).  For packed
+ * layouts n_q_tiles is sum over segments of ceil(len_q / 128); entries past
+ * it are unspecified.  Scratch: workspace of g4_tile_schedule_workspace_bytes.
+ */
+size_t g4_tile_schedule_workspace_bytes(const g4_attn_args* args);
+int g4_tile_schedule(const g4_attn_args* args, int32_t* counts, int32_t* key_tiles,
+                     int32_t stride, void* stream);
+
+/*
  * Dense Gemma-4 mask builder: writes out[b][q][k] = 1 if allowed, else 0
  * (uint8, (B,Sq,Sk) contiguous).  Query row i sits at absolute position
  * q_start + i (q_start < 0 selects lower-right alignment, kv_len - q_len).
