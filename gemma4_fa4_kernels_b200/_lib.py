@@ -37,6 +37,9 @@ EXPORTED_SYMBOLS = (
     "g4_attn_bwd",
     "g4_attn_bwd_noalloc",
     "g4_attn_bwd_noalloc_device_error",
+    "g4_merge_attention_partial",
+    "g4_cast_f32_bf16",
+    "g4_add_f32",
     "g4_read_device_error",
     "g4_selftest_wait",
     "g4_tile_schedule_workspace_bytes",
@@ -99,6 +102,24 @@ class G4AttnArgs(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t),
         ("causal_shift", ctypes.c_int32),
         ("grad_accumulate", ctypes.c_int32),
+    ]
+
+
+class G4MergeArgs(ctypes.Structure):
+    """Mirror of ``g4_merge_args``."""
+
+    _fields_ = [
+        ("o_acc", ctypes.c_void_p),
+        ("lse_acc", ctypes.c_void_p),
+        ("o_part", ctypes.c_void_p),
+        ("lse_part", ctypes.c_void_p),
+        ("o_acc_stride", ctypes.c_int64 * 2),
+        ("o_part_stride", ctypes.c_int64 * 2),
+        ("lse_acc_stride", ctypes.c_int64 * 2),
+        ("lse_part_stride", ctypes.c_int64 * 2),
+        ("tokens", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
     ]
 
 
@@ -165,6 +186,15 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = [P, ctypes.c_void_p]
             fn.restype = ctypes.c_int
+        lib.g4_merge_attention_partial.argtypes = [ctypes.POINTER(G4MergeArgs), ctypes.c_void_p]
+        lib.g4_merge_attention_partial.restype = ctypes.c_int
+        lib.g4_cast_f32_bf16.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+                                         ctypes.c_int64, ctypes.c_void_p]
+        lib.g4_cast_f32_bf16.restype = ctypes.c_int
+        lib.g4_add_f32.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                   ctypes.c_void_p]
+        lib.g4_add_f32.restype = ctypes.c_int
         lib.g4_read_device_error.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int),
                                              ctypes.c_void_p]
         lib.g4_read_device_error.restype = ctypes.c_int

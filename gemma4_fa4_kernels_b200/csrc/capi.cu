@@ -59,6 +59,8 @@ enum KernelId {
   kKSelftest,
   kKGemmDvDk,
   kKCast,
+  kKMerge,
+  kKAdd,
   kKCount
 };
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
@@ -67,7 +69,7 @@ const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq
                                            "fwd_score",   "fwd_pv",      "decode",
                                            "decode_combine", "prep_fwd",  "prep_bwd",
                                            "prep_dw_reduce", "selftest_wait", "bwd_gemm_dvdk",
-                                           "cast_f32_bf16"};
+                                           "cast_f32_bf16", "ring_merge", "add_f32"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -1727,6 +1729,65 @@ int g4_selftest_wait(int mode, int* code, int* completed, double* wait_ms) {
   if (e != cudaSuccess) return cuda_fail(e, "selftest");
   *completed = static_cast<int>(host[0]);
   *wait_ms = static_cast<double>(host[1]) * 1e-6;
+  return G4_OK;
+}
+
+int g4_merge_attention_partial(const g4_merge_args* a, void* stream) {
+  g_last_error.clear();
+  if (!a || !a->o_acc || !a->lse_acc || !a->o_part || !a->lse_part)
+    return fail(G4_ERR_INVALID, "o_acc, lse_acc, o_part and lse_part are required");
+  if (a->tokens < 0 || a->heads <= 0 || a->head_dim <= 0 || a->head_dim % 8)
+    return fail(G4_ERR_INVALID, "tokens >= 0, heads > 0 and head_dim a positive multiple of 8");
+  if (!aligned16(a->o_acc) || !aligned16(a->o_part))
+    return fail(G4_ERR_INVALID, "o_acc and o_part must be 16-byte aligned");
+  for (int i = 0; i < 2; ++i)
+    if (a->o_acc_stride[i] % 4 || a->o_part_stride[i] % 8)
+      return fail(G4_ERR_INVALID, "output strides must keep every row 16-byte aligned");
+  g4::MergeParams p;
+  p.o_acc = a->o_acc;
+  p.lse_acc = a->lse_acc;
+  p.o_part = static_cast<const __nv_bfloat16*>(a->o_part);
+  p.lse_part = a->lse_part;
+  for (int i = 0; i < 2; ++i) {
+    p.o_acc_stride[i] = a->o_acc_stride[i];
+    p.o_part_stride[i] = a->o_part_stride[i];
+    p.lse_acc_stride[i] = a->lse_acc_stride[i];
+    p.lse_part_stride[i] = a->lse_part_stride[i];
+  }
+  p.tokens = a->tokens;
+  p.heads = a->heads;
+  p.head_dim = a->head_dim;
+  LaunchScope ls(kKMerge, static_cast<cudaStream_t>(stream));
+  const int e = g4::launch_merge_partial(p, static_cast<cudaStream_t>(stream));
+  if (e) return cuda_fail(static_cast<cudaError_t>(e), "merge launch");
+  return G4_OK;
+}
+
+int g4_cast_f32_bf16(const float* src, void* dst, int64_t tokens, int32_t heads, int32_t head_dim,
+                     int64_t dst_token_stride, int64_t dst_head_stride, void* stream) {
+  g_last_error.clear();
+  if (!src || !dst) return fail(G4_ERR_INVALID, "src and dst are required");
+  if (tokens < 0 || heads <= 0 || head_dim <= 0 || head_dim % 8)
+    return fail(G4_ERR_INVALID, "tokens >= 0, heads > 0 and head_dim a positive multiple of 8");
+  if (!aligned16(src) || !aligned16(dst) || dst_token_stride % 8 || dst_head_stride % 8)
+    return fail(G4_ERR_INVALID, "src/dst must be 16-byte aligned with strides multiples of 8");
+  const int64_t st[3] = {0, dst_token_stride, dst_head_stride};
+  LaunchScope ls(kKCast, static_cast<cudaStream_t>(stream));
+  const int e = g4::launch_cast_f32_bf16(src, tokens, heads, head_dim,
+                                         static_cast<__nv_bfloat16*>(dst), st, 1,
+                                         std::max<int64_t>(tokens, 1),
+                                         static_cast<cudaStream_t>(stream));
+  if (e) return cuda_fail(static_cast<cudaError_t>(e), "cast launch");
+  return G4_OK;
+}
+
+int g4_add_f32(float* dst, const float* src, int64_t n, void* stream) {
+  g_last_error.clear();
+  if (!dst || !src || n < 0 || n % 4 || !aligned16(dst) || !aligned16(src))
+    return fail(G4_ERR_INVALID, "dst/src 16-byte aligned and n a non-negative multiple of 4");
+  LaunchScope ls(kKAdd, static_cast<cudaStream_t>(stream));
+  const int e = g4::launch_add_f32(dst, src, n, static_cast<cudaStream_t>(stream));
+  if (e) return cuda_fail(static_cast<cudaError_t>(e), "add launch");
   return G4_OK;
 }
 

@@ -218,6 +218,22 @@ int launch_prep_dw_reduce(const float* part, int n_parts, int d, float* dw, cuda
 // bounded-wait self-test (one CTA): see g4_selftest_wait
 int launch_selftest_wait(int mode, int* err, unsigned long long* out, cudaStream_t stream);
 
+// Ring context parallelism (ring.cu): o_acc / lse_acc <- merge with a block's
+// partial (o_part bf16, lse_part); strides in elements, feature stride 1.
+struct MergeParams {
+  float* o_acc;
+  float* lse_acc;
+  const __nv_bfloat16* o_part;
+  const float* lse_part;
+  int64_t o_acc_stride[2];     // token, head
+  int64_t o_part_stride[2];
+  int64_t lse_acc_stride[2];   // head, token
+  int64_t lse_part_stride[2];
+  int tokens, heads, head_dim;
+};
+int launch_merge_partial(const MergeParams& p, cudaStream_t stream);
+int launch_add_f32(float* dst, const float* src, int64_t n, cudaStream_t stream);
+
 int launch_plan_qtile_ranges(const MatParams& p, cudaStream_t stream);
 // metadata masks: exact key-tile lists per query tile into p.klist (and the
 // counts into p.ranges); run before launch_plan_qtile_ranges

@@ -211,3 +211,71 @@ def build_mask(batch, q_len, kv_len, *, window, allow_vision_bidirectional, visi
                            _stream(device))
     _raise_for(rc, "g4_build_mask")
     return out
+
+
+def _rows_view(t: torch.Tensor):
+    """(tokens, heads, d) strides of a (1, S, H, D) or (T, H, D) tensor."""
+    if t.dim() == 4:
+        if t.shape[0] != 1:
+            raise ValueError("merges take one sequence (batch 1) or a packed tensor")
+        return t.shape[1], t.shape[2], t.shape[3], t.stride(1), t.stride(2)
+    return t.shape[0], t.shape[1], t.shape[2], t.stride(0), t.stride(1)
+
+
+def _lse_view(lse: torch.Tensor):
+    """(head, token) strides of a (1, H, S) or (H, T) LSE."""
+    if lse.dim() == 3:
+        return lse.stride(1), lse.stride(2)
+    return lse.stride(0), lse.stride(1)
+
+
+def merge_partial(o_acc, lse_acc, o_part, lse_part) -> None:
+    """In place: fp32 ``o_acc`` / ``lse_acc`` <- the exact softmax merge with a
+    block's bf16 output ``o_part`` and LSE ``lse_part``
+    (``g4_merge_attention_partial``)."""
+    if o_acc.dtype != torch.float32 or lse_acc.dtype != torch.float32:
+        raise ValueError("o_acc and lse_acc must be float32")
+    if o_part.dtype != torch.bfloat16 or lse_part.dtype != torch.float32:
+        raise ValueError("o_part must be bfloat16 and lse_part float32")
+    lib = _lib.load()
+    tok, heads, d, ts, hs = _rows_view(o_acc)
+    ptok, pheads, pd, pts, phs = _rows_view(o_part)
+    if (tok, heads, d) != (ptok, pheads, pd) or o_acc.stride(-1) != 1 or o_part.stride(-1) != 1:
+        raise ValueError("o_acc and o_part must have the same rows, heads and unit feature stride")
+    a = _lib.G4MergeArgs()
+    a.o_acc, a.lse_acc = o_acc.data_ptr(), lse_acc.data_ptr()
+    a.o_part, a.lse_part = o_part.data_ptr(), lse_part.data_ptr()
+    a.o_acc_stride[:] = [ts, hs]
+    a.o_part_stride[:] = [pts, phs]
+    a.lse_acc_stride[:] = list(_lse_view(lse_acc))
+    a.lse_part_stride[:] = list(_lse_view(lse_part))
+    a.tokens, a.heads, a.head_dim = tok, heads, d
+    _raise_for(lib.g4_merge_attention_partial(ctypes.byref(a), _stream(o_acc.device)),
+               "g4_merge_attention_partial")
+
+
+def cast_f32_bf16(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 copy of a contiguous fp32 ``(1, S, H, D)`` / ``(T, H, D)`` tensor
+    (``g4_cast_f32_bf16``)."""
+    if src.dtype != torch.float32 or not src.is_contiguous():
+        raise ValueError("src must be a contiguous float32 tensor")
+    out = torch.empty(src.shape, dtype=torch.bfloat16, device=src.device) if out is None else out
+    tok, heads, d, _, _ = _rows_view(src)
+    _, _, _, ts, hs = _rows_view(out)
+    lib = _lib.load()
+    _raise_for(lib.g4_cast_f32_bf16(src.data_ptr(), out.data_ptr(), tok, heads, d, ts, hs,
+                                    _stream(src.device)), "g4_cast_f32_bf16")
+    return out
+
+
+def add_f32_(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    """In place ``dst += src`` for contiguous float32 tensors of equal size
+    (``g4_add_f32``)."""
+    if dst.dtype != torch.float32 or src.dtype != torch.float32:
+        raise ValueError("dst and src must be float32")
+    if not (dst.is_contiguous() and src.is_contiguous()) or dst.numel() != src.numel():
+        raise ValueError("dst and src must be contiguous with equal sizes")
+    lib = _lib.load()
+    _raise_for(lib.g4_add_f32(dst.data_ptr(), src.data_ptr(), dst.numel(), _stream(dst.device)),
+               "g4_add_f32")
+    return dst

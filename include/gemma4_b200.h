@@ -182,6 +182,43 @@ int g4_attn_bwd_noalloc(const g4_attn_args* args, void* stream);
 int g4_attn_bwd_noalloc_device_error(int* code, void* stream);
 
 /*
+ * Ring context parallelism helpers (no reference counterpart: the reference
+ * runs long global contexts on one GPU, h100.py:713-747).  A sequence split
+ * across ranks is attended block by block of keys (g4_attn_fwd with
+ * causal_shift for blocks that lie wholly before the queries); each block
+ * gives its rows a partial output and LSE.
+ *
+ * g4_merge_attention_partial: o_acc / lse_acc (fp32 running output, natural
+ * log LSE) <- the exact softmax combination with a block's bf16 output o_part
+ * and its lse_part:  L = log(e^La + e^Lb), O = Oa e^(La-L) + Ob e^(Lb-L).
+ * Rows with La = Lb = -inf stay O = 0, L = -inf (start from o_acc = 0,
+ * lse_acc = -inf).  Output strides [token, head] in elements with unit feature
+ * stride; LSE strides [head, token] in floats.
+ *
+ * g4_cast_f32_bf16: dst (bf16, strides [token, head]) <- src (fp32, contiguous
+ * [token][head][head_dim]): the final dQ / dK / dV / O of accumulated calls.
+ */
+typedef struct g4_merge_args {
+  float* o_acc;
+  float* lse_acc;
+  const void* o_part;
+  const float* lse_part;
+  int64_t o_acc_stride[2];
+  int64_t o_part_stride[2];
+  int64_t lse_acc_stride[2];
+  int64_t lse_part_stride[2];
+  int32_t tokens;
+  int32_t heads;
+  int32_t head_dim;  /* a multiple of 8 */
+} g4_merge_args;
+int g4_merge_attention_partial(const g4_merge_args* args, void* stream);
+int g4_cast_f32_bf16(const float* src, void* dst, int64_t tokens, int32_t heads, int32_t head_dim,
+                     int64_t dst_token_stride, int64_t dst_head_stride, void* stream);
+/* dst += src over n floats (n a multiple of 4, 16-byte aligned): the key
+ * gradients of a sliding-window halo returned to the rank that owns the keys. */
+int g4_add_f32(float* dst, const float* src, int64_t n, void* stream);
+
+/*
  * Synchronise `stream` and read the device error word of a workspace used by
  * a previous call; *code receives 0 or a G4 device error (1 = TMA wait
  * expired, 2 = MMA wait expired, 3 = role hand-off wait expired).
@@ -296,7 +333,9 @@ int g4_prep_bwd(const g4_prep_args* args, void* stream);
  * forward O = P V, 12 decode, 13 decode combine, 14 preparation forward,
  * 15 preparation backward, 16 preparation dweight reduction, 17 wait self-test,
  * 18 backward dV and dK tile GEMMs in one launch (used instead of 7 and 8 when
- * the dO and Q operands take at most 80 MiB together).
+ * the dO and Q operands take at most 80 MiB together), 19 fp32 -> bf16 cast
+ * (the dV / dK of a multi-band backward), 20 ring merge of a partial output,
+ * 21 fp32 add (halo key gradients).
  *  - g4_launch_count: launches of `kernel_id` issued by this process so far.
  *  - g4_profile_enable(1): every later launch is bracketed by CUDA events on
  *    its own stream; g4_profile_read synchronises those events and returns the
