@@ -199,3 +199,35 @@ def test_prep_rotary_adjoint_is_the_transpose():
         lhs = np.sum(prep.apply_partial_rotary(x, c, s, rd) * g)
         rhs = np.sum(x * prep.rotary_adjoint(g, c, s, rd))
         assert abs(lhs - rhs) < 1e-12
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "attn_*.npz"))),
+                         ids=lambda p: os.path.basename(p))
+def test_torch_cpu_baseline_matches_reference_golden(path):
+    """The torch restatement timed as bench.py's CPU baseline reproduces the
+    reference's outputs and autograd gradients (float64, and float32 upcast
+    within float32 rounding)."""
+    import torch
+
+    from oracle.attention_torch import reference_attention_torch
+
+    z = np.load(path)
+    if "padding" in z:
+        pytest.skip("key padding is not part of the benchmarked configurations")
+    meta = _meta(z)
+    window = None if meta["window"] < 0 else meta["window"]
+    kw = dict(sliding_window=window, allow_vision_bidirectional=bool(meta["bidir"]),
+              vision_block_ids=z["vision"] if "vision" in z else None,
+              document_ids=z["docs"] if "docs" in z else None)
+    for upcast, tol in ((torch.float64, 1e-10), (torch.float32, 2e-4)):
+        q, k, v = (torch.from_numpy(z[n]).requires_grad_(True) for n in ("q", "k", "v"))
+        out, lse = reference_attention_torch(q, k, v, upcast=upcast, **kw)
+        loss = (out * torch.from_numpy(z["dout"])).sum()
+        if "dlse" in z:
+            dl = torch.from_numpy(z["dlse"])
+            loss = loss + torch.where(torch.isfinite(lse), lse.double() * dl, torch.zeros_like(dl)).sum()
+        loss.backward()
+        np.testing.assert_allclose(out.detach().numpy(), z["out"], rtol=tol, atol=tol)
+        for t, name in ((q, "dq"), (k, "dk"), (v, "dv")):
+            np.testing.assert_allclose(t.grad.numpy(), z[name], rtol=tol * 10, atol=tol * 10,
+                                       err_msg=name)
