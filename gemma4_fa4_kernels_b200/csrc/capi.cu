@@ -186,8 +186,11 @@ int check_common(const g4_attn_args* a) {
   if (a->k == a->v) return fail(G4_ERR_INVALID, "K and V must be distinct operands");
   if (a->batch <= 0 || a->seqlen_q <= 0 || a->seqlen_k <= 0)
     return fail(G4_ERR_INVALID, "batch and sequence lengths must be positive");
-  if (!packed && a->seqlen_q > a->seqlen_k)
-    return fail(G4_ERR_UNSUPPORTED, "fixed layout requires Sq <= Sk");
+  // every query keeps q_abs = q + Sk - Sq + shift >= 0: Sq may exceed Sk only by
+  // the causal shift (ring blocks whose keys all precede their queries)
+  const int64_t shift = a->window == 0 ? std::max<int64_t>(0, a->causal_shift) : 0;
+  if (!packed && int64_t(a->seqlen_q) > int64_t(a->seqlen_k) + shift)
+    return fail(G4_ERR_UNSUPPORTED, "fixed layout requires Sq <= Sk + causal_shift");
   if (a->num_kv_heads <= 0 || a->num_q_heads <= 0 || a->num_q_heads % a->num_kv_heads)
     return fail(G4_ERR_INVALID, "query heads must be a positive multiple of KV heads");
   if (a->head_dim_qk != a->head_dim_v || (a->head_dim_qk != 256 && a->head_dim_qk != 512))

@@ -93,7 +93,8 @@ typedef struct g4_attn_args {
   int32_t causal_shift;    /* global layers (window == 0) only: added to every query's
                               position, q_abs = q + Sk - Sq + shift, shift >= 0 (the reference
                               contract is 0).  shift >= Sq makes every key visible: ring context
-                              parallelism's blocks of keys that precede the queries. */
+                              parallelism's blocks of keys that precede the queries.  In the
+                              fixed layout Sq may exceed Sk by at most the shift. */
   int32_t grad_accumulate; /* backward: 0 = dq/dk/dv are bf16 and overwritten; 1 = they are fp32
                               (strides in fp32 elements, multiples of 8) and the gradients are
                               added to their contents (partial sums over ring steps) */

@@ -23,6 +23,10 @@ from oracle.masks import gemma4_attention_mask
 
 
 def _allowed(sq, sk, *, shift, window, vision_ids, document_ids):
+    # the kernels' contract (g4_attn_args): every query keeps q_abs >= 0, and the
+    # shift applies to global layers only
+    assert sk - sq + shift >= 0, "Sq may exceed Sk only by the causal shift"
+    assert shift == 0 or not window, "causal shift on a local layer"
     if not window:
         q_abs = torch.arange(sq)[:, None] + (sk - sq + shift)
         return torch.arange(sk)[None, :] <= q_abs

@@ -168,9 +168,12 @@ def test_gradient_accumulation_adds_into_fp32():
         assert rel_l2(a.cpu().numpy(), 2 * _np(r)) <= 2e-3
 
 
-@pytest.mark.parametrize("shift", [0, 64, 700], ids=["none", "partial", "all_keys"])
-def test_causal_shift(shift):
-    hq, hkv, sq, sk, d = 8, 1, 700, 900, 512
+@pytest.mark.parametrize("sq,sk,shift", [(700, 900, 0), (700, 900, 64), (700, 900, 700),
+                                         (900, 500, 900), (1200, 600, 1200)],
+                         ids=["none", "partial", "all_keys", "more_queries_than_keys",
+                              "ring_early_chunk"])
+def test_causal_shift(sq, sk, shift):
+    hq, hkv, d = 8, 1, 512
     q, k, v, do = make_inputs((1, sq, hq, d), (1, sk, hkv, d), (1, sk, hkv, d), seed=10)
     out, lse = ops.attn_fwd(q, k, v, causal_shift=shift)
     dq, dk, dv = ops.attn_bwd(q, k, v, out, lse, do, causal_shift=shift)
