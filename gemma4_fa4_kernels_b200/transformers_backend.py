@@ -1,4 +1,4 @@
-"""Transformers backend: Gemma-4 text attention through the B200 kernels.
+"""Transformers backend: Gemma-4 attention through the B200 kernels.
 
 ``register_gemma4_fa4_b200()`` registers an attention function and a mask
 function under ``BACKEND_NAME`` in Transformers' attention and mask registries
@@ -6,26 +6,32 @@ function under ``BACKEND_NAME`` in Transformers' attention and mask registries
 error), so that a Gemma-4 model loaded with ``attn_implementation="gemma4_fa4_b200"``
 runs its sliding (d256, window 1024) and full (d512, causal) attention layers
 on the CUDA kernels of this package (reference: transformers_integration.py:
-3500-3550 registration, 1702-2098 prepared routing, 118-189 mask plan).
+3500-3550 registration, 1702-2098 prepared routing, 1250-1449 packing of
+padded batches, 118-189 and 543-647 mask plan and its proof).
 
 The mask function returns a ``Gemma4MaskPlan``: the composed mask predicate
-that Transformers built (causal, sliding overlay, packed sequences, padding)
-plus its query/key geometry, unevaluated.  The attention function checks that
-predicate against the kernels' own mask before it dispatches: it evaluates the
-plan with Transformers' ``sdpa_mask`` on the query rows (all of them when the
-mask is small, otherwise the first and last rows and every row next to a
-packed-sequence boundary) and compares with ``g4_build_mask`` for the
-candidate native mask (with or without documents taken from ``position_ids``).
-The reference proves the same equality by parsing the pinned mask closures;
-evaluation needs no pinned Transformers revision.  A mismatch, padding, or a
-sliding-window cache whose keys are not the positions 0..K-1 raises
-``UnsupportedB200Path`` before any launch (``allow_sdpa_fallback=True`` routes
-such calls to PyTorch SDPA with the dense Transformers mask instead).
+that Transformers built (causal, sliding overlay, the image overlay of
+multimodal inputs, packed sequences, padding) plus its query/key geometry,
+unevaluated.  Before any launch the attention function proves that predicate
+equal to the kernels' own mask on EVERY (query, key) element: it evaluates the
+plan with Transformers' ``sdpa_mask`` in row chunks on the device and compares
+them with ``g4_build_mask`` for the candidate native mask (documents from
+``position_ids`` or none; images from a ``vision_block_ids`` keyword, as the
+reference's Transformers patch passes them, or from the plan itself: two
+consecutive tokens of one image are the only pairs a sliding query may see
+ahead of itself, so the plan's (t, t+1) entries give the image groups).  The
+reference proves the equality by parsing the pinned mask closures; evaluation
+needs no pinned Transformers revision.  A mismatch, padding that is not one
+contiguous run per row, padding together with a cache, or a sliding-window
+cache whose keys are not the positions 0..K-1 raises ``UnsupportedB200Path``
+before any launch.  There is no SDPA or eager fallback.
 
-Dispatch: equal query and key lengths use the autograd path (fixed layout, or
-packed segments for global layers with packed sequences); shorter query spans
-against a cache (decode, chunked prefill) use the lower-right fixed layout
-without autograd; a single query token takes the split-key decode kernels.
+Dispatch: equal query and key lengths use the autograd path: fixed layout, or
+packed segments for padded batches (valid tokens gathered, outputs scattered
+back, padded query rows zero) and for global layers with packed sequences;
+shorter query spans against a cache (decode, chunked prefill) use the
+lower-right fixed layout without autograd; a single query token takes the
+split-key decode kernels.
 """
 
 from __future__ import annotations
@@ -41,9 +47,8 @@ from .model_spec import GLOBAL_ATTENTION, SLIDING_ATTENTION, AttentionLayerSpec
 
 BACKEND_NAME = "gemma4_fa4_b200"
 
-# Masks up to this many elements are compared in full; larger ones on sampled rows.
-_FULL_CHECK_ELEMENTS = 1 << 24
-_EDGE_ROWS = 64
+# Mask elements compared per chunk of query rows (the whole mask is compared).
+_CHECK_CHUNK_ELEMENTS = 1 << 26
 
 
 @dataclass(frozen=True)
@@ -125,17 +130,47 @@ def _packed_documents(position_ids: torch.Tensor | None, batch: int,
     return docs.contiguous()
 
 
-def _check_rows(q_length: int, kv_length: int, batch: int,
-                documents: torch.Tensor | None) -> list[tuple[int, int]]:
-    """Contiguous query-row blocks on which the two masks are compared."""
-    if batch * q_length * kv_length <= _FULL_CHECK_ELEMENTS:
-        return [(0, q_length)]
-    rows = {(0, min(_EDGE_ROWS, q_length)), (max(0, q_length - _EDGE_ROWS), q_length)}
-    if documents is not None:
-        starts = torch.nonzero(documents[:, 1:] != documents[:, :-1])[:, 1] + 1
-        for s in torch.unique(starts).tolist()[:256]:
-            rows.add((max(0, s - 2), min(q_length, s + 2)))
-    return sorted(rows)
+def _valid_runs(pad: torch.Tensor) -> list[tuple[int, int]]:
+    """Per batch row the one contiguous run of valid (unpadded) tokens."""
+    runs = []
+    for row in pad.to(torch.bool).cpu():
+        idx = torch.nonzero(row).flatten()
+        if idx.numel() == 0:
+            raise UnsupportedB200Path("a batch row without any valid token")
+        a, b = int(idx[0]), int(idx[-1]) + 1
+        if b - a != idx.numel():
+            raise UnsupportedB200Path("padding must leave one contiguous run of tokens per row")
+        runs.append((a, b))
+    return runs
+
+
+def _vision_from_plan(plan: Gemma4MaskPlan, valid: int, device) -> torch.Tensor | None:
+    """Image groups read off the plan: a sliding query sees a later key only
+    inside its own image, so (t, t+1) allowed marks t and t+1 as one image.
+    Returns (B, valid) int32 ids (-1 for text) or None when no pair is linked."""
+    if plan.mask_function is None or plan.q_length < 2:
+        return None
+    t0 = plan.q_offset
+    n = plan.q_length - 1
+    b = torch.arange(plan.batch_size, device=device).view(-1, 1, 1, 1)
+    h = torch.zeros(1, device=device, dtype=torch.long).view(1, 1, 1, 1)
+    q = (torch.arange(n, device=device) + t0).view(1, 1, -1, 1)
+    link = plan.mask_function(b, h, q, q + 1)
+    link = torch.as_tensor(link, device=device).to(torch.bool).expand(plan.batch_size, 1, n, 1)
+    link = link[:, 0, :, 0]
+    if plan.attention_mask is not None:
+        pad = plan.attention_mask.to(torch.bool)
+        link = link & pad[:, t0:t0 + n] & pad[:, t0 + 1:t0 + n + 1]
+    if not bool(link.any()):
+        return None
+    member = torch.zeros(plan.batch_size, valid, dtype=torch.bool, device=device)
+    member[:, t0:t0 + n] |= link
+    member[:, t0 + 1:t0 + n + 1] |= link
+    start = torch.zeros_like(member)
+    start[:, t0:t0 + n] = link
+    start[:, t0 + 1:t0 + n] &= ~link[:, :-1]  # a run starts where the previous link is off
+    ids = start.to(torch.int32).cumsum(-1, dtype=torch.int32) - 1
+    return torch.where(member, ids, torch.full_like(ids, -1)).contiguous()
 
 
 def _transformers_rows(plan: Gemma4MaskPlan, row0: int, rows: int,
@@ -150,44 +185,79 @@ def _transformers_rows(plan: Gemma4MaskPlan, row0: int, rows: int,
     return mask[:, 0].to(torch.bool)
 
 
-def _native_rows(plan: Gemma4MaskPlan, spec: AttentionLayerSpec, documents, row0: int,
-                 rows: int, valid: int, device: torch.device) -> torch.Tensor:
-    """The kernels' mask for query rows [row0, row0 + rows) against key
-    positions 0..kv_length-1 (keys at or past ``valid`` are outside the cache)."""
+def _pad_to(meta: torch.Tensor | None, batch: int, length: int, fill: int, device):
+    if meta is None:
+        return None
+    out = torch.full((batch, length), fill, dtype=torch.int32, device=device)
+    out[:, :meta.shape[1]] = meta
+    return out
+
+
+def _plan_matches(plan, spec, documents, vision, pad, valid, device) -> bool:
+    """Every element of the Transformers mask equals the kernels' mask for
+    query rows holding a valid token (padded query rows are not attention
+    rows), keys beyond ``valid`` being outside the cache."""
     window = spec.sliding_window or 0
-    doc_rows = None
-    if documents is not None:
-        doc_rows = torch.full((plan.batch_size, plan.kv_length), -1, dtype=torch.int32,
-                              device=device)
-        doc_rows[:, :documents.shape[1]] = documents
-    dense = ops.build_mask(plan.batch_size, rows, plan.kv_length, window=window,
-                           allow_vision_bidirectional=False, document_ids=doc_rows,
-                           q_start=plan.q_offset + row0, device=device).to(torch.bool)
-    if valid < plan.kv_length:
-        dense[:, :, valid:] = False
-    if documents is not None:  # a query's own document is the documents row at its position
-        q_docs = documents[:, plan.q_offset + row0:plan.q_offset + row0 + rows]
-        dense &= (doc_rows.unsqueeze(1) == q_docs.unsqueeze(-1))
-    return dense
-
-
-def _plan_matches(plan, spec, documents, valid, device) -> bool:
-    for row0, row1 in _check_rows(plan.q_length, plan.kv_length, plan.batch_size, documents):
-        hf = _transformers_rows(plan, row0, row1 - row0, device)
-        mine = _native_rows(plan, spec, documents, row0, row1 - row0, valid, device)
+    doc_k = _pad_to(documents, plan.batch_size, plan.kv_length, -1, device)
+    vis_k = _pad_to(vision, plan.batch_size, plan.kv_length, -1, device)
+    key_pad = None
+    if pad is not None:
+        key_pad = torch.zeros(plan.batch_size, plan.kv_length, dtype=torch.bool, device=device)
+        key_pad[:, :valid] = pad
+    step = max(1, _CHECK_CHUNK_ELEMENTS // max(1, plan.batch_size * plan.kv_length))
+    for row0 in range(0, plan.q_length, step):
+        rows = min(step, plan.q_length - row0)
+        hf = _transformers_rows(plan, row0, rows, device)
+        mine = ops.build_mask(plan.batch_size, rows, plan.kv_length, window=window,
+                              allow_vision_bidirectional=window > 0, vision_ids=vis_k,
+                              document_ids=doc_k, key_padding_mask=key_pad,
+                              q_start=plan.q_offset + row0, device=device).to(torch.bool)
+        if valid < plan.kv_length:
+            mine[:, :, valid:] = False
+        if pad is not None:  # compare valid query rows only
+            qv = pad[:, plan.q_offset + row0:plan.q_offset + row0 + rows].unsqueeze(-1)
+            hf, mine = hf & qv, mine & qv
         if not torch.equal(hf, mine):
             return False
     return True
 
 
-def _sdpa_fallback(plan: Gemma4MaskPlan, query, key, value, spec) -> Gemma4DispatchResult:
-    mask = _transformers_rows(plan, 0, plan.q_length, query.device).unsqueeze(1)
-    rep = query.shape[1] // key.shape[1]
-    k = key[:, :, :plan.kv_length].repeat_interleave(rep, dim=1)
-    v = value[:, :, :plan.kv_length].repeat_interleave(rep, dim=1)
-    out = torch.nn.functional.scaled_dot_product_attention(query, k, v, attn_mask=mask,
-                                                           scale=spec.softmax_scale)
-    return Gemma4DispatchResult(out.transpose(1, 2), None, "sdpa_fallback")
+def _segments(runs, documents, q_len):
+    """Packed segment bounds (flattened token index) of every valid run, split
+    at document boundaries when ``documents`` is given."""
+    bounds = [0]
+    total = 0
+    for row, (a, b) in enumerate(runs):
+        cuts = []
+        if documents is not None:
+            d = documents[row, a:b]
+            cuts = (torch.nonzero(d[1:] != d[:-1]).flatten() + 1).tolist()
+        bounds += [total + c for c in cuts] + [total + b - a]
+        total += b - a
+    return bounds
+
+
+def _packed_call(q, k, v, runs, *, window, documents, vision, split_documents):
+    """Gather the valid runs into the packed layout, run the varlen kernels
+    (autograd), scatter the outputs back; padded query rows get zeros."""
+    batch, s = q.shape[0], q.shape[1]
+    dev = q.device
+    idx = torch.cat([torch.arange(r * s + a, r * s + b, device=dev) for r, (a, b) in
+                     enumerate(runs)])
+    flat = lambda t: t.reshape(batch * s, *t.shape[2:]).index_select(0, idx)  # noqa: E731
+    qp, kp, vp = flat(q), flat(k), flat(v)
+    if split_documents:
+        bounds = _segments(runs, documents, s)
+    else:
+        bounds = _segments(runs, None, s)
+    cu = torch.tensor(bounds, dtype=torch.int32, device=dev)
+    lengths = [b - a for a, b in zip(bounds[:-1], bounds[1:])]
+    meta = lambda m: None if m is None else m.reshape(-1).index_select(0, idx).contiguous()  # noqa
+    docs_p = None if split_documents else meta(documents)
+    out, lse = b200._run(qp, kp, vp, window=window, vision=meta(vision), documents=docs_p,
+                         cu_q=cu, cu_k=cu, max_q=max(lengths), max_k=max(lengths))
+    full = out.new_zeros(batch * s, *out.shape[1:]).index_copy(0, idx, out)
+    return full.reshape(batch, s, *out.shape[1:]), lse
 
 
 def gemma4_fa4_b200_prepared(module: Any, query: torch.Tensor, key: torch.Tensor,
@@ -195,9 +265,11 @@ def gemma4_fa4_b200_prepared(module: Any, query: torch.Tensor, key: torch.Tensor
                              dropout: float = 0.0, scaling: float | None = 1.0,
                              sliding_window: int | None = None,
                              position_ids: torch.Tensor | None = None,
-                             output_attentions: bool = False, allow_sdpa_fallback: bool = False,
+                             output_attentions: bool = False,
+                             vision_block_ids: torch.Tensor | None = None,
                              **_kwargs) -> Gemma4DispatchResult:
-    """Route Transformers' prepared ``(B, H, S, D)`` Q/K/V to the kernels."""
+    """Route Transformers' prepared ``(B, H, S, D)`` Q/K/V to the kernels.
+    ``vision_block_ids`` (B, S) optionally names each token's image (-1 text)."""
     if query.dim() != 4 or key.dim() != 4 or value.dim() != 4:
         raise ValueError("Transformers attention passes (B, H, S, D) tensors")
     spec = _spec_for_module(module, query, key)
@@ -209,31 +281,41 @@ def gemma4_fa4_b200_prepared(module: Any, query: torch.Tensor, key: torch.Tensor
             f"expected the {BACKEND_NAME!r} mask plan; register both entries with "
             "register_gemma4_fa4_b200()")
     batch, _, q_len, _ = query.shape
+    dev = query.device
     if plan.batch_size != batch or plan.q_length != q_len or key.shape[2] < plan.kv_length:
         raise ValueError("the mask plan does not describe these tensors")
-
-    def unsupported(reason: str) -> Gemma4DispatchResult:
-        if allow_sdpa_fallback:
-            return _sdpa_fallback(plan, query, key, value, spec)
-        raise UnsupportedB200Path(reason)
-
     if plan.kv_offset != 0:
-        return unsupported("keys must be the positions 0..K-1 (no rolled sliding-window cache)")
+        raise UnsupportedB200Path("keys must be the positions 0..K-1 (no rolled sliding-window "
+                                  "cache)")
     valid = plan.q_offset + q_len  # keys a causal query row can reach
     if valid > plan.kv_length:
-        return unsupported("queries extend past the key range")
-    if plan.attention_mask is not None and not bool(
-            plan.attention_mask[:, :valid].to(torch.bool).all().item()):
-        return unsupported("padded batches are not routed to the kernels")
-    documents = _packed_documents(position_ids, batch, q_len) if q_len == valid else None
-    candidates = [documents, None] if documents is not None else [None]
+        raise UnsupportedB200Path("queries extend past the key range")
+    pad = None
+    if plan.attention_mask is not None:
+        pad = plan.attention_mask[:, :valid].to(torch.bool)
+        if bool(pad.all().item()):
+            pad = None
+    runs = None
+    if pad is not None:
+        if q_len != valid:
+            raise UnsupportedB200Path("padded batches are routed for prefill only (no cache)")
+        runs = _valid_runs(pad)
+    prefill = q_len == valid
+    documents = _packed_documents(position_ids, batch, q_len) if prefill else None
+    sliding = spec.kind == "sliding_attention"
+    vision = None
+    if sliding:
+        if vision_block_ids is not None:
+            vision = vision_block_ids.to(device=dev, dtype=torch.int32)[:, :valid].contiguous()
+        else:
+            vision = _vision_from_plan(plan, valid, dev)
     chosen = "none"
-    for docs in candidates:
-        if _plan_matches(plan, spec, docs, valid, query.device):
+    for docs in ([documents, None] if documents is not None else [None]):
+        if _plan_matches(plan, spec, docs, vision, pad, valid, dev):
             chosen = docs
             break
     if isinstance(chosen, str):
-        return unsupported("the Transformers mask differs from the Gemma-4 kernel mask")
+        raise UnsupportedB200Path("the Transformers mask differs from the Gemma-4 kernel mask")
     documents = chosen
 
     q = query.transpose(1, 2)
@@ -241,33 +323,29 @@ def gemma4_fa4_b200_prepared(module: Any, query: torch.Tensor, key: torch.Tensor
     v = value[:, :, :valid].transpose(1, 2)
     window = spec.sliding_window or 0
     b200._validate_bshd(q, k, v, spec, label="transformers backend")
-    if q_len < valid:
+    if not prefill:
         if torch.is_grad_enabled() and any(t.requires_grad for t in (query, key, value)):
-            return unsupported("gradients through a cache (query shorter than keys) are not routed")
+            raise UnsupportedB200Path("gradients through a cache (query shorter than keys) are "
+                                      "not routed")
         with torch.no_grad():
-            out, lse = ops.attn_fwd(q, k, v, window=window)
+            out, lse = ops.attn_fwd(q, k, v, window=window, vision_ids=vision)
         return Gemma4DispatchResult(out, lse, "decode" if q_len == 1 else "prefix")
+    if runs is not None:  # padded batch: the valid runs as packed segments
+        out, lse = _packed_call(q, k, v, runs, window=window, documents=documents,
+                                vision=vision, split_documents=not sliding)
+        return Gemma4DispatchResult(out, lse, f"{spec.kind}_padded")
     if documents is None:
-        out, lse = b200._run(q, k, v, window=window)
-        return Gemma4DispatchResult(out, lse, f"{spec.kind}_fixed")
-    if spec.kind == "sliding_attention":
-        out, lse = b200._run(q, k, v, window=window, documents=documents.contiguous())
+        out, lse = b200._run(q, k, v, window=window, vision=vision)
+        suffix = "_vision" if vision is not None else "_fixed"
+        return Gemma4DispatchResult(out, lse, spec.kind + suffix)
+    if sliding:
+        out, lse = b200._run(q, k, v, window=window, vision=vision,
+                             documents=documents.contiguous())
         return Gemma4DispatchResult(out, lse, "sliding_attention_documents")
     # global layers: one packed segment per sequence of the batch rows
-    bounds = [0]
-    for row in range(batch):
-        d = documents[row]
-        cuts = (torch.nonzero(d[1:] != d[:-1]).flatten() + 1).tolist()
-        bounds += [row * q_len + c for c in cuts] + [(row + 1) * q_len]
-    cu = torch.tensor(bounds, dtype=torch.int32, device=query.device)
-    lengths = [b - a for a, b in zip(bounds[:-1], bounds[1:])]
-    qp = q.reshape(batch * q_len, *q.shape[2:])
-    kp = k.reshape(batch * q_len, *k.shape[2:])
-    vp = v.reshape(batch * q_len, *v.shape[2:])
-    out, lse = b200._run(qp, kp, vp, window=0, cu_q=cu, cu_k=cu, max_q=max(lengths),
-                         max_k=max(lengths))
-    return Gemma4DispatchResult(out.reshape(batch, q_len, *out.shape[1:]), lse,
-                                "full_attention_packed")
+    out, lse = _packed_call(q, k, v, [(0, q_len)] * batch, window=0, documents=documents,
+                            vision=None, split_documents=True)
+    return Gemma4DispatchResult(out, lse, "full_attention_packed")
 
 
 def gemma4_fa4_b200_attention_forward(module: Any, query: torch.Tensor, key: torch.Tensor,

@@ -117,3 +117,88 @@ def test_cached_decoding_matches_eager_attention():
             outs[name] = torch.cat(steps, dim=1)
     assert _paths(mine) == ["decode", "decode"]
     _no_worse(outs["mine"], outs["eager"], outs["ref"], "decode")
+
+
+def _mask_mapping(model, ids, attention_mask, position_ids, image_types=None):
+    """The masks a multimodal Gemma-4 forward builds: causal for full layers;
+    sliding for local layers, with the image overlay (same image group in
+    either direction) when ``image_types`` marks image tokens (Transformers'
+    create_causal_mask_mapping for Gemma-4)."""
+    from transformers.masking_utils import create_causal_mask, create_sliding_window_causal_mask
+    from transformers.models.gemma4.modeling_gemma4 import token_type_ids_mask_function
+
+    emb = model.embed_tokens(ids)
+    kw = dict(config=model.config, inputs_embeds=emb, attention_mask=attention_mask,
+              past_key_values=None, position_ids=position_ids)
+    sliding_kw = dict(kw)
+    if image_types is not None:
+        is_img = image_types == 1
+        prev = torch.roll(is_img, shifts=1, dims=-1)
+        prev[..., 0] = False
+        groups = torch.cumsum((is_img & ~prev).int(), dim=1) - 1
+        groups = torch.where(is_img, groups, -1)
+        sliding_kw["or_mask_function"] = token_type_ids_mask_function(image_types, groups)
+    return {"full_attention": create_causal_mask(**kw),
+            "sliding_attention": create_sliding_window_causal_mask(**sliding_kw)}
+
+
+def _padded_inputs(b=2, s=300):
+    ids = torch.randint(0, 512, (b, s), device="cuda")
+    att = torch.ones(b, s, dtype=torch.long, device="cuda")
+    att[0, :37] = 0      # left padding
+    att[1, s - 51:] = 0  # right padding
+    pos = (att.cumsum(-1) - 1).clamp_min(0)
+    return ids, att, pos
+
+
+def test_padded_batches_are_packed_into_varlen_calls():
+    eager, mine, ref = _models()
+    ids, att, pos = _padded_inputs()
+    outs = {}
+    with torch.no_grad():
+        for name, m in (("ref", ref), ("eager", eager), ("mine", mine)):
+            masks = _mask_mapping(m, ids, att, pos)
+            outs[name] = m(input_ids=ids, attention_mask=masks,
+                           position_ids=pos).last_hidden_state
+    assert _paths(mine) == ["sliding_attention_padded", "full_attention_padded"]
+    keep = att.bool()
+    _no_worse(outs["mine"][keep], outs["eager"][keep], outs["ref"][keep], "padded hidden")
+
+
+def test_multimodal_padded_batch_routes_images_to_the_kernels():
+    """Image tokens (bidirectional within an image on the sliding layers) in a
+    padded batch, forward and weight gradients, against the FP32 model."""
+    eager, mine, ref = _models()
+    ids, att, pos = _padded_inputs()
+    types = torch.zeros_like(ids)
+    types[0, 60:124] = 1     # an image of 64 tokens in row 0
+    types[0, 200:300] = 1    # and one of 100 that ends the row
+    types[1, 10:42] = 1      # an image in row 1, before its right padding
+    keep = att.bool()
+    outs = {}
+    for name, m in (("ref", ref), ("eager", eager), ("mine", mine)):
+        masks = _mask_mapping(m, ids, att, pos, types)
+        h = m(input_ids=ids, attention_mask=masks, position_ids=pos).last_hidden_state
+        h[keep].float().square().mean().backward()
+        outs[name] = h.detach()
+    assert _paths(mine) == ["sliding_attention_padded", "full_attention_padded"]
+    _no_worse(outs["mine"][keep], outs["eager"][keep], outs["ref"][keep], "multimodal hidden")
+    for layer_e, layer_m, layer_r in zip(eager.layers, mine.layers, ref.layers):
+        for pname in ("q_proj", "k_proj", "o_proj"):
+            g = [getattr(layer.self_attn, pname).weight.grad for layer in (layer_m, layer_e, layer_r)]
+            _no_worse(*g, what=f"multimodal {pname}")
+
+
+def test_multimodal_unpadded_uses_the_vision_kernels():
+    eager, mine, ref = _models()
+    ids = torch.randint(0, 512, (1, 400), device="cuda")
+    types = torch.zeros_like(ids)
+    types[0, 100:228] = 1
+    pos = torch.arange(400, device="cuda")[None]
+    outs = {}
+    with torch.no_grad():
+        for name, m in (("ref", ref), ("eager", eager), ("mine", mine)):
+            masks = _mask_mapping(m, ids, None, pos, types)
+            outs[name] = m(input_ids=ids, attention_mask=masks, position_ids=pos).last_hidden_state
+    assert _paths(mine) == ["sliding_attention_vision", "full_attention_fixed"]
+    _no_worse(outs["mine"], outs["eager"], outs["ref"], "vision hidden")

@@ -87,17 +87,61 @@ def test_head_dim_and_plan_type_rejections():
                                     sliding_window=1024)
 
 
-def test_rolled_cache_and_padding_are_refused_before_launch():
+def test_rolled_cache_and_unroutable_padding_are_refused_before_launch():
     q, k, v = _qkv()
     module = SimpleNamespace(is_sliding=True)
     with pytest.raises(UnsupportedB200Path, match="positions 0"):
         tb.gemma4_fa4_b200_prepared(module, q, k, v, tb.Gemma4MaskPlan(1, 16, 16, 0, 4, None, None),
                                     sliding_window=1024)
     pad = torch.ones(1, 16, dtype=torch.bool)
-    pad[0, 3] = False
-    with pytest.raises(UnsupportedB200Path, match="padded"):
+    pad[0, 3] = False  # a hole inside the row: not one contiguous run
+    with pytest.raises(UnsupportedB200Path, match="contiguous"):
         tb.gemma4_fa4_b200_prepared(module, q, k, v, tb.Gemma4MaskPlan(1, 16, 16, 0, 0, None, pad),
                                     sliding_window=1024)
+    qd = q[:, :, :4]
+    pad = torch.ones(1, 16, dtype=torch.bool)
+    pad[0, 0] = False  # left padding with a cache (decode)
+    with pytest.raises(UnsupportedB200Path, match="prefill only"):
+        tb.gemma4_fa4_b200_prepared(module, qd, k, v, tb.Gemma4MaskPlan(1, 4, 16, 12, 0, None, pad),
+                                    sliding_window=1024)
+
+
+def test_valid_runs_and_packed_segments():
+    pad = torch.tensor([[0, 0, 1, 1, 1, 1], [1, 1, 1, 0, 0, 0]], dtype=torch.bool)
+    runs = tb._valid_runs(pad)
+    assert runs == [(2, 6), (0, 3)]
+    assert tb._segments(runs, None, 6) == [0, 4, 7]
+    docs = torch.tensor([[5, 5, 0, 0, 1, 1], [0, 1, 1, 1, 1, 1]], dtype=torch.int32)
+    assert tb._segments(runs, docs, 6) == [0, 2, 4, 5, 7]
+    with pytest.raises(UnsupportedB200Path):
+        tb._valid_runs(torch.zeros(1, 4, dtype=torch.bool))
+
+
+def _sliding_with_images(groups, window=1024):
+    """A Transformers-style sliding mask function with the image overlay of
+    multimodal Gemma-4 inputs (same image group, either direction)."""
+    g = torch.as_tensor(groups)
+
+    def fn(b, h, q, k):
+        base = (k <= q) & (k > q - window)
+        qg, kg = g[b, q.clamp(max=g.shape[1] - 1)], g[b, k.clamp(max=g.shape[1] - 1)]
+        return base | ((qg == kg) & (qg >= 0))
+    return fn
+
+
+def test_image_groups_are_read_off_the_plan():
+    groups = [[-1, 0, 0, 0, -1, -1, 1, 1, -1, 2], [-1] * 10]
+    plan = tb.Gemma4MaskPlan(2, 10, 10, 0, 0, _sliding_with_images(groups), None)
+    vis = tb._vision_from_plan(plan, 10, torch.device("cpu"))
+    # runs of two or more linked tokens become images; a one-token image needs
+    # no future key, so it stays text
+    assert vis.tolist() == [[-1, 0, 0, 0, -1, -1, 1, 1, -1, -1], [-1] * 10]
+    text = tb.Gemma4MaskPlan(1, 10, 10, 0, 0, _sliding_with_images([[-1] * 10]), None)
+    assert tb._vision_from_plan(text, 10, torch.device("cpu")) is None
+    # a chunk of queries against a cache: links only inside the chunk
+    chunk = tb.Gemma4MaskPlan(1, 4, 10, 6, 0, _sliding_with_images([groups[0]]), None)
+    assert tb._vision_from_plan(chunk, 10, torch.device("cpu")).tolist() == \
+        [[-1, -1, -1, -1, -1, -1, 0, 0, -1, -1]]
 
 
 def test_packed_documents_from_position_ids():
@@ -108,12 +152,3 @@ def test_packed_documents_from_position_ids():
     assert tb._packed_documents(None, 1, 9) is None
     # one position row broadcast over the batch
     assert tb._packed_documents(pos, 2, 9).shape == (2, 9)
-
-
-def test_check_rows_cover_edges_and_document_boundaries():
-    assert tb._check_rows(100, 100, 1, None) == [(0, 100)]
-    big = 8192
-    docs = torch.zeros(1, big, dtype=torch.int32)
-    docs[0, 3000:] = 1
-    rows = tb._check_rows(big, big, 1, docs)
-    assert (0, 64) in rows and (big - 64, big) in rows and (2998, 3002) in rows
