@@ -464,13 +464,15 @@ def decode_measure(ops, _lib, dev, seed, iters):
         _lib.profile_enable(False)
         prof = _lib.profile_read()
         call_us = statistics.median(a.elapsed_time(b) for a, b in evs) * 1e3
-        n_dec, dec_ms = prof.get("decode", (0, 0.0))
+        kname = "decode_short" if prof.get("decode_short", (0, 0.0))[0] > 0 else "decode"
+        n_dec, dec_ms = prof.get(kname, (0, 0.0))
         kern_us = dec_ms / max(n_dec, 1) * 1e3
         nbytes = 2 * cap * hkv * d * 2 + 2 * hq * d * 2 + hq * 4
         gbs = nbytes / (kern_us * 1e-6) / 1e9
         out[c["key"]] = {"workload": c["name"], "us_per_call": round(call_us, 2),
                          "traffic": load_traffic().get(f"decode@{c['key']}"),
-                         "decode_kernel_us": round(kern_us, 2), "bytes": nbytes,
+                         "decode_kernel": kname, "decode_kernel_us": round(kern_us, 2),
+                         "bytes": nbytes,
                          "kernel_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4),
                          "call_gbs": round(nbytes / (call_us * 1e-6) / 1e9, 1),
                          "launches_per_call": {n: prof[n][0] // iters for n in prof

@@ -61,6 +61,7 @@ enum KernelId {
   kKCast,
   kKMerge,
   kKAdd,
+  kKDecodeShort,
   kKCount
 };
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
@@ -69,7 +70,8 @@ const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq
                                            "fwd_score",   "fwd_pv",      "decode",
                                            "decode_combine", "prep_fwd",  "prep_bwd",
                                            "prep_dw_reduce", "selftest_wait", "bwd_gemm_dvdk",
-                                           "cast_f32_bf16", "ring_merge", "add_f32"};
+                                           "cast_f32_bf16", "ring_merge", "add_f32",
+                                           "decode_short"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -239,6 +241,7 @@ struct Workspace {
   int decode_splits = 0;
   size_t part_o = 0;       // float[B * Hq * splits * D]
   size_t part_ml = 0;      // float2[B * Hq * splits]
+  size_t decode_counters = 0;  // int[B * Hkv] (short-window decode)
   bool materialized = false;
   int n_qt_total = 0;
   int64_t head_cap_tiles = 0;
@@ -277,13 +280,39 @@ bool decode_eligible(const g4_attn_args* a) {
          a->num_q_heads / a->num_kv_heads <= g4::kDecodeMaxGroup;
 }
 
-// Key-range splits per (sequence, KV head): enough CTAs for one per SM, never
-// more splits than 128-key tiles, and no split left without a tile at the
-// longest sequence.
+// Sliding-window decode with query groups of at most four heads runs the
+// short-window kernel (CUDA cores, one launch); everything else the
+// tensor-core split-key kernel and its merge.
+int64_t decode_keys(const g4_attn_args* a) {
+  int64_t keys = a->cu_seqlens_q ? a->max_seqlen_k : a->seqlen_k;
+  if (a->window > 0) keys = std::min<int64_t>(keys, a->window);
+  return keys;
+}
+
+bool decode_short(const g4_attn_args* a) {
+  const int G = a->num_q_heads / a->num_kv_heads;
+  return a->window > 0 && G <= g4::kDecodeShortMaxGroup &&
+         decode_keys(a) <= int64_t(g4::kDecodeShortMaxSplits) * g4::decode_short_keys(a->head_dim_qk);
+}
+
+// Key-range splits per (sequence, KV head).  Short-window kernel: two CTAs per
+// SM, at least 32 keys and at most decode_short_keys(D) keys per CTA.  Tensor-core
+// kernel: enough CTAs for one per SM, never more splits than 128-key tiles, and
+// no split left without a tile at the longest sequence.
 int decode_splits(const g4_attn_args* a) {
   const bool packed = a->cu_seqlens_q != nullptr;
   int64_t keys = packed ? a->max_seqlen_k : a->seqlen_k;
   if (a->window > 0) keys = std::min<int64_t>(keys, a->window);
+  if (decode_short(a)) {
+    const int64_t units = std::max<int64_t>(1, int64_t(a->batch) * a->num_kv_heads);
+    const int per = g4::decode_short_keys(a->head_dim_qk);
+    const int64_t lo = (keys + per - 1) / per;
+    // one wave: at most two CTAs per SM in total
+    int64_t n = std::min<int64_t>(std::max<int64_t>(1, 2 * sm_count() / units),
+                                  std::max<int64_t>(1, keys / 32));
+    n = std::max<int64_t>(std::max<int64_t>(n, lo), 1);
+    return static_cast<int>(std::min<int64_t>(n, g4::kDecodeShortMaxSplits));
+  }
   const int64_t max_tiles = std::max<int64_t>(1, (keys + g4::kTileN - 1) / g4::kTileN);
   const int64_t units = std::max<int64_t>(1, int64_t(a->batch) * a->num_kv_heads);
   int64_t n = (sm_count() + units - 1) / units;
@@ -309,6 +338,10 @@ Workspace plan_workspace(const g4_attn_args* a, int mode) {
     size_t off = 256;
     w.decode = true;
     w.decode_splits = decode_splits(a);
+    if (decode_short(a)) {  // arrival counters of the fused merge, zeroed per call
+      w.decode_counters = off;
+      off = align256(off + sizeof(int) * size_t(a->batch) * size_t(a->num_kv_heads));
+    }
     if (w.decode_splits > 1) {
       const size_t rows = size_t(a->batch) * size_t(a->num_q_heads) * size_t(w.decode_splits);
       w.part_o = off;
@@ -841,7 +874,12 @@ int run_decode(const g4_attn_args* a, cudaStream_t st) {
   const Workspace w = plan_workspace(a, 0);
   if (!a->workspace || a->workspace_bytes < w.total)
     return fail(G4_ERR_WORKSPACE, "workspace of %zu bytes required", w.total);
-  cudaError_t ce = cudaMemsetAsync(a->workspace, 0, 256, st);
+  const bool short_kernel = decode_short(a);
+  // header, and the short kernel's arrival counters right behind it
+  const size_t reset = short_kernel ? align256(w.decode_counters + sizeof(int) * size_t(a->batch) *
+                                                                   size_t(a->num_kv_heads))
+                                    : 256;
+  cudaError_t ce = cudaMemsetAsync(a->workspace, 0, reset, st);
   if (ce != cudaSuccess) return cuda_fail(ce, "workspace reset");
   const bool packed = a->cu_seqlens_q != nullptr;
   g4::DecodeParams p;
@@ -865,6 +903,19 @@ int run_decode(const g4_attn_args* a, cudaStream_t st) {
   p.part_ml = w.part_ml ? ws_ptr<float2>(a, w.part_ml) : nullptr;
   p.err = ws_ptr<int>(a, 0);
   const int D = a->head_dim_qk;
+  if (short_kernel) {
+    p.k = static_cast<const __nv_bfloat16*>(a->k);
+    p.v = static_cast<const __nv_bfloat16*>(a->v);
+    for (int i = 0; i < 3; ++i) {
+      p.k_stride[i] = packed && i == 0 ? 0 : a->k_stride[i];
+      p.v_stride[i] = packed && i == 0 ? 0 : a->v_stride[i];
+    }
+    p.counters = ws_ptr<int>(a, w.decode_counters);
+    LaunchScope ls(kKDecodeShort, st);
+    const int e = g4::launch_decode_short(D, p, a->num_kv_heads, st);
+    if (e) return cuda_fail(static_cast<cudaError_t>(e), "short-window decode launch");
+    return G4_OK;
+  }
   const int64_t bk = packed ? 1 : a->batch;
   CUtensorMap tk, tv;
   int rc;

@@ -172,8 +172,25 @@ struct DecodeParams {
   float* part_o;                   // [seq][Hq][n_split][D] unnormalised O (n_split > 1)
   float2* part_ml;                 // [seq][Hq][n_split] (running max log2, row sum)
   int* err;
+  // short-window kernel (attn_decode_short.cu): raw K/V and the per-(sequence,
+  // KV head) arrival counters of its fused merge (zero at launch)
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int* counters;
 };
 constexpr int kDecodeMaxGroup = 16;
+// Short-window decode: CUDA-core dot products, one launch (the last CTA of a
+// (sequence, KV head) merges the splits); query groups of at most 4 heads and
+// at most decode_short_keys(D) keys per CTA.
+constexpr int kDecodeShortMaxGroup = 4;
+// the merge holds every split's weight of the group's heads in shared memory
+constexpr int kDecodeShortMaxSplits = 1024;
+// keys per CTA: 32 KB of K and V rows in flight per CTA (64 keys at d256, 32
+// at d512), held in registers
+__host__ __device__ constexpr int decode_short_keys(int d) { return 16384 / d; }
+int launch_decode_short(int d, const DecodeParams& p, int num_kv_heads, cudaStream_t stream);
 constexpr int kDecodeMaxSplits = 1024;
 constexpr int kDecodeStages = 6;   // 32 KB ring stages
 int decode_smem_bytes(int d);

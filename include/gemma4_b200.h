@@ -336,7 +336,8 @@ int g4_prep_bwd(const g4_prep_args* args, void* stream);
  * 18 backward dV and dK tile GEMMs in one launch (used instead of 7 and 8 when
  * the dO and Q operands take at most 80 MiB together), 19 fp32 -> bf16 cast
  * (the dV / dK of a multi-band backward), 20 ring merge of a partial output,
- * 21 fp32 add (halo key gradients).
+ * 21 fp32 add (halo key gradients), 22 short-window decode (sliding layers,
+ * query groups of at most 4 heads: one launch, merge fused).
  *  - g4_launch_count: launches of `kernel_id` issued by this process so far.
  *  - g4_profile_enable(1): every later launch is bracketed by CUDA events on
  *    its own stream; g4_profile_read synchronises those events and returns the

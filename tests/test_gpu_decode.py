@@ -44,7 +44,12 @@ def _decode_fixed(b, sk, hq, hkv, d, window, seed, capacity=None, docs=None):
     out, lse = ops.attn_fwd(q, k, v, window=window, document_ids=doc_t)
     torch.cuda.synchronize()
     after = _lib.launch_counts()
-    assert after["decode"] == before["decode"] + 1, "decode kernel did not serve the call"
+    # sliding layers with query groups of at most 4 heads: the one-launch
+    # short-window kernel; everything else the tensor-core split-key kernel
+    kernel = "decode_short" if window > 0 and hq // hkv <= 4 else "decode"
+    assert after[kernel] == before[kernel] + 1, f"{kernel} did not serve the call"
+    if kernel == "decode_short":
+        assert after["decode_combine"] == before["decode_combine"]  # merge fused
     ref_o, ref_lse = oracle.attention_fwd(
         bshd_to_bhsd_np(q), bshd_to_bhsd_np(k), bshd_to_bhsd_np(v),
         sliding_window=window or None, allow_vision_bidirectional=window > 0,
@@ -71,6 +76,27 @@ def test_global_d512_decode_splits_and_merges():
 def test_local_d256_decode_window(sk):
     # window 1024: a longer cache keeps only the last 1024 keys
     _decode_fixed(1, sk, 32, 16, 256, 1024, seed=50 + sk, capacity=max(sk, 1024))
+
+
+@pytest.mark.parametrize("b,hq,hkv,d,sk", [(1, 32, 16, 256, 1024), (3, 8, 2, 512, 700),
+                                            (2, 4, 4, 256, 97)],
+                         ids=["c4_local_window", "d512_group4", "group1"])
+def test_short_window_decode_shapes(b, hq, hkv, d, sk):
+    """The short-window kernel over its template range (head dims, groups of
+    1-4 query heads) with several splits merged by the last arriving CTA."""
+    _decode_fixed(b, sk, hq, hkv, d, 1024, seed=80 + sk, capacity=sk + 64)
+
+
+def test_short_window_decode_repeats_on_one_workspace():
+    """The merge counters return to zero after every call: repeated calls on
+    the same inputs give identical results."""
+    q, k, v = make_inputs((1, 1, 32, 256), (1, 1024, 16, 256), (1, 1024, 16, 256), seed=88,
+                          with_dout=False)
+    o1, l1 = ops.attn_fwd(q, k, v, window=1024)
+    for _ in range(3):
+        o2, l2 = ops.attn_fwd(q, k, v, window=1024)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
 
 
 def test_local_d256_decode_documents():

@@ -81,7 +81,7 @@ def test_layer_forward_matches_the_fp32_composition(kind, s):
     n1 = _lib.launch_counts()
     # Q, K and V(local) or Q and K/V(global, one launch) through the fused preparation
     assert n1["prep_fwd"] - n0["prep_fwd"] == (3 if kind == "local" else 2)
-    assert sum(n1[k] - n0[k] for k in ("attn_fwd", "fwd_score", "decode")) >= 1
+    assert sum(n1[k] - n0[k] for k in ("attn_fwd", "fwd_score", "decode", "decode_short")) >= 1
     assert out.shape == (1, s, H) and lse.shape == (1, hq, s)
     window = L.LOCAL_WINDOW if kind == "local" else None
     lin = torch.nn.functional.linear
