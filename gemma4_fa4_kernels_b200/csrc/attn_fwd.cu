@@ -487,6 +487,507 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
 }
 
+// =====================================================================================
+// Persistent local forward (d256).  Local layers give every query tile at most
+// nine or ten key tiles, so a CTA's start (barrier set-up, TMEM allocation, the
+// resident Q load, the first S) and end (the O epilogue) are a large share of a
+// one-tile CTA's life.  Here one CTA per SM walks the (head, query tile) items in
+// the same longest-first order (round i of CTA c takes item i * G + c, or
+// i * G + G - 1 - c in odd rounds, for G CTAs), and the
+// roles run ahead across items: the producer loads the next item's Q as soon as
+// the current item's last S MMA has read Q (q_free) and streams its K/V into the
+// same ring; the MMA warp issues the next item's first S while the softmax
+// warps write the current item's O, and its first PV (which overwrites O) waits
+// until they have read it (o_free).  Barrier phases follow global counters:
+// tiles T over all items (S/P buffers, o_done) and active items I (q_full,
+// q_free, o_free).
+// =====================================================================================
+struct FwdItem {
+  bool valid;   // an item of the problem
+  int head, seq, qt, g;
+  SeqInfo si;
+  int kt_lo, n_kt;
+  const int* klist;
+};
+
+__device__ __forceinline__ FwdItem fwd_item(const FwdParams& p, int64_t L, int num_q_heads) {
+  FwdItem it;
+  it.valid = false;
+  it.n_kt = 0;
+  it.kt_lo = 0;
+  it.klist = nullptr;
+  const int nqt = (p.layout.seqlen_q + kTileM - 1) / kTileM;
+  const int64_t items = static_cast<int64_t>(num_q_heads) *
+                        (p.tiles != nullptr ? int64_t(*p.n_tiles) : int64_t(p.layout.batch) * nqt);
+  if (L >= items) return it;
+  it.head = static_cast<int>(L % num_q_heads);
+  const int item = static_cast<int>(L / num_q_heads);
+  if (p.tiles != nullptr) {
+    const int2 t = p.tiles[item];
+    it.seq = t.x;
+    it.qt = t.y;
+    it.g = item;
+  } else {
+    it.seq = item % p.layout.batch;
+    it.qt = nqt - 1 - item / p.layout.batch;  // longest causal rows first
+    it.g = it.seq * nqt + it.qt;
+  }
+  it.si = p.layout.seq(it.seq);
+  it.valid = true;
+  if (p.klist) {
+    it.klist = p.klist + static_cast<int64_t>(it.g) * p.klist_stride;
+    it.n_kt = p.ranges[it.g].y;
+  } else {
+    const int qa0 = it.qt * kTileM + it.si.q_off;
+    const int qa1 = min((it.qt + 1) * kTileM, it.si.len_q) - 1 + it.si.q_off;
+    const int lo = p.mask.window > 0 ? max(0, qa0 - p.mask.window + 1) : 0;
+    const int hi = min(qa1, it.si.len_k - 1);
+    if (hi >= lo) {
+      it.kt_lo = lo / kTileN;
+      it.n_kt = hi / kTileN - it.kt_lo + 1;
+    }
+  }
+  return it;
+}
+// Item of round i for this CTA: rounds alternate direction (CTA c takes items
+// c, 2G-1-c, 2G+c, ...), which evens out the longest-first costs per CTA.
+__device__ __forceinline__ int64_t fwd_item_index(int64_t i) {
+  const int64_t g = gridDim.x;
+  return i * g + ((i & 1) ? g - 1 - blockIdx.x : blockIdx.x);
+}
+__device__ __forceinline__ int fwd_ktile(const FwdItem& it, int j) {
+  return it.klist ? (it.klist[j] & 0x7fffffff) : it.kt_lo + j;
+}
+
+struct FwdPMisc {
+  uint64_t q_full;
+  uint64_t q_free;
+  uint64_t o_free;
+  uint64_t ring_full[8];
+  uint64_t ring_empty[8];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  float xbuf[2][2 * kTileM];  // as FwdMisc::xbuf, indexed by the global tile parity
+};
+static_assert(sizeof(FwdPMisc) <= 3072, "persistent forward misc block exceeds its budget");
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    attn_fwd_persistent_kernel(const __grid_constant__ CUtensorMap tmQ,
+                               const __grid_constant__ CUtensorMap tmK,
+                               const __grid_constant__ CUtensorMap tmV, const FwdParams p,
+                               int num_q_heads) {
+  constexpr int DQK = 256;
+  using Cfg = FwdCfg<DQK>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  pdl_enter();
+  if ((smem_addr(smem) & 1023u) != 0) {
+    if (p.err) atomicCAS(p.err, 0, 5);
+    return;
+  }
+  uint8_t* q_s = smem;
+  uint8_t* ring = smem + Cfg::kQBytes;
+  FwdPMisc* misc = reinterpret_cast<FwdPMisc*>(ring + Cfg::kStages * Cfg::kStageBytes);
+  const int tid = threadIdx.x;
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);
+
+  if (tid == 0) {
+    mbar_init(&misc->q_full, 1);
+    mbar_init(&misc->q_free, 1);
+    mbar_init(&misc->o_free, kFwdSoftThreads);
+    for (int s2 = 0; s2 < Cfg::kStages; ++s2) {
+      mbar_init(&misc->ring_full[s2], 1);
+      mbar_init(&misc->ring_empty[s2], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&misc->s_full[b], 1);
+      mbar_init(&misc->p_full[b], kFwdSoftThreads);
+    }
+    mbar_init(&misc->o_done, 1);
+    mbar_init(&misc->drain, 1);
+    misc->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kFwdProducerWarp) {
+    tmem_alloc(&misc->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc->tmem_base;
+  const CtaAbort ab{&misc->abort, p.err};
+
+  if (warp == kFwdProducerWarp) {
+    // ============================ TMA producer ============================
+    uint32_t it = 0;   // ring slots used so far
+    int I = 0;         // active items so far
+    bool ok = true;
+    if (elect_one()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+    }
+    __syncwarp();
+    auto acquire = [&](uint32_t& stage) -> bool {
+      stage = it % Cfg::kStages;
+      const uint32_t ph = (it / Cfg::kStages) & 1;
+      return mbar_wait(&misc->ring_empty[stage], ph ^ 1, ab, kDevTimeoutMma);
+    };
+    for (int64_t i = 0; ok; ++i) {
+      const FwdItem wi = fwd_item(p, fwd_item_index(i), num_q_heads);
+      if (!wi.valid) break;
+      if (wi.n_kt == 0) continue;
+      const int kv_head = wi.head / p.group;
+      // Q of this item once the previous item's S MMAs have read the last one
+      if (I > 0 && !(ok = mbar_wait(&misc->q_free, (I - 1) & 1, ab, kDevTimeoutMma))) break;
+      if (elect_one()) {
+        mbar_expect_tx(&misc->q_full, Cfg::kQBytes);
+        for (int blk = 0; blk < DQK / 64; ++blk)
+          tma_load_4d(q_s + blk * 16384, &tmQ, &misc->q_full, blk * 64, wi.head,
+                      wi.si.q_base + wi.qt * kTileM, wi.si.b_coord);
+      }
+      __syncwarp();
+      auto load_k = [&](int kt) {
+        for (int c = 0; c < Cfg::kKChunks && ok; ++c) {
+          uint32_t st;
+          if (!(ok = acquire(st))) break;
+          if (elect_one()) {
+            mbar_expect_tx(&misc->ring_full[st], Cfg::kStageBytes);
+            uint8_t* dst = ring + st * Cfg::kStageBytes;
+            for (int h = 0; h < 2; ++h)
+              tma_load_4d(dst + h * 16384, &tmK, &misc->ring_full[st], (2 * c + h) * 64, kv_head,
+                          wi.si.k_base + kt * kTileN, wi.si.b_coord);
+          }
+          __syncwarp();
+          ++it;
+        }
+      };
+      auto load_v = [&](int kt) {
+        for (int c = 0; c < Cfg::kVChunks && ok; ++c) {
+          uint32_t st;
+          if (!(ok = acquire(st))) break;
+          if (elect_one()) {
+            mbar_expect_tx(&misc->ring_full[st], Cfg::kStageBytes);
+            uint8_t* dst = ring + st * Cfg::kStageBytes;
+            for (int blk = 0; blk < 4; ++blk)
+              tma_load_4d(dst + blk * 8192, &tmV, &misc->ring_full[st], blk * 64, kv_head,
+                          wi.si.k_base + kt * kTileN + c * 64, wi.si.b_coord);
+          }
+          __syncwarp();
+          ++it;
+        }
+      };
+      load_k(fwd_ktile(wi, 0));
+      for (int j = 0; j < wi.n_kt && ok; ++j) {
+        if (j + 1 < wi.n_kt) load_k(fwd_ktile(wi, j + 1));
+        load_v(fwd_ktile(wi, j));
+      }
+      ++I;
+    }
+    __syncwarp();
+  } else if (warp == kFwdMmaWarp) {
+    // ============================ MMA issuer ============================
+    constexpr uint32_t kIdS = idesc_bf16(128, 128, false, false);
+    constexpr uint32_t kIdPV = idesc_bf16(128, 256, false, true);
+    const uint32_t q_base = smem_addr(q_s);
+    const uint32_t ring_base = smem_addr(ring);
+    uint32_t it = 0;
+    int64_t T = 0;  // tiles so far (all items)
+    int I = 0;
+    bool ok = true;
+    auto take = [&](uint32_t& stage) -> bool {
+      stage = it % Cfg::kStages;
+      const uint32_t ph = (it / Cfg::kStages) & 1;
+      if (!mbar_wait(&misc->ring_full[stage], ph, ab, kDevTimeoutTma)) return false;
+      tc_fence_after();
+      return true;
+    };
+    auto issue_s = [&](int64_t t) {
+      const uint32_t d = tmem + static_cast<uint32_t>(t & 1) * 128;
+      for (int c = 0; c < Cfg::kKChunks && ok; ++c) {
+        uint32_t st;
+        if (!(ok = take(st))) break;
+        const uint32_t kb = ring_base + st * Cfg::kStageBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int g = c * 8 + kk;
+          const uint64_t a = sdesc_sw128(q_base + (g >> 2) * 16384 + (g & 3) * 32, 16, 1024);
+          const uint64_t b = sdesc_sw128(kb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          umma_ss_w(d, a, b, kIdS, (c | kk) != 0);
+        }
+        umma_commit_w(&misc->ring_empty[st]);
+        ++it;
+      }
+      umma_commit_w(&misc->s_full[t & 1]);
+    };
+    auto issue_pv = [&](int64_t t, bool first) {
+      const uint32_t a_t = tmem + static_cast<uint32_t>(t & 1) * 128;
+      for (int c = 0; c < Cfg::kVChunks && ok; ++c) {
+        uint32_t st;
+        if (!(ok = take(st))) break;
+        const uint32_t vb = ring_base + st * Cfg::kStageBytes;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t b = sdesc_sw128(vb + kk * 2048, 8192, 1024);
+          umma_ts_w(tmem + 256, a_t + c * 32 + kk * 8, b, kIdPV, !(first && c == 0 && kk == 0));
+        }
+        umma_commit_w(&misc->ring_empty[st]);
+        ++it;
+      }
+      umma_commit_w(&misc->o_done);
+    };
+    for (int64_t i = 0; ok; ++i) {
+      const FwdItem wi = fwd_item(p, fwd_item_index(i), num_q_heads);
+      if (!wi.valid) break;
+      const int n = wi.n_kt;
+      if (n == 0) continue;
+      if (!(ok = mbar_wait(&misc->q_full, I & 1, ab, kDevTimeoutTma))) break;
+      tc_fence_after();
+      // S of tile j; once the item's last S is issued, Q may be replaced
+      auto item_s = [&](int j) {
+        issue_s(T + j);
+        if (j + 1 == n) umma_commit_w(&misc->q_free);
+      };
+      item_s(0);
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n) item_s(j + 1);
+        const int64_t t = T + j;
+        if (!(ok = mbar_wait(&misc->p_full[t & 1], (t >> 1) & 1, ab, kDevTimeoutPeer))) break;
+        if (j == 0 && I > 0 &&
+            !(ok = mbar_wait(&misc->o_free, (I - 1) & 1, ab, kDevTimeoutPeer)))
+          break;
+        tc_fence_after();
+        issue_pv(t, j == 0);
+      }
+      T += n;
+      ++I;
+    }
+    umma_commit_w(&misc->drain);
+    mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
+    __syncwarp();
+  } else {
+    // ======================= softmax + epilogue (warps 0-7) =======================
+    // Control flow stays uniform over the 256 softmax threads: every item and
+    // tile reaches named barrier 1 the same number of times whatever `ok` says.
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int half = warp >> 2;
+    const int row = tid & (kTileM - 1);
+    const bool meta = p.mask.has_meta();
+    bool ok = true;
+    int64_t T = 0;
+    int I = 0;
+    for (int64_t i = 0;; ++i) {
+      const FwdItem wi = fwd_item(p, fwd_item_index(i), num_q_heads);
+      if (!wi.valid) break;
+      const SeqInfo& si = wi.si;
+      const int q_off = si.q_off;
+      const int q_idx = wi.qt * kTileM + row;
+      const bool row_valid = q_idx < si.len_q;
+      const int q_abs = q_idx + q_off;
+      const int qvis = (row_valid && p.mask.vis) ? p.mask.vis[si.meta_base + q_abs] : -1;
+      const int qdoc = (row_valid && p.mask.doc) ? p.mask.doc[si.meta_base + q_abs] : 0;
+      const int qa0 = wi.qt * kTileM + q_off;
+      const int qa1 = min((wi.qt + 1) * kTileM, si.len_q) - 1 + q_off;
+      const int n = wi.n_kt;
+      __nv_bfloat16* orow = p.o + static_cast<int64_t>(si.b_coord) * p.o_stride[0] +
+                            static_cast<int64_t>(si.q_base + q_idx) * p.o_stride[1] +
+                            static_cast<int64_t>(wi.head) * p.o_stride[2] + half * 128;
+      float* lse_row = p.lse + static_cast<int64_t>(si.b_coord) * p.lse_stride[0] +
+                       static_cast<int64_t>(wi.head) * p.lse_stride[1] + si.q_base + q_idx;
+      if (n == 0) {  // no visible key: O = 0, LSE = -inf
+        if (row_valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow);
+          for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+          if (half == 0) *lse_row = -INFINITY;
+        }
+        continue;
+      }
+      float m_run = -INFINITY, l_half = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const int64_t t = T + j;
+        const int ent = wi.klist ? wi.klist[j] : 0;
+        const int k0 = (wi.klist ? (ent & 0x7fffffff) : wi.kt_lo + j) * kTileN;
+        const int kh = k0 + half * 64;
+        const int cls = wi.klist ? ((ent & 0x80000000) ? 1 : 2)
+                                 : (meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0,
+                                                               si.len_k));
+        int* kvis = reinterpret_cast<int*>(misc->xbuf[(t + 1) & 1]);
+        int* kdoc = kvis + kTileN;
+        if (meta) {
+          asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
+          if (tid < kTileN) {
+            const int kk = k0 + tid;
+            const bool in = kk < si.len_k;
+            kvis[tid] = (p.mask.vis && in) ? p.mask.vis[si.meta_base + kk] : -1;
+            kdoc[tid] = (p.mask.doc && in) ? p.mask.doc[si.meta_base + kk] : 0;
+          }
+          asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
+        }
+        if (ok) ok = mbar_wait(&misc->s_full[t & 1], (t >> 1) & 1, ab, kDevTimeoutMma);
+        ok = __all_sync(0xffffffffu, ok);
+        float sv[64];
+        if (ok) {
+          tc_fence_after();
+          uint32_t r0[32], r1[32];
+          const uint32_t sb = lane_base + static_cast<uint32_t>(t & 1) * 128 + half * 64;
+          tmem_ld32(sb + 0, r0);
+          tmem_ld32(sb + 32, r1);
+          tmem_wait_ld();
+          reg_fence32(r0);
+          reg_fence32(r1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            sv[i] = __uint_as_float(r0[i]);
+            sv[32 + i] = __uint_as_float(r1[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) sv[i] = -INFINITY;
+        }
+        if (cls != 1 && !meta) {
+          const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
+          const int k_hi = min(q_abs, si.len_k - 1);
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (kh + i < k_lo || kh + i > k_hi) sv[i] = -INFINITY;
+        } else if (cls != 1) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const int k = kh + i;
+            const bool keep = k < si.len_k &&
+                              mask_allows(p.mask.window, q_abs, k, qvis, qdoc,
+                                          kvis[half * 64 + i], kdoc[half * 64 + i]);
+            if (!keep) sv[i] = -INFINITY;
+          }
+        }
+        float mt = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mt = fmaxf(mt, sv[i]);
+        float* pm = misc->xbuf[t & 1];
+        pm[half * kTileM + row] = mt * kLog2e;
+        asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
+        mt = fmaxf(pm[row], pm[kTileM + row]);
+        float alpha = 1.f;
+        bool rescale = false;
+        if (mt > m_run + kLazyRescaleLog2) {
+          if (m_run != -INFINITY) {
+            alpha = ex2(m_run - mt);
+            rescale = true;
+          }
+          m_run = mt;
+        }
+        if (!ok) continue;
+        const float m_sub = (m_run == -INFINITY) ? 0.f : m_run;
+        float rowsum = 0.f;
+        {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float p0 = ex2(fmaf(sv[2 * i], kLog2e, -m_sub));
+            const float p1 = ex2(fmaf(sv[2 * i + 1], kLog2e, -m_sub));
+            rowsum += p0 + p1;
+            pk[i] = pack_bf16x2(p0, p1);
+          }
+          tmem_st32(lane_base + static_cast<uint32_t>(t & 1) * 128 + half * 32, pk);
+        }
+        l_half = l_half * alpha + rowsum;
+        tmem_wait_st();
+        if (j > 0) {
+          ok = mbar_wait(&misc->o_done, (t - 1) & 1, ab, kDevTimeoutMma);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok && __any_sync(0xffffffffu, rescale)) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 4; c += 2) {
+              const uint32_t oc = lane_base + 256 + half * 128 + c * 32;
+              uint32_t r0[32], r1[32];
+              tmem_ld32(oc, r0);
+              tmem_ld32(oc + 32, r1);
+              tmem_wait_ld();
+              reg_fence32(r0);
+              reg_fence32(r1);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                r0[i] = __float_as_uint(__uint_as_float(r0[i]) * alpha);
+                r1[i] = __float_as_uint(__uint_as_float(r1[i]) * alpha);
+              }
+              tmem_st32(oc, r0);
+              tmem_st32(oc + 32, r1);
+            }
+            tmem_wait_st();
+          }
+        }
+        tc_fence_before();
+        if (ok) mbar_arrive(&misc->p_full[t & 1]);
+      }
+      // ---- epilogue: O / l -> bf16, LSE; then O is free for the next item ----
+      float* ls = misc->xbuf[(T + n) & 1];
+      ls[half * kTileM + row] = l_half;
+      asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
+      const float l_run = ls[row] + ls[kTileM + row];
+      // every thread has read the sums before the next item's first tile reuses
+      // this buffer for its row maxima
+      asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
+      if (ok) ok = mbar_wait(&misc->o_done, (T + n - 1) & 1, ab, kDevTimeoutMma);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        if (ok) {
+          tmem_ld32(lane_base + 256 + half * 128 + c * 32, r);
+          tmem_wait_ld();
+          reg_fence32(r);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        if (row_valid) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l,
+                                __uint_as_float(r[2 * i + 1]) * inv_l);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&misc->o_free);
+      if (row_valid && half == 0)
+        *lse_row = (l_run > 0.f) ? (m_run + __log2f(l_run)) * kLn2 : -INFINITY;
+      T += n;
+      ++I;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kFwdProducerWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int launch_fwd_persistent(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                          const FwdParams& p, int ctas, int num_q_heads, cudaStream_t stream) {
+  using Cfg = FwdCfg<256>;
+  cudaError_t e = cudaFuncSetAttribute(attn_fwd_persistent_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = launch_chained(attn_fwd_persistent_kernel, dim3(ctas), dim3(kFwdThreads), Cfg::kSmemBytes,
+                     stream, tq, tk, tv, p, num_q_heads);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  return static_cast<int>(cudaGetLastError());
+}
+
 template <int DQK>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                const FwdParams& p, int grid_x, int num_q_heads, int slabs, cudaStream_t stream) {

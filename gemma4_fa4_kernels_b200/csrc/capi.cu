@@ -1114,8 +1114,17 @@ int g4_attn_fwd(const g4_attn_args* a, void* stream) {
   }
   const int slabs = a->head_dim_v / 256;
   LaunchScope ls(kKFwd, st);
-  int e = D == 256 ? g4::launch_fwd<256>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st)
-                   : g4::launch_fwd<512>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st);
+  int e;
+  if (D == 256 && slabs == 1 && (p.klist != nullptr || (!p.mask.vis && !p.mask.doc))) {
+    // d256: one persistent CTA per SM walks every (head, query tile) item;
+    // text masks need no list, metadata masks read the planner's lists
+    const int64_t items = int64_t(a->num_q_heads) * grid_x;
+    const int ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(items, sm_count())));
+    e = g4::launch_fwd_persistent(tq, tk, tv, p, ctas, a->num_q_heads, st);
+  } else {
+    e = D == 256 ? g4::launch_fwd<256>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st)
+                 : g4::launch_fwd<512>(tq, tk, tv, p, grid_x, a->num_q_heads, slabs, st);
+  }
   if (e) return cuda_fail(static_cast<cudaError_t>(e), "forward launch");
   return G4_OK;
 }

@@ -284,6 +284,10 @@ template <int DQK>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                const FwdParams& p, int grid_x, int num_q_heads, int slabs, cudaStream_t stream);
 
+// Persistent local forward (d256): `ctas` CTAs walk every (head, query tile) item.
+int launch_fwd_persistent(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                          const FwdParams& p, int ctas, int num_q_heads, cudaStream_t stream);
+
 int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int64_t tokens_q,
                           cudaStream_t stream);
 
