@@ -88,14 +88,14 @@ struct BandSlots {
 };
 
 // Key tile j of query tile g (range rg): the j-th listed tile for metadata
-// masks, else kt_lo + j.  List entries carry kFullTile when every pair of the
-// tile is allowed (the kernels then skip the mask).
-constexpr int kFullTile = static_cast<int>(0x80000000u);
+// masks, else kt_lo + j.  List entries carry kTileEntryFull when every pair of
+// the tile is allowed (the kernels then skip the mask) and kTileEntryText when
+// the range rule is exact there (the kernels skip the metadata).
 __device__ __forceinline__ int qtile_entry(const MatParams& p, int g, const int4& rg, int j) {
   return p.klist ? p.klist[static_cast<int64_t>(g) * p.klist_stride + j] : rg.x + j;
 }
 __device__ __forceinline__ int qtile_key(const MatParams& p, int g, const int4& rg, int j) {
-  return qtile_entry(p, g, rg, j) & 0x7fffffff;
+  return qtile_entry(p, g, rg, j) & kTileEntryIndex;
 }
 // Position of key tile kt among query tile g's key tiles, or -1 (lists are
 // sorted ascending and start at rg.x).
@@ -106,7 +106,7 @@ __device__ __forceinline__ int qtile_key_pos(const MatParams& p, int g, const in
   int lo = 0, hi = rg.y - 1;
   while (lo <= hi) {
     const int mid = (lo + hi) >> 1;
-    const int v = l[mid] & 0x7fffffff;
+    const int v = l[mid] & kTileEntryIndex;
     if (v == kt) return mid;
     if (v < kt) lo = mid + 1;
     else hi = mid - 1;
@@ -122,18 +122,21 @@ __device__ __forceinline__ uint32_t tile_chunk_offset(int r, int c) {
 
 // =====================================================================================
 // plan (metadata masks): per query tile the exact list of key tiles that hold
-// at least one allowed pair, each tagged kFullTile when all its pairs (of valid
-// rows and keys) are allowed.  One CTA per query tile, one thread per row: the
-// row's key bound is [q - W + 1, max(q, pair_last)] (the vision exception has no
-// right window cap, masks.py:55-66); every key tile under the tile's bound is
-// tested against the exact predicate with its metadata staged in shared
-// memory.  Writes ranges[g] = (first listed tile, count, -, sequence); the
-// scratch prefix follows in plan_qtile_ranges_kernel.  The reference builds
-// the same incidence on the host (sparse_schedule.py:181-374).
+// at least one allowed pair, each tagged kTileEntryFull when all its pairs (of
+// valid rows and keys) are allowed and kTileEntryText when the range rule is
+// exact on it.  One CTA per query tile, one thread per row: the row's key
+// bound is [q - W + 1, max(q, pair_last)] (the vision exception has no right
+// window cap, masks.py:55-66).  Each key tile under the tile's bound has its
+// metadata staged in shared memory (the next tile's is loaded meanwhile); a
+// tile without vision keys whose keys share the query tile's single document
+// is classified per row in closed form, any other tile by testing the exact
+// predicate on every pair.  Writes ranges[g] = (first listed tile, count, -,
+// sequence); the scratch prefix follows in plan_qtile_ranges_kernel.  The
+// reference builds the same incidence on the host (sparse_schedule.py:181-374).
 // =====================================================================================
 __global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParams p) {
   __shared__ int kvis[kTileN], kdoc[kTileN];
-  __shared__ int lo_s, hi_s;
+  __shared__ int lo_s, hi_s, qdoc0;
   pdl_enter();
   const int g = blockIdx.x;
   const bool packed = p.layout.packed();
@@ -152,7 +155,7 @@ __global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParam
   const int r = threadIdx.x;
   const int W = p.mask.window;
   const int q_idx = qt * kTileM + r;
-  const bool valid = q_idx < si.len_q;
+  const bool valid = q_idx < si.len_q;  // row 0 of a listed query tile always is
   const int q_abs = q_idx + si.q_off;
   int qvis = -1, qdoc = 0, lo = 0x7fffffff, hi = -1;
   if (valid) {
@@ -167,26 +170,44 @@ __global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParam
   if (r == 0) {
     lo_s = 0x7fffffff;
     hi_s = -1;
+    qdoc0 = qdoc;
   }
   __syncthreads();
   if (valid && hi >= lo) {
     atomicMin(&lo_s, lo);
     atomicMax(&hi_s, hi);
   }
-  __syncthreads();
+  const bool one_doc = __syncthreads_and(!valid || qdoc == qdoc0);
+  // the range rule of this row (window bound, causal bound, end of the keys)
+  const int lo_r = W > 0 ? max(0, q_abs - W + 1) : 0;
+  const int hi_r = min(q_abs, si.len_k - 1);
   int* out = const_cast<int*>(p.klist) + static_cast<int64_t>(g) * p.klist_stride;
   int cnt = 0, first = 0;
+  const int kt_begin = hi_s >= 0 ? lo_s / kTileN : 0;
   const int kt_end = hi_s >= 0 ? hi_s / kTileN : -1;
-  for (int kt = hi_s >= 0 ? lo_s / kTileN : 0; kt <= kt_end; ++kt) {
+  auto key_meta = [&](int kt, int& v, int& d) {
+    const int kk = kt * kTileN + r;
+    const bool kin = kt <= kt_end && kk < si.len_k;
+    v = (p.mask.vis && kin) ? p.mask.vis[si.meta_base + kk] : -1;
+    d = (p.mask.doc && kin) ? p.mask.doc[si.meta_base + kk] : 0;
+  };
+  int nv, nd;
+  key_meta(kt_begin, nv, nd);
+  for (int kt = kt_begin; kt <= kt_end; ++kt) {
     const int k0 = kt * kTileN;
-    const int kk = k0 + r;
-    const bool kin = kk < si.len_k;
+    const int cv = nv, cd = nd;
+    key_meta(kt + 1, nv, nd);  // in flight while this tile is classified
+    const bool kin = k0 + r < si.len_k;
     __syncthreads();  // the previous tile's metadata is no longer read
-    kvis[r] = (p.mask.vis && kin) ? p.mask.vis[si.meta_base + kk] : -1;
-    kdoc[r] = (p.mask.doc && kin) ? p.mask.doc[si.meta_base + kk] : 0;
-    __syncthreads();
+    kvis[r] = cv;
+    kdoc[r] = cd;
+    const bool text = one_doc && __syncthreads_and(!kin || (cv < 0 && cd == qdoc0));
     bool any = false, all = valid;
-    if (valid) {
+    if (valid && text) {
+      const int k1 = min(k0 + kTileN, si.len_k) - 1;
+      any = max(lo_r, k0) <= min(hi_r, k1);
+      all = lo_r <= k0 && hi_r >= k0 + kTileN - 1;
+    } else if (valid) {
       for (int j = 0; j < kTileN; ++j) {
         const int k = k0 + j;
         const bool ok = k < si.len_k && k >= lo && k <= hi &&
@@ -198,7 +219,8 @@ __global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParam
     const int any_t = __syncthreads_or(any);
     const int all_t = __syncthreads_and(all || !valid);
     if (any_t) {
-      if (r == 0 && cnt < p.klist_stride) out[cnt] = kt | (all_t ? kFullTile : 0);
+      if (r == 0 && cnt < p.klist_stride)
+        out[cnt] = kt | (all_t ? kTileEntryFull : 0) | (text ? kTileEntryText : 0);
       if (cnt == 0) first = kt;
       ++cnt;
     }
@@ -659,8 +681,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
       for (int j = 0; j < work; ++j) {
         const int b = j & 1;
         const int ent = qtile_entry(p, g, rg, j);
-        const int k0 = (ent & 0x7fffffff) * kTileN;
-        const int cls = p.klist ? ((ent & kFullTile) ? 1 : 2)
+        const int k0 = (ent & kTileEntryIndex) * kTileN;
+        const bool text_rule = !meta || (p.klist && (ent & kTileEntryText));
+        const int cls = p.klist ? ((ent & kTileEntryFull) ? 1 : 2)
                                 : (meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k));
         if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
         ok = __all_sync(0xffffffffu, ok);
@@ -685,7 +708,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         }
         const int kc = k0 + c_begin * 32;
         if (!(cls == 1 && kc + kCols <= si.len_k)) {
-          if (!meta) {
+          if (text_rule) {
             // text only: the row's visible keys are one range (window bound,
             // causal bound, end of the sequence)
             const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
@@ -769,8 +792,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     for (int j = 0; j < work; ++j) {
       const int b = j & 1;
       const int ent = qtile_entry(p, g, rg, j);
-      const int k0 = (ent & 0x7fffffff) * kTileN;
-      const int cls = p.klist ? ((ent & kFullTile) ? 1 : 2)
+      const int k0 = (ent & kTileEntryIndex) * kTileN;
+      const bool text_rule = !meta || (p.klist && (ent & kTileEntryText));
+      const int cls = p.klist ? ((ent & kTileEntryFull) ? 1 : 2)
                               : (meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k));
       if (ok) ok = mbar_wait(&misc->s_full[b], (j >> 1) & 1, ab, kDevTimeoutMma);
       if (ok && Cfg::kTS && MODE == kScoreDs)
@@ -830,8 +854,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           if (cls == 1 && row_ok && kc + 32 <= si.len_k) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) pv[i] = ex2(fmaf(__uint_as_float(sr[i]), kLog2e, -lse2_r));
-          } else if (!meta) {
-            // text only: the row's visible keys are one range (window bound,
+          } else if (text_rule) {
+            // text rule: the row's visible keys are one range (window bound,
             // causal bound, end of the sequence); none for a row without keys
             const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
             const int k_hi = row_ok ? min(q_abs, si.len_k - 1) : -1;

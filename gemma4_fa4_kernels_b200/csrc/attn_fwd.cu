@@ -175,8 +175,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     n_kt = misc->k_hi >= 0 ? misc->k_hi / kTileN - kt_lo + 1 : 0;
   }
   // key tile of step j, and whether the planner found every pair of it allowed
-  auto ktile = [&](int j) { return klist ? (klist[j] & 0x7fffffff) : kt_lo + j; };
-  auto kfull = [&](int j) { return klist != nullptr && (klist[j] & 0x80000000) != 0; };
+  auto ktile = [&](int j) { return klist ? (klist[j] & kTileEntryIndex) : kt_lo + j; };
+  auto kfull = [&](int j) { return klist != nullptr && (klist[j] & kTileEntryFull) != 0; };
+  auto ktext = [&](int j) { return klist != nullptr && (klist[j] & kTileEntryText) != 0; };
   const CtaAbort ab{&misc->abort, p.err};
 
   if (warp == kFwdProducerWarp) {
@@ -322,9 +323,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int kh = k0 + half * 64;  // first key of this thread's half
       const int cls = klist ? (kfull(j) ? 1 : 2)
                             : (meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0, si.len_k));
+      const bool text_rule = !meta || ktext(j);
       int* kvis = reinterpret_cast<int*>(misc->xbuf[(j + 1) & 1]);
       int* kdoc = kvis + kTileN;
-      if (meta) {
+      if (!text_rule) {
         asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
         if (tid < kTileN) {
           const int kk = k0 + tid;
@@ -355,8 +357,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
         for (int i = 0; i < 64; ++i) s[i] = -INFINITY;
       }
-      if (cls != 1 && !meta) {
-        // text only: the row's visible keys are one range (window bound,
+      if (cls != 1 && text_rule) {
+        // text rule: the row's visible keys are one range (window bound,
         // causal bound, end of the sequence)
         const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
         const int k_hi = min(q_abs, si.len_k - 1);
@@ -556,7 +558,7 @@ __device__ __forceinline__ int64_t fwd_item_index(int64_t i) {
   return i * g + ((i & 1) ? g - 1 - blockIdx.x : blockIdx.x);
 }
 __device__ __forceinline__ int fwd_ktile(const FwdItem& it, int j) {
-  return it.klist ? (it.klist[j] & 0x7fffffff) : it.kt_lo + j;
+  return it.klist ? (it.klist[j] & kTileEntryIndex) : it.kt_lo + j;
 }
 
 struct FwdPMisc {
@@ -790,6 +792,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int q_abs = q_idx + q_off;
       const int qvis = (row_valid && p.mask.vis) ? p.mask.vis[si.meta_base + q_abs] : -1;
       const int qdoc = (row_valid && p.mask.doc) ? p.mask.doc[si.meta_base + q_abs] : 0;
+      // Metadata masks read a list entry and, for tiles that are not full, the
+      // keys' vision / document ids: both are loaded ahead (the entry two tiles,
+      // the ids one tile before use) so their latency hides under the softmax.
+      // Entries are bounded by the row's capacity, not its length, so the first
+      // two are requested together with the length; entries past it go unused.
+      auto entry = [&](int j) { return (wi.klist && j < p.klist_stride) ? wi.klist[j] : 0; };
+      int ent_cur = entry(0), ent_nxt = entry(1);
       const int qa0 = wi.qt * kTileM + q_off;
       const int qa1 = min((wi.qt + 1) * kTileM, si.len_q) - 1 + q_off;
       const int n = wi.n_kt;
@@ -807,26 +816,46 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         continue;
       }
       float m_run = -INFINITY, l_half = 0.f;
+      auto key_meta = [&](int ent, int j, int& mv, int& md) {
+        mv = -1;
+        md = 0;
+        if (!meta || tid >= kTileN || j >= n ||
+            (wi.klist && (ent & (kTileEntryFull | kTileEntryText))))
+          return;
+        const int kk = (wi.klist ? (ent & kTileEntryIndex) : wi.kt_lo + j) * kTileN + tid;
+        if (kk < si.len_k) {
+          if (p.mask.vis) mv = p.mask.vis[si.meta_base + kk];
+          if (p.mask.doc) md = p.mask.doc[si.meta_base + kk];
+        }
+      };
+      int mv_cur, md_cur;
+      key_meta(ent_cur, 0, mv_cur, md_cur);
       for (int j = 0; j < n; ++j) {
         const int64_t t = T + j;
-        const int ent = wi.klist ? wi.klist[j] : 0;
-        const int k0 = (wi.klist ? (ent & 0x7fffffff) : wi.kt_lo + j) * kTileN;
+        const int ent = ent_cur;
+        const int ent2 = entry(j + 2);
+        int mv_nxt, md_nxt;
+        key_meta(ent_nxt, j + 1, mv_nxt, md_nxt);
+        const int k0 = (wi.klist ? (ent & kTileEntryIndex) : wi.kt_lo + j) * kTileN;
         const int kh = k0 + half * 64;
-        const int cls = wi.klist ? ((ent & 0x80000000) ? 1 : 2)
+        const bool text_rule = !meta || (wi.klist && (ent & kTileEntryText));
+        const int cls = wi.klist ? ((ent & kTileEntryFull) ? 1 : 2)
                                  : (meta ? 2 : text_tile_class(p.mask.window, qa0, qa1, k0,
                                                                si.len_k));
         int* kvis = reinterpret_cast<int*>(misc->xbuf[(t + 1) & 1]);
         int* kdoc = kvis + kTileN;
-        if (meta) {
+        if (!text_rule && cls != 1) {  // the same for all 256 threads
           asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
           if (tid < kTileN) {
-            const int kk = k0 + tid;
-            const bool in = kk < si.len_k;
-            kvis[tid] = (p.mask.vis && in) ? p.mask.vis[si.meta_base + kk] : -1;
-            kdoc[tid] = (p.mask.doc && in) ? p.mask.doc[si.meta_base + kk] : 0;
+            kvis[tid] = mv_cur;
+            kdoc[tid] = md_cur;
           }
           asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
         }
+        ent_cur = ent_nxt;
+        ent_nxt = ent2;
+        mv_cur = mv_nxt;
+        md_cur = md_nxt;
         if (ok) ok = mbar_wait(&misc->s_full[t & 1], (t >> 1) & 1, ab, kDevTimeoutMma);
         ok = __all_sync(0xffffffffu, ok);
         float sv[64];
@@ -848,7 +877,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
           for (int i = 0; i < 64; ++i) sv[i] = -INFINITY;
         }
-        if (cls != 1 && !meta) {
+        if (cls != 1 && text_rule) {
           const int k_lo = p.mask.window > 0 ? q_abs - p.mask.window + 1 : 0;
           const int k_hi = min(q_abs, si.len_k - 1);
 #pragma unroll

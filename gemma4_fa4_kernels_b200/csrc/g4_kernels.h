@@ -42,6 +42,15 @@ inline cudaError_t launch_chained(void (*kernel)(Exp...), dim3 grid, dim3 block,
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
 }
 
+// Key-tile list entries written by plan_qtile_lists_kernel: the key tile's
+// index in the low 30 bits, kTileEntryFull when every pair of the tile (valid
+// rows and keys) is allowed, kTileEntryText when the window / causal range
+// rule alone is exact on the tile (no key of the tile is a vision token, and
+// every valid row and key of it lie in one document).
+constexpr int kTileEntryIndex = 0x3fffffff;
+constexpr int kTileEntryText = 0x40000000;
+constexpr int kTileEntryFull = static_cast<int>(0x80000000u);
+
 struct FwdParams {
   SeqLayout layout;
   MaskSpec mask;
@@ -53,8 +62,8 @@ struct FwdParams {
   const int2* tiles;               // packed: (segment, q tile) work list, else null
   const int* n_tiles;
   // metadata masks: per query tile (flattened index) the exact key-tile list
-  // from plan_qtile_lists_kernel (entries tagged 0x80000000 when every pair is
-  // allowed) and its count in ranges[g].y; null for text masks
+  // from plan_qtile_lists_kernel (entries tagged as kTileEntry* describes) and
+  // its count in ranges[g].y; null for text masks
   const int4* ranges;
   const int* klist;
   int klist_stride;
@@ -181,16 +190,22 @@ struct DecodeParams {
   int* counters;
 };
 constexpr int kDecodeMaxGroup = 16;
-// Short-window decode: CUDA-core dot products, one launch (the last CTA of a
-// (sequence, KV head) merges the splits); query groups of at most 4 heads and
-// at most decode_short_keys(D) keys per CTA.
+// Short-window decode: CUDA-core dot products, one launch; query groups of at
+// most 4 heads and at most decode_short_keys(D) keys per CTA.  Up to
+// kDecodeClusterMax splits of a (sequence, KV head) form a cluster and merge
+// through distributed shared memory (`cluster`); more splits merge in the last
+// arriving CTA through workspace partials.
 constexpr int kDecodeShortMaxGroup = 4;
-// the merge holds every split's weight of the group's heads in shared memory
+constexpr int kDecodeClusterMax = 16;
+// the ticket merge holds every split's weight of the group's heads in shared memory
 constexpr int kDecodeShortMaxSplits = 1024;
 // keys per CTA: 32 KB of K and V rows in flight per CTA (64 keys at d256, 32
 // at d512), held in registers
 __host__ __device__ constexpr int decode_short_keys(int d) { return 16384 / d; }
-int launch_decode_short(int d, const DecodeParams& p, int num_kv_heads, cudaStream_t stream);
+int launch_decode_short(int d, const DecodeParams& p, int num_kv_heads, bool cluster,
+                        cudaStream_t stream);
+// whether clusters of `splits` CTAs of the short decode kernel can be resident
+bool decode_cluster_supported(int d, int group, int splits);
 constexpr int kDecodeMaxSplits = 1024;
 constexpr int kDecodeStages = 6;   // 32 KB ring stages
 int decode_smem_bytes(int d);

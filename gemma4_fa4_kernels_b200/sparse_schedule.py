@@ -11,9 +11,12 @@ the B200 kernel design:
 * tiles are 128 x 128 in both directions (the reference's H100 kernels use
   128 x 80 forward and 64 x 64 backward tiles);
 * every forward row also says which of its tiles are full (all pairs
-  allowed), the tiles on which the kernels skip the mask.  The backward rows
-  are the transpose (per key tile, the query tiles that reach it), which is
-  how the key-major kernels walk the same incidence.
+  allowed), the tiles on which the kernels skip the mask, and which are text
+  tiles (no vision key, one document for the tile's rows and keys), on which
+  the window / causal range rule alone is exact and the kernels read no
+  metadata.  The backward rows are the transpose (per key tile, the query
+  tiles that reach it), which is how the key-major kernels walk the same
+  incidence.
 """
 
 from __future__ import annotations
@@ -28,18 +31,25 @@ from . import _lib
 from .ops import _raise_for, _stream
 
 TILE = 128
+# key-tile list entries (include/gemma4_b200.h, g4_tile_schedule): the tile
+# index in the low 30 bits, then the text and full tags
+_ENTRY_INDEX = 0x3FFFFFFF
+_ENTRY_TEXT = 0x40000000
+_ENTRY_FULL = -0x80000000  # bit 31 of an int32 entry
 
 
 @dataclass(frozen=True)
 class SparseTileRows:
     """Ordered adjacency from row tiles to the column tiles that hold at least
-    one allowed pair; ``full`` marks columns whose every pair is allowed."""
+    one allowed pair; ``full`` marks columns whose every pair is allowed,
+    ``text`` those on which the window / causal range rule is exact."""
 
     rows: tuple[tuple[int, ...], ...]
     row_block_size: int
     column_block_size: int
     column_blocks: int
     full: tuple[tuple[bool, ...], ...] = ()
+    text: tuple[tuple[bool, ...], ...] = ()
 
     def __post_init__(self) -> None:
         for row in self.rows:
@@ -130,15 +140,16 @@ def build_gemma4_local_sparse_schedule(
     _raise_for(lib.g4_tile_schedule(ctypes.byref(a), counts.data_ptr(), keys.data_ptr(), nk,
                                     _stream(device)), "g4_tile_schedule")
     counts_h, keys_h = counts.cpu().tolist(), keys.cpu().tolist()
-    rows, full = [], []
+    rows, full, text = [], [], []
     for g in range(nq):
         ent = keys_h[g][:counts_h[g]]
-        rows.append(tuple(e & 0x7FFFFFFF for e in ent))
-        full.append(tuple(bool(e & 0x80000000) for e in ent))
+        rows.append(tuple(e & _ENTRY_INDEX for e in ent))
+        full.append(tuple(bool(e & _ENTRY_FULL) for e in ent))
+        text.append(tuple(bool(e & _ENTRY_TEXT) for e in ent))
     cols = [[] for _ in range(nk)]
     for g, row in enumerate(rows):
         for kt in row:
             cols[kt].append(g)
-    forward = SparseTileRows(tuple(rows), TILE, TILE, nk, tuple(full))
+    forward = SparseTileRows(tuple(rows), TILE, TILE, nk, tuple(full), tuple(text))
     backward = SparseTileRows(tuple(tuple(c) for c in cols), TILE, TILE, max(nq, 1))
     return Gemma4LocalSparseSchedule(q_length, k_length, forward, backward)

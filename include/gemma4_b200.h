@@ -243,8 +243,11 @@ int g4_selftest_wait(int mode, int* code, int* completed, double* wait_ms);
  * tile of 128 rows (flattened over sequences / segments), the key tiles of 128
  * keys that hold at least one allowed (query, key) pair, ascending.  This is
  * the exact incidence the kernels iterate: tiles outside a list are never
- * loaded.  Bit 31 of an entry is set when every pair of the tile (valid rows
- * and keys) is allowed, which lets the kernels skip the mask there.
+ * loaded.  An entry is the key tile's index in bits 0-29; bit 31 is set when
+ * every pair of the tile (valid rows and keys) is allowed, which lets the
+ * kernels skip the mask there; bit 30 when no key of the tile is a vision
+ * token and every valid row and key of the tile lie in one document, so the
+ * window / causal range rule alone is exact there (no metadata is read).
  * Replaces build_gemma4_local_sparse_schedule / SparseTileRows
  * (src/gemma4_fa4/sparse_schedule.py:181-374, host Python in the reference;
  * built on the device here).  Outputs (device int32): counts[n_q_tiles] and

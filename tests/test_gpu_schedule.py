@@ -8,6 +8,9 @@ evaluated at the library's 128 x 128 tiles, forward rows and the transposed
 backward rows alike.  The "full" tags (every pair of the tile allowed, mask
 skipped by the kernels) are checked against the dense oracle mask.
 
+Tiles tagged "text" (the kernels apply the window / causal range rule there
+and read no metadata) must carry exactly that rule's block of the mask.
+
 Cases cover text windows, contiguous vision spans, a vision id that repeats far
 in the future (the tiles in between must be absent), document boundaries,
 rectangular lower-right queries and a short window.
@@ -83,12 +86,24 @@ def test_device_schedule_matches_reference_incidence(name):
         vision_block_ids=None if vis is None else vis[None],
         document_ids=None if doc is None else doc[None],
         allow_vision_bidirectional=True)[0, 0]
-    for qt, (row, full) in enumerate(zip(got.forward.rows, got.forward.full)):
+    # the window / causal range rule alone (what the kernels apply on text tiles)
+    ranged = gemma4_attention_mask(batch_size=1, q_len=sq, kv_len=sk, sliding_window=w)[0, 0]
+    n_text = 0
+    for qt, (row, full, text) in enumerate(zip(got.forward.rows, got.forward.full,
+                                               got.forward.text)):
         block_q = allowed[qt * 128:(qt + 1) * 128]
-        for kt, f in zip(row, full):
+        for kt, f, tx in zip(row, full, text):
             block = block_q[:, kt * 128:(kt + 1) * 128]
             want = block.shape[1] == 128 and bool(block.all())
             assert f == want, (qt, kt)
+            if tx:
+                n_text += 1
+                rule = ranged[qt * 128:(qt + 1) * 128, kt * 128:(kt + 1) * 128]
+                assert np.array_equal(block, rule), ("text tag on a tile the rule misses", qt, kt)
+    if vis is None and doc is None:
+        assert n_text == got.forward.candidate_pairs  # no metadata: every tile is text
+    else:
+        assert 0 < n_text < got.forward.candidate_pairs
 
 
 def test_far_repeat_skips_the_tiles_between():
