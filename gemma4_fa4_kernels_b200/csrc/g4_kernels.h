@@ -190,22 +190,16 @@ struct DecodeParams {
   int* counters;
 };
 constexpr int kDecodeMaxGroup = 16;
-// Short-window decode: CUDA-core dot products, one launch; query groups of at
-// most 4 heads and at most decode_short_keys(D) keys per CTA.  Up to
-// kDecodeClusterMax splits of a (sequence, KV head) form a cluster and merge
-// through distributed shared memory (`cluster`); more splits merge in the last
-// arriving CTA through workspace partials.
+// Short-window decode: CUDA-core dot products, one launch (the last CTA of a
+// (sequence, KV head) merges the splits); query groups of at most 4 heads and
+// at most decode_short_keys(D) keys per CTA.
 constexpr int kDecodeShortMaxGroup = 4;
-constexpr int kDecodeClusterMax = 16;
-// the ticket merge holds every split's weight of the group's heads in shared memory
+// the merge holds every split's weight of the group's heads in shared memory
 constexpr int kDecodeShortMaxSplits = 1024;
 // keys per CTA: 32 KB of K and V rows in flight per CTA (64 keys at d256, 32
 // at d512), held in registers
 __host__ __device__ constexpr int decode_short_keys(int d) { return 16384 / d; }
-int launch_decode_short(int d, const DecodeParams& p, int num_kv_heads, bool cluster,
-                        cudaStream_t stream);
-// whether clusters of `splits` CTAs of the short decode kernel can be resident
-bool decode_cluster_supported(int d, int group, int splits);
+int launch_decode_short(int d, const DecodeParams& p, int num_kv_heads, cudaStream_t stream);
 constexpr int kDecodeMaxSplits = 1024;
 constexpr int kDecodeStages = 6;   // 32 KB ring stages
 int decode_smem_bytes(int d);
