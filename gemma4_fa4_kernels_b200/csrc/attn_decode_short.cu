@@ -9,21 +9,22 @@
 // (a query group of at most 4 heads gives 2 FLOP per K/V byte), so a CTA is
 // busy from its first instruction.
 //
-// CTA (split, KV head, sequence), 256 threads, at most decode_short_keys(D)
-// keys (64 for d256, 32 for d512: 32 KB of K and V):
-//   1. every K row and V chunk the CTA needs is requested up front (16-B loads
-//      into registers), so the whole slice is in flight at once; the group's
-//      query vectors go to fp32 shared memory;
-//   2. scores: warp w takes keys w, w+8, ...; each lane holds D/32 features of
-//      the key row, the group's dot products are reduced across the warp;
-//      masked keys get -inf;
-//   3. per head the split's max and sum (exp2 domain, as the other kernels);
-//   4. O: thread t owns 8 features of one key group (keys g, g+G', ...) and
-//      accumulates p * V; the key groups are summed through shared memory.
+// CTA (split, KV head, sequence), 256 threads, at most decode_short_keys(D, G)
+// keys (64 for d256 with groups of up to 2 heads: 32 KB of K and V).  Every
+// warp works alone on its own keys until the CTA combine:
+//   1. the warp requests its K rows, V rows (this lane's D/32 features of each)
+//      and the group's query features up front, so the whole slice is in
+//      flight at once;
+//   2. scores: per key and head a lane's partial dot product, summed by xor
+//      shuffles (every lane ends with every score); masked keys get -inf;
+//   3. the warp's softmax over its keys (exp2 domain, as the other kernels) and
+//      its unnormalised O = sum p V, all in registers;
+//   4. the warps' (max, sum, O) are combined through shared memory.
 // One split writes O and LSE directly.  With several splits each CTA writes its
 // unnormalised O, max and sum, then takes a ticket on the (sequence, KV head)
 // counter; the CTA that takes the last ticket merges every split (exact
-// log-sum-exp combination) and resets the counter for the next call.
+// log-sum-exp combination, every split's partial requested at once) and resets
+// the counter for the next call.
 //
 // Mask for the single query at q = Sk - 1: every key is causal (the vision rule
 // never adds a key), the window keeps k > q - W and documents doc[k] == doc[q]
@@ -54,21 +55,31 @@ __device__ __forceinline__ void bf16x8_to_float(const uint4& w, float* f) {
   }
 }
 
+template <int D, int G>
+struct ShortCfg {
+  static constexpr int kPerLane = D / 32;                // features of a row per lane
+  static constexpr int kLoads = kPerLane / 8;            // 16-B loads per lane and row
+  static constexpr int kKeys = decode_short_keys(D, G);  // keys per CTA at most
+  static constexpr int kKeysPerWarp = kKeys / kShortWarps;
+  static constexpr int kOut = G * D / kShortThreads;     // combined outputs per thread
+  // merge: split partials requested per batch and output
+  static constexpr int kBatch = kOut >= 8 ? 4 : 32 / kOut;
+  // warp partials: O [warp][G][D], max and sum [warp][G]
+  static constexpr int kSmemBytes = (kShortWarps * G * D + 2 * kShortWarps * G) * 4;
+  static_assert(kKeysPerWarp >= 1 && kKeys == kKeysPerWarp * kShortWarps, "keys per warp");
+  static_assert(G * D % kShortThreads == 0, "outputs per thread");
+};
+
 }  // namespace
 
 template <int D, int G>
 __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const DecodeParams p) {
-  constexpr int kPerLane = D / 32;               // features of a key row per lane
-  constexpr int kLoads = kPerLane / 8;           // 16-B loads per lane and key
-  constexpr int kColThreads = D / 8;             // threads covering one V row
-  constexpr int kKeyGroups = kShortThreads / kColThreads;
-  constexpr int kKeys = decode_short_keys(D);    // keys per CTA at most
-  constexpr int kKeysPerWarp = kKeys / kShortWarps;
-  constexpr int kKeysPerGroup = kKeys / kKeyGroups;
-  __shared__ float qs[G][D];
-  __shared__ float ps[G][kKeys];
-  __shared__ float red[kKeyGroups][G][D];
-  __shared__ float stat[G][2];
+  using Cfg = ShortCfg<D, G>;
+  constexpr int kPerLane = Cfg::kPerLane, kLoads = Cfg::kLoads, kKPW = Cfg::kKeysPerWarp;
+  extern __shared__ __align__(16) float sm[];
+  float* wo = sm;                                   // [warp][G][D]
+  float* wm = wo + kShortWarps * G * D;             // [warp][G]
+  float* wl = wm + kShortWarps * G;                 // [warp][G]
   __shared__ int last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -80,160 +91,171 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
   const int total = max(0, si.len_k - k_lo);
   const int per = (total + p.n_split - 1) / p.n_split;
   const int kb = k_lo + split * per;
-  const int n = min(kKeys, max(0, min(si.len_k, kb + per) - kb));
+  const int n = min(Cfg::kKeys, max(0, min(si.len_k, kb + per) - kb));
   const int head0 = kvh * G;
+  const int j0 = warp * kKPW;  // this warp's first key in the CTA's slice
 
-  // Every K row this warp needs is requested before any arithmetic (one or
-  // two 16-B loads per lane and key): the loads of a CTA are all in flight at
-  // once instead of one latency per key.
+  // ---- 1. every load of the warp in flight at once ----
   const __nv_bfloat16* kbase = p.k + static_cast<int64_t>(si.b_coord) * p.k_stride[0] +
-                               static_cast<int64_t>(kvh) * p.k_stride[2];
-  uint4 kraw[kKeysPerWarp][kLoads];
-#pragma unroll
-  for (int i = 0; i < kKeysPerWarp; ++i) {
-    const int j = warp + i * kShortWarps;
-    const __nv_bfloat16* row =
-        kbase + static_cast<int64_t>(si.k_base + kb + min(j, max(n - 1, 0))) * p.k_stride[1];
-#pragma unroll
-    for (int l = 0; l < kLoads; ++l)
-      kraw[i][l] = j < n ? *reinterpret_cast<const uint4*>(row + l * 256 + lane * 8)
-                         : make_uint4(0, 0, 0, 0);
-  }
-  // and this thread's V rows: K and V of the whole slice are in flight together
-  const int vc = tid % kColThreads, vg = tid / kColThreads;
+                               static_cast<int64_t>(kvh) * p.k_stride[2] + lane * 8;
   const __nv_bfloat16* vbase = p.v + static_cast<int64_t>(si.b_coord) * p.v_stride[0] +
-                               static_cast<int64_t>(kvh) * p.v_stride[2] + vc * 8;
-  uint4 vraw[kKeysPerGroup];
+                               static_cast<int64_t>(kvh) * p.v_stride[2] + lane * 8;
+  uint4 kr[kKPW][kLoads], vr[kKPW][kLoads];
 #pragma unroll
-  for (int i = 0; i < kKeysPerGroup; ++i) {
-    const int j = vg + i * kKeyGroups;
-    vraw[i] = j < n ? *reinterpret_cast<const uint4*>(
-                          vbase + static_cast<int64_t>(si.k_base + kb + j) * p.v_stride[1])
+  for (int i = 0; i < kKPW; ++i) {
+    const bool in = j0 + i < n;
+    const int64_t t = si.k_base + kb + min(j0 + i, max(n - 1, 0));
+#pragma unroll
+    for (int l = 0; l < kLoads; ++l) {
+      kr[i][l] = in ? *reinterpret_cast<const uint4*>(kbase + t * p.k_stride[1] + l * 256)
                     : make_uint4(0, 0, 0, 0);
+      vr[i][l] = in ? *reinterpret_cast<const uint4*>(vbase + t * p.v_stride[1] + l * 256)
+                    : make_uint4(0, 0, 0, 0);
+    }
   }
-  for (int i = tid; i < G * D; i += kShortThreads) {
-    const int h = i / D, d = i % D;
-    qs[h][d] = __bfloat162float(p.q[static_cast<int64_t>(si.b_coord) * p.q_stride[0] +
-                                    static_cast<int64_t>(si.q_base) * p.q_stride[1] +
-                                    static_cast<int64_t>(head0 + h) * p.q_stride[2] + d]);
-  }
-  const int qdoc = (p.doc != nullptr && si.len_k > 0) ? p.doc[si.meta_base + q_abs] : 0;
-  __syncthreads();
-
-  // ---- scores (log2 domain) ----
-  float qr[G][kPerLane];
+  uint4 qr[G][kLoads];
+  const __nv_bfloat16* qbase = p.q + static_cast<int64_t>(si.b_coord) * p.q_stride[0] +
+                               static_cast<int64_t>(si.q_base) * p.q_stride[1] + lane * 8;
 #pragma unroll
   for (int h = 0; h < G; ++h)
 #pragma unroll
     for (int l = 0; l < kLoads; ++l)
+      qr[h][l] = *reinterpret_cast<const uint4*>(
+          qbase + static_cast<int64_t>(head0 + h) * p.q_stride[2] + l * 256);
+  int kdoc[kKPW];
+  int qdoc = 0;
+  if (p.doc != nullptr) {
+    qdoc = p.doc[si.meta_base + q_abs];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) qr[h][l * 8 + e] = qs[h][l * 256 + lane * 8 + e];
-#pragma unroll
-  for (int i = 0; i < kKeysPerWarp; ++i) {
-    const int j = warp + i * kShortWarps;
-    float kf[kPerLane];
-#pragma unroll
-    for (int l = 0; l < kLoads; ++l) bf16x8_to_float(kraw[i][l], kf + l * 8);
-    float dot[G];
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      float acc = 0.f;
-#pragma unroll
-      for (int e = 0; e < kPerLane; ++e) acc = fmaf(qr[h][e], kf[e], acc);
-      dot[h] = acc;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int h = 0; h < G; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], off);
-    if (lane == 0 && j < n) {
-      const bool keep = p.doc == nullptr || p.doc[si.meta_base + kb + j] == qdoc;
-#pragma unroll
-      for (int h = 0; h < G; ++h) ps[h][j] = keep ? dot[h] * kLog2e : -INFINITY;
-    }
+    for (int i = 0; i < kKPW; ++i) kdoc[i] = j0 + i < n ? p.doc[si.meta_base + kb + j0 + i] : 0;
   }
-  __syncthreads();
 
-  // ---- per-head max and sum over this split's keys ----
-  if (warp < G) {
-    float m = -INFINITY;
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, ps[warp][j]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    const float msub = m == -INFINITY ? 0.f : m;
-    float l = 0.f;
-    for (int j = lane; j < n; j += 32) {
-      const float e = ex2(ps[warp][j] - msub);  // exp2(-inf) = 0
-      ps[warp][j] = e;
-      l += e;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-    if (lane == 0) {
-      stat[warp][0] = m;
-      stat[warp][1] = l;
-    }
-  }
-  __syncthreads();
-
-  // ---- O = P V over this split's keys ----
+  // ---- 2. scores (log2 domain), summed across the warp ----
+  float s[G][kKPW];
   {
-    float acc[G][8];
+    float qf[G][kPerLane];
 #pragma unroll
     for (int h = 0; h < G; ++h)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[h][e] = 0.f;
+      for (int l = 0; l < kLoads; ++l) bf16x8_to_float(qr[h][l], qf[h] + l * 8);
 #pragma unroll
-    for (int i = 0; i < kKeysPerGroup; ++i) {
-      const int j = vg + i * kKeyGroups;
-      if (j < n) {
-        float vf[8];
-        bf16x8_to_float(vraw[i], vf);
+    for (int i = 0; i < kKPW; ++i) {
+      float kf[kPerLane];
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float w = ps[h][j];
+      for (int l = 0; l < kLoads; ++l) bf16x8_to_float(kr[i][l], kf + l * 8);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[h][e] = fmaf(w, vf[e], acc[h][e]);
-        }
+      for (int h = 0; h < G; ++h) {
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < kPerLane; ++e) acc = fmaf(qf[h][e], kf[e], acc);
+        s[h][i] = acc;
       }
     }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
     for (int h = 0; h < G; ++h)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) red[vg][h][vc * 8 + e] = acc[h][e];
+      for (int i = 0; i < kKPW; ++i) s[h][i] += __shfl_xor_sync(0xffffffffu, s[h][i], off);
+
+  // ---- 3. the warp's softmax and O over its keys ----
+  float m[G], l[G], acc[G][kPerLane];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kKPW; ++i) {
+      const bool keep = j0 + i < n && (p.doc == nullptr || kdoc[i] == qdoc);
+      s[h][i] = keep ? s[h][i] * kLog2e : -INFINITY;
+      m[h] = fmaxf(m[h], s[h][i]);
+    }
+    const float msub = m[h] == -INFINITY ? 0.f : m[h];
+    l[h] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kKPW; ++i) {
+      s[h][i] = ex2(s[h][i] - msub);  // exp2(-inf) = 0
+      l[h] += s[h][i];
+    }
+#pragma unroll
+    for (int e = 0; e < kPerLane; ++e) acc[h][e] = 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < kKPW; ++i) {
+    float vf[kPerLane];
+#pragma unroll
+    for (int q = 0; q < kLoads; ++q) bf16x8_to_float(vr[i][q], vf + q * 8);
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+      for (int e = 0; e < kPerLane; ++e) acc[h][e] = fmaf(s[h][i], vf[e], acc[h][e]);
+  }
+
+  // ---- 4. combine the warps ----
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float* dst = wo + (warp * G + h) * D + lane * 8;
+#pragma unroll
+    for (int q = 0; q < kLoads; ++q) {
+      reinterpret_cast<float4*>(dst + q * 256)[0] =
+          make_float4(acc[h][q * 8 + 0], acc[h][q * 8 + 1], acc[h][q * 8 + 2], acc[h][q * 8 + 3]);
+      reinterpret_cast<float4*>(dst + q * 256)[1] =
+          make_float4(acc[h][q * 8 + 4], acc[h][q * 8 + 5], acc[h][q * 8 + 6], acc[h][q * 8 + 7]);
+    }
+    if (lane == 0) {
+      wm[warp * G + h] = m[h];
+      wl[warp * G + h] = l[h];
+    }
   }
   __syncthreads();
-
+  const int ns = p.n_split;
   const int hq = p.num_q_heads;
-  if (p.n_split == 1) {
-    for (int i = tid; i < G * D; i += kShortThreads) {
-      const int h = i / D, d = i % D;
-      float o = 0.f;
+  float co[Cfg::kOut], cm[Cfg::kOut], cl[Cfg::kOut];  // this CTA's O, max and sum
 #pragma unroll
-      for (int g = 0; g < kKeyGroups; ++g) o += red[g][h][d];
-      const float l = stat[h][1];
+  for (int c = 0; c < Cfg::kOut; ++c) {
+    const int i = tid + c * kShortThreads;
+    const int h = i / D, d = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kShortWarps; ++w)
+      if (wl[w * G + h] > 0.f) M = fmaxf(M, wm[w * G + h]);
+    float L = 0.f, o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kShortWarps; ++w) {
+      const float lw = wl[w * G + h];
+      const float x = lw > 0.f ? ex2(wm[w * G + h] - M) : 0.f;
+      L = fmaf(x, lw, L);
+      o = fmaf(x, wo[(w * G + h) * D + d], o);
+    }
+    co[c] = o;
+    cm[c] = M;
+    cl[c] = L;
+  }
+  if (ns == 1) {
+#pragma unroll
+    for (int c = 0; c < Cfg::kOut; ++c) {
+      const int i = tid + c * kShortThreads;
+      const int h = i / D, d = i % D;
       p.o[static_cast<int64_t>(si.b_coord) * p.o_stride[0] +
           static_cast<int64_t>(si.q_base) * p.o_stride[1] +
           static_cast<int64_t>(head0 + h) * p.o_stride[2] + d] =
-          __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+          __float2bfloat16_rn(cl[c] > 0.f ? co[c] / cl[c] : 0.f);
       if (d == 0)
         p.lse[static_cast<int64_t>(si.b_coord) * p.lse_stride[0] +
               static_cast<int64_t>(head0 + h) * p.lse_stride[1] + si.q_base] =
-            l > 0.f ? (stat[h][0] + __log2f(l)) * kLn2 : -INFINITY;
+            cl[c] > 0.f ? (cm[c] + __log2f(cl[c])) * kLn2 : -INFINITY;
     }
     return;
   }
 
   // ---- several splits: partials, then the last arriving CTA merges ----
-  const int ns = p.n_split;
-  for (int i = tid; i < G * D; i += kShortThreads) {
-    const int h = i / D, d = i % D;
-    float o = 0.f;
 #pragma unroll
-    for (int g = 0; g < kKeyGroups; ++g) o += red[g][h][d];
+  for (int c = 0; c < Cfg::kOut; ++c) {
+    const int i = tid + c * kShortThreads;
+    const int h = i / D, d = i % D;
     const int64_t row = (static_cast<int64_t>(seq) * hq + head0 + h) * ns + split;
-    p.part_o[row * D + d] = o;
-    if (d == 0) p.part_ml[row] = make_float2(stat[h][0], stat[h][1]);
+    p.part_o[row * D + d] = co[c];
+    if (d == 0) p.part_ml[row] = make_float2(cm[c], cl[c]);
   }
   __threadfence();
   __syncthreads();
@@ -242,29 +264,27 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // Merge, latency-bound on L2: every split's (max, sum) is fetched in
-  // parallel into shared memory (the O reduction buffer, free again), each
-  // head's weights 2^(m_s - M) / L are formed once, then every thread sums its
-  // features over the splits with independent loads.
-  float* wts = &red[0][0][0];                  // [G][ns] weights
-  float* sums = wts + G * ns;                  // [G][ns] row sums, then unused
-  for (int i = tid; i < G * ns; i += kShortThreads) {
-    const int h = i / ns, s2 = i % ns;
-    const float2 ml = __ldcg(p.part_ml + (static_cast<int64_t>(seq) * hq + head0 + h) * ns + s2);
-    wts[i] = ml.y > 0.f ? ml.x : -INFINITY;
-    sums[i] = ml.y;
-  }
-  __syncthreads();
+  // Merge: per head the splits' weights 2^(m_s - M) / L (warp h, in shared
+  // memory over the warp partials, which are no longer read), then every
+  // thread sums its outputs over the splits with kBatch loads per output in
+  // flight.
+  float* wts = wo;  // [G][ns]
   if (warp < G) {
+    const float2* ml = p.part_ml + (static_cast<int64_t>(seq) * hq + head0 + warp) * ns;
     float M = -INFINITY;
-    for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, wts[warp * ns + s2]);
+    for (int s2 = lane; s2 < ns; s2 += 32) {
+      const float2 v = __ldcg(ml + s2);
+      const float mv = v.y > 0.f ? v.x : -INFINITY;
+      wts[warp * ns + s2] = mv;
+      M = fmaxf(M, mv);
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
     float L = 0.f;
     for (int s2 = lane; s2 < ns; s2 += 32) {
       const float w = M == -INFINITY ? 0.f : ex2(wts[warp * ns + s2] - M);
       wts[warp * ns + s2] = w;
-      L = fmaf(w, sums[warp * ns + s2], L);
+      L = fmaf(w, __ldcg(ml + s2).y, L);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
@@ -272,42 +292,72 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
     const float inv = L > 0.f ? 1.f / L : 0.f;
     for (int s2 = lane; s2 < ns; s2 += 32) wts[warp * ns + s2] *= inv;
     if (lane == 0) {
-      stat[warp][0] = M;
-      stat[warp][1] = L;
+      wm[warp] = M;
+      wl[warp] = L;
     }
   }
   __syncthreads();
-  for (int i = tid; i < G * D; i += kShortThreads) {
+  float out[Cfg::kOut];
+#pragma unroll
+  for (int c = 0; c < Cfg::kOut; ++c) out[c] = 0.f;
+  for (int s0 = 0; s0 < ns; s0 += Cfg::kBatch) {
+    float v[Cfg::kOut][Cfg::kBatch];
+#pragma unroll
+    for (int c = 0; c < Cfg::kOut; ++c) {
+      const int i = tid + c * kShortThreads;
+      const int h = i / D, d = i % D;
+      const float* po = p.part_o + (static_cast<int64_t>(seq) * hq + head0 + h) * ns * D + d;
+#pragma unroll
+      for (int b = 0; b < Cfg::kBatch; ++b)
+        v[c][b] = s0 + b < ns ? __ldcg(po + static_cast<int64_t>(s0 + b) * D) : 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < Cfg::kOut; ++c) {
+      const int h = (tid + c * kShortThreads) / D;
+#pragma unroll
+      for (int b = 0; b < Cfg::kBatch; ++b)
+        if (s0 + b < ns) out[c] = fmaf(wts[h * ns + s0 + b], v[c][b], out[c]);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < Cfg::kOut; ++c) {
+    const int i = tid + c * kShortThreads;
     const int h = i / D, d = i % D;
-    const float* po = p.part_o + (static_cast<int64_t>(seq) * hq + head0 + h) * ns * D + d;
-    const float* w = wts + h * ns;
-    float acc = 0.f;
-#pragma unroll 8
-    for (int s2 = 0; s2 < ns; ++s2) acc = fmaf(w[s2], __ldcg(po + static_cast<int64_t>(s2) * D), acc);
     p.o[static_cast<int64_t>(si.b_coord) * p.o_stride[0] +
         static_cast<int64_t>(si.q_base) * p.o_stride[1] +
-        static_cast<int64_t>(head0 + h) * p.o_stride[2] + d] = __float2bfloat16_rn(acc);
+        static_cast<int64_t>(head0 + h) * p.o_stride[2] + d] = __float2bfloat16_rn(out[c]);
     if (d == 0) {
-      const float L = stat[h][1];
+      const float L = wl[h];
       p.lse[static_cast<int64_t>(si.b_coord) * p.lse_stride[0] +
             static_cast<int64_t>(head0 + h) * p.lse_stride[1] + si.q_base] =
-          L > 0.f ? (stat[h][0] + __log2f(L)) * kLn2 : -INFINITY;
+          L > 0.f ? (wm[h] + __log2f(L)) * kLn2 : -INFINITY;
     }
   }
   if (tid == 0) *counter = 0;  // ready for the next call on this workspace
 }
 
+template <int D, int G>
+static int launch_short_dg(const DecodeParams& p, int num_kv_heads, cudaStream_t stream) {
+  constexpr int kSmem = ShortCfg<D, G>::kSmemBytes;
+  if (kSmem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(decode_short_kernel<D, G>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  const dim3 grid(p.n_split, num_kv_heads, p.layout.batch);
+  decode_short_kernel<D, G><<<grid, kShortThreads, kSmem, stream>>>(p);
+  return static_cast<int>(cudaGetLastError());
+}
+
 template <int D>
 static int launch_short_d(const DecodeParams& p, int num_kv_heads, cudaStream_t stream) {
-  const dim3 grid(p.n_split, num_kv_heads, p.layout.batch);
   switch (p.group) {
-    case 1: decode_short_kernel<D, 1><<<grid, kShortThreads, 0, stream>>>(p); break;
-    case 2: decode_short_kernel<D, 2><<<grid, kShortThreads, 0, stream>>>(p); break;
-    case 3: decode_short_kernel<D, 3><<<grid, kShortThreads, 0, stream>>>(p); break;
-    case 4: decode_short_kernel<D, 4><<<grid, kShortThreads, 0, stream>>>(p); break;
+    case 1: return launch_short_dg<D, 1>(p, num_kv_heads, stream);
+    case 2: return launch_short_dg<D, 2>(p, num_kv_heads, stream);
+    case 3: return launch_short_dg<D, 3>(p, num_kv_heads, stream);
+    case 4: return launch_short_dg<D, 4>(p, num_kv_heads, stream);
     default: return static_cast<int>(cudaErrorInvalidValue);
   }
-  return static_cast<int>(cudaGetLastError());
 }
 
 int launch_decode_short(int d, const DecodeParams& p, int num_kv_heads, cudaStream_t stream) {

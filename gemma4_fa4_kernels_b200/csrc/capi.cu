@@ -292,11 +292,12 @@ int64_t decode_keys(const g4_attn_args* a) {
 bool decode_short(const g4_attn_args* a) {
   const int G = a->num_q_heads / a->num_kv_heads;
   return a->window > 0 && G <= g4::kDecodeShortMaxGroup &&
-         decode_keys(a) <= int64_t(g4::kDecodeShortMaxSplits) * g4::decode_short_keys(a->head_dim_qk);
+         decode_keys(a) <=
+             int64_t(g4::kDecodeShortMaxSplits) * g4::decode_short_keys(a->head_dim_qk, G);
 }
 
 // Key-range splits per (sequence, KV head).  Short-window kernel: two CTAs per
-// SM, at least 32 keys and at most decode_short_keys(D) keys per CTA.  Tensor-core
+// SM, at least 32 keys and at most decode_short_keys(D, G) keys per CTA.  Tensor-core
 // kernel: enough CTAs for one per SM, never more splits than 128-key tiles, and
 // no split left without a tile at the longest sequence.
 int decode_splits(const g4_attn_args* a) {
@@ -305,7 +306,7 @@ int decode_splits(const g4_attn_args* a) {
   if (a->window > 0) keys = std::min<int64_t>(keys, a->window);
   if (decode_short(a)) {
     const int64_t units = std::max<int64_t>(1, int64_t(a->batch) * a->num_kv_heads);
-    const int per = g4::decode_short_keys(a->head_dim_qk);
+    const int per = g4::decode_short_keys(a->head_dim_qk, a->num_q_heads / a->num_kv_heads);
     const int64_t lo = (keys + per - 1) / per;
     // one wave: at most two CTAs per SM in total
     int64_t n = std::min<int64_t>(std::max<int64_t>(1, 2 * sm_count() / units),

@@ -192,13 +192,16 @@ struct DecodeParams {
 constexpr int kDecodeMaxGroup = 16;
 // Short-window decode: CUDA-core dot products, one launch (the last CTA of a
 // (sequence, KV head) merges the splits); query groups of at most 4 heads and
-// at most decode_short_keys(D) keys per CTA.
+// at most decode_short_keys(D, G) keys per CTA.
 constexpr int kDecodeShortMaxGroup = 4;
 // the merge holds every split's weight of the group's heads in shared memory
 constexpr int kDecodeShortMaxSplits = 1024;
-// keys per CTA: 32 KB of K and V rows in flight per CTA (64 keys at d256, 32
-// at d512), held in registers
-__host__ __device__ constexpr int decode_short_keys(int d) { return 16384 / d; }
+// keys per CTA, held in registers: 32 KB of K and V rows in flight per CTA
+// (64 keys at d256, 32 at d512), half that for groups of 3 or 4 heads (whose
+// query features take the registers)
+__host__ __device__ constexpr int decode_short_keys(int d, int g) {
+  return (g > 2 ? 8192 : 16384) / d;
+}
 int launch_decode_short(int d, const DecodeParams& p, int num_kv_heads, cudaStream_t stream);
 constexpr int kDecodeMaxSplits = 1024;
 constexpr int kDecodeStages = 6;   // 32 KB ring stages
