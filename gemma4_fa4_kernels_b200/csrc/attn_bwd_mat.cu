@@ -124,18 +124,24 @@ __device__ __forceinline__ uint32_t tile_chunk_offset(int r, int c) {
 // plan (metadata masks): per query tile the exact list of key tiles that hold
 // at least one allowed pair, each tagged kTileEntryFull when all its pairs (of
 // valid rows and keys) are allowed and kTileEntryText when the range rule is
-// exact on it.  One CTA per query tile, one thread per row: the row's key
-// bound is [q - W + 1, max(q, pair_last)] (the vision exception has no right
-// window cap, masks.py:55-66).  Each key tile under the tile's bound has its
-// metadata staged in shared memory (the next tile's is loaded meanwhile); a
-// tile without vision keys whose keys share the query tile's single document
-// is classified per row in closed form, any other tile by testing the exact
-// predicate on every pair.  Writes ranges[g] = (first listed tile, count, -,
-// sequence); the scratch prefix follows in plan_qtile_ranges_kernel.  The
-// reference builds the same incidence on the host (sparse_schedule.py:181-374).
+// exact on it.  One CTA per query tile, four threads per row (a quarter of the
+// keys each): the row's key bound is [q - W + 1, max(q, pair_last)] (the vision
+// exception has no right window cap, masks.py:55-66).  Each key tile under
+// the tile's bound has its metadata staged in shared memory (the next tile's
+// is loaded meanwhile); a tile without vision keys whose keys share the query
+// tile's single document is classified per row in closed form, any other tile
+// by testing the exact predicate on every pair.  Writes ranges[g] = (first
+// listed tile, count, -, sequence); the scratch prefix follows in
+// plan_qtile_ranges_kernel.  The reference builds the same incidence on the
+// host (sparse_schedule.py:181-374).
 // =====================================================================================
-__global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParams p) {
-  __shared__ int kvis[kTileN], kdoc[kTileN];
+constexpr int kPlanParts = 4;
+constexpr int kPlanThreads = kTileM * kPlanParts;
+constexpr int kPlanKeysPerPart = kTileN / kPlanParts;
+
+__global__ void __launch_bounds__(kPlanThreads) plan_qtile_lists_kernel(const MatParams p) {
+  __shared__ __align__(16) int kvis[kTileN];
+  __shared__ __align__(16) int kdoc[kTileN];
   __shared__ int lo_s, hi_s, qdoc0;
   pdl_enter();
   const int g = blockIdx.x;
@@ -152,7 +158,9 @@ __global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParam
     qt = g % p.n_qt_fixed;
   }
   const SeqInfo si = p.layout.seq(seq);
-  const int r = threadIdx.x;
+  const int tid = threadIdx.x;
+  const int r = tid & (kTileM - 1);  // query row
+  const int part = tid / kTileM;     // key quarter [part * 32, + 32) of each tile
   const int W = p.mask.window;
   const int q_idx = qt * kTileM + r;
   const bool valid = q_idx < si.len_q;  // row 0 of a listed query tile always is
@@ -167,13 +175,13 @@ __global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParam
       hi = p.mask.pair_last ? max(hi, p.mask.pair_last[si.meta_base + q_abs]) : si.len_k - 1;
     hi = min(hi, si.len_k - 1);
   }
-  if (r == 0) {
+  if (tid == 0) {
     lo_s = 0x7fffffff;
     hi_s = -1;
     qdoc0 = qdoc;
   }
   __syncthreads();
-  if (valid && hi >= lo) {
+  if (part == 0 && valid && hi >= lo) {
     atomicMin(&lo_s, lo);
     atomicMax(&hi_s, hi);
   }
@@ -185,9 +193,10 @@ __global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParam
   int cnt = 0, first = 0;
   const int kt_begin = hi_s >= 0 ? lo_s / kTileN : 0;
   const int kt_end = hi_s >= 0 ? hi_s / kTileN : -1;
+  // threads 0..127 stage key k0 + tid of each tile
   auto key_meta = [&](int kt, int& v, int& d) {
-    const int kk = kt * kTileN + r;
-    const bool kin = kt <= kt_end && kk < si.len_k;
+    const int kk = kt * kTileN + tid;
+    const bool kin = tid < kTileN && kt <= kt_end && kk < si.len_k;
     v = (p.mask.vis && kin) ? p.mask.vis[si.meta_base + kk] : -1;
     d = (p.mask.doc && kin) ? p.mask.doc[si.meta_base + kk] : 0;
   };
@@ -197,35 +206,48 @@ __global__ void __launch_bounds__(kTileM) plan_qtile_lists_kernel(const MatParam
     const int k0 = kt * kTileN;
     const int cv = nv, cd = nd;
     key_meta(kt + 1, nv, nd);  // in flight while this tile is classified
-    const bool kin = k0 + r < si.len_k;
+    const bool kin = tid < kTileN && k0 + tid < si.len_k;
     __syncthreads();  // the previous tile's metadata is no longer read
-    kvis[r] = cv;
-    kdoc[r] = cd;
+    if (tid < kTileN) {
+      kvis[tid] = cv;
+      kdoc[tid] = cd;
+    }
     const bool text = one_doc && __syncthreads_and(!kin || (cv < 0 && cd == qdoc0));
-    bool any = false, all = valid;
+    bool any = false, all = true;
     if (valid && text) {
-      const int k1 = min(k0 + kTileN, si.len_k) - 1;
-      any = max(lo_r, k0) <= min(hi_r, k1);
-      all = lo_r <= k0 && hi_r >= k0 + kTileN - 1;
+      if (part == 0) {
+        const int k1 = min(k0 + kTileN, si.len_k) - 1;
+        any = max(lo_r, k0) <= min(hi_r, k1);
+        all = lo_r <= k0 && hi_r >= k0 + kTileN - 1;
+      }
     } else if (valid) {
-      for (int j = 0; j < kTileN; ++j) {
-        const int k = k0 + j;
-        const bool ok = k < si.len_k && k >= lo && k <= hi &&
-                        mask_allows(W, q_abs, k, qvis, qdoc, kvis[j], kdoc[j]);
-        any |= ok;
-        all &= ok;
+      const int kq = k0 + part * kPlanKeysPerPart;
+      const int4* v4 = reinterpret_cast<const int4*>(kvis + part * kPlanKeysPerPart);
+      const int4* d4 = reinterpret_cast<const int4*>(kdoc + part * kPlanKeysPerPart);
+#pragma unroll
+      for (int c = 0; c < kPlanKeysPerPart / 4; ++c) {
+        const int4 a = v4[c], b = d4[c];
+        const int av[4] = {a.x, a.y, a.z, a.w}, bd[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = kq + 4 * c + e;
+          const bool ok = k < si.len_k && k >= lo && k <= hi &&
+                          mask_allows(W, q_abs, k, qvis, qdoc, av[e], bd[e]);
+          any |= ok;
+          all &= ok;
+        }
       }
     }
     const int any_t = __syncthreads_or(any);
     const int all_t = __syncthreads_and(all || !valid);
     if (any_t) {
-      if (r == 0 && cnt < p.klist_stride)
+      if (tid == 0 && cnt < p.klist_stride)
         out[cnt] = kt | (all_t ? kTileEntryFull : 0) | (text ? kTileEntryText : 0);
       if (cnt == 0) first = kt;
       ++cnt;
     }
   }
-  if (r == 0) p.ranges[g] = make_int4(first, min(cnt, p.klist_stride), 0, seq);
+  if (tid == 0) p.ranges[g] = make_int4(first, min(cnt, p.klist_stride), 0, seq);
 }
 
 // =====================================================================================
@@ -1645,7 +1667,7 @@ int launch_cast_f32_bf16(const float* src, int64_t rows, int heads, int d, __nv_
 
 int launch_plan_qtile_lists(const MatParams& p, int n_qt_total, cudaStream_t stream) {
   if (n_qt_total <= 0) return 0;
-  cudaError_t e = launch_chained(plan_qtile_lists_kernel, dim3(n_qt_total), dim3(kTileM), 0,
+  cudaError_t e = launch_chained(plan_qtile_lists_kernel, dim3(n_qt_total), dim3(kPlanThreads), 0,
                                  stream, p);
   if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
