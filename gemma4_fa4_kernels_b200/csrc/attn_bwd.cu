@@ -39,55 +39,90 @@ namespace g4 {
 // =====================================================================================
 // 1. preprocess
 // =====================================================================================
-// One warp per (token, head) row; every load of the row is issued before the
-// first multiply (DV / 256 pairs of 16-B loads per lane) so that a warp keeps
-// the whole row in flight.
+// One warp per 512 features of (token, head) rows: a row of d512, two rows of
+// d256.  Every load of the warp is issued before the first multiply (two
+// 16-B loads of O and dO per lane and row of 256 features), so that a warp
+// keeps 2 KB in flight whatever the head dimension.
+template <int DV>
+struct PreCfg {
+  static constexpr int kRows = DV == 256 ? 2 : 1;  // rows per warp
+  static constexpr int kIters = DV / 256;           // 16-B loads per lane and row
+};
+
 template <int DV>
 __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const BwdParams p, int64_t tokens_q) {
+  constexpr int kRows = PreCfg<DV>::kRows, kIters = PreCfg<DV>::kIters;
   pdl_enter();
-  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= tokens_q * p.num_q_heads) return;
-  const int h = static_cast<int>(row % p.num_q_heads);
-  const int64_t tok = row / p.num_q_heads;
-  int64_t b, s;
-  if (p.layout.packed()) {
-    b = 0;
-    s = tok;
-  } else {
-    b = tok / p.layout.seqlen_q;
-    s = tok % p.layout.seqlen_q;
+  const int64_t rows = tokens_q * p.num_q_heads;
+  const int64_t row0 = warp_id * kRows;
+  if (row0 >= rows) return;
+  uint4 ov[kRows][kIters], gv[kRows][kIters];
+  int64_t bs[kRows], ss[kRows], tk[kRows];
+  int hs[kRows];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    const int64_t row = min(row0 + r, rows - 1);  // a missing last row repeats (unwritten)
+    hs[r] = static_cast<int>(row % p.num_q_heads);
+    tk[r] = row / p.num_q_heads;
+    if (p.layout.packed()) {
+      bs[r] = 0;
+      ss[r] = tk[r];
+    } else {
+      bs[r] = tk[r] / p.layout.seqlen_q;
+      ss[r] = tk[r] % p.layout.seqlen_q;
+    }
+    const __nv_bfloat16* o =
+        p.o + bs[r] * p.o_stride[0] + ss[r] * p.o_stride[1] + hs[r] * p.o_stride[2];
+    const __nv_bfloat16* g =
+        p.dout + bs[r] * p.do_stride[0] + ss[r] * p.do_stride[1] + hs[r] * p.do_stride[2];
+#pragma unroll
+    for (int it = 0; it < kIters; ++it) {
+      ov[r][it] = *reinterpret_cast<const uint4*>(o + it * 256 + lane * 8);
+      gv[r][it] = *reinterpret_cast<const uint4*>(g + it * 256 + lane * 8);
+    }
   }
-  const __nv_bfloat16* o = p.o + b * p.o_stride[0] + s * p.o_stride[1] + h * p.o_stride[2];
-  const __nv_bfloat16* g = p.dout + b * p.do_stride[0] + s * p.do_stride[1] + h * p.do_stride[2];
-  constexpr int kIters = DV / 256;
-  uint4 ov[kIters], gv[kIters];
+  float acc[kRows];
 #pragma unroll
-  for (int it = 0; it < kIters; ++it) {
-    ov[it] = *reinterpret_cast<const uint4*>(o + it * 256 + lane * 8);
-    gv[it] = *reinterpret_cast<const uint4*>(g + it * 256 + lane * 8);
-  }
-  float acc = 0.f;
+  for (int r = 0; r < kRows; ++r) {
+    acc[r] = 0.f;
 #pragma unroll
-  for (int it = 0; it < kIters; ++it) {
-    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov[it]);
-    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[it]);
+    for (int it = 0; it < kIters; ++it) {
+      const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov[r][it]);
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[r][it]);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 a = __bfloat1622float2(o2[i]);
-      const float2 d = __bfloat1622float2(g2[i]);
-      acc = fmaf(a.x, d.x, acc);
-      acc = fmaf(a.y, d.y, acc);
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __bfloat1622float2(o2[i]);
+        const float2 d = __bfloat1622float2(g2[i]);
+        acc[r] = fmaf(a.x, d.x, acc[r]);
+        acc[r] = fmaf(a.y, d.y, acc[r]);
+      }
     }
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+  if (lane < kRows && row0 + lane < rows) {
+    // lane r writes row r (the values are selected without dynamic indexing)
+    float a = acc[0];
+    int64_t b = bs[0], s = ss[0], tok = tk[0];
+    int h = hs[0];
+#pragma unroll
+    for (int r = 1; r < kRows; ++r)
+      if (lane == r) {
+        a = acc[r];
+        b = bs[r];
+        s = ss[r];
+        tok = tk[r];
+        h = hs[r];
+      }
     const int64_t li = b * p.lse_stride[0] + h * p.lse_stride[1] + s;
     const float lse = p.lse[li];
     const float dl = p.dlse ? p.dlse[li] : 0.f;
     const int64_t wi = h * p.ws_head_stride + tok;
-    p.delta[wi] = acc - (isfinite(dl) ? dl : 0.f);
+    p.delta[wi] = a - (isfinite(dl) ? dl : 0.f);
     p.lse2[wi] = lse == -INFINITY ? -INFINITY : lse * kLog2e;
   }
 }
@@ -96,7 +131,9 @@ int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int64_t tokens_q,
                           cudaStream_t stream) {
   const int64_t rows = tokens_q * p.num_q_heads;
   const int threads = 256;
-  const int64_t blocks = (rows * 32 + threads - 1) / threads;
+  const int per_warp = head_dim_v == 256 ? PreCfg<256>::kRows : PreCfg<512>::kRows;
+  const int64_t warps = (rows + per_warp - 1) / per_warp;
+  const int64_t blocks = (warps * 32 + threads - 1) / threads;
   if (blocks == 0) return 0;
   const dim3 grid(static_cast<unsigned>(blocks));
   const cudaError_t e =
