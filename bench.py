@@ -567,18 +567,17 @@ def steady(fn, dev, per_rep_ms, *, batches=5):
 
 
 def workload_line(name, fl, fn, dev, peaks, *, warm, reps):
-    """A secondary configuration: fwd+bwd time per step with steps back to back
-    (the value), the per-call ruler beside it (events around each rep: an idle
-    GPU waits for the host's first launch there, which matters for sub-ms
-    steps), TFLOP/s and % of both peaks, and the kernels one step launched."""
+    """A secondary configuration: median fwd+bwd time over `reps` (events around
+    each rep; the value), the same steps timed back to back beside it, TFLOP/s
+    and % of both peaks, and the kernels one step launched."""
     launches = launched(fn, dev)  # one step, also the first warm-up
     r = ruler(fn, dev, warm=max(warm - 1, 0), reps=reps)
     st = steady(fn, dev, r["median_ms"], batches=5 if r["median_ms"] < 1000 else 1)
-    tf = fl["total"] / (st["median_ms"] * 1e-3) / 1e12
-    return {"workload": name, "median_ms": st["median_ms"], "iqr_ms": st["iqr_ms"],
-            "timing": f"back-to-back steps, {st['steps_per_batch']} per event pair, median of "
-                      f"{st['batches']} batches",
-            "per_call": {"median_ms": r["median_ms"], "iqr_ms": r["iqr_ms"], "reps": reps},
+    tf = fl["total"] / (r["median_ms"] * 1e-3) / 1e12
+    return {"workload": name, "median_ms": r["median_ms"], "iqr_ms": r["iqr_ms"],
+            "timing": f"events around each of {reps} reps after {warm} warm-ups, median and IQR",
+            "back_to_back": {"median_ms": st["median_ms"], "iqr_ms": st["iqr_ms"],
+                             "steps_per_batch": st["steps_per_batch"], "batches": st["batches"]},
             "value": round(tf, 2), "unit": "TFLOP/s", "flops_per_step": fl["total"],
             "pct_sustained_peak": round(tf / peaks[0], 4), "pct_burst_peak": round(tf / peaks[1], 4),
             "launches_per_step": launches}
@@ -698,9 +697,7 @@ def run_single(args):
     for key, hq, hkv, d, win, n_layers in (("local_d256", 32, 16, 256, 1024, 50),
                                            ("global_d512", 32, 4, 512, 0, 10)):
         q5, k5, v5, _ = make_qkv((1, s5, hq, d), (1, s5, hkv, d), 6000, dev)
-        fwd5 = lambda: ops.attn_fwd(q5, k5, v5, window=win)  # noqa: E731
-        r = ruler(fwd5, dev, warm=3, reps=10)
-        r = steady(fwd5, dev, r["median_ms"])  # layers run back to back in a prefill
+        r = ruler(lambda: ops.attn_fwd(q5, k5, v5, window=win), dev, warm=3, reps=10)
         f5 = flops(text_pairs(s5, win), hq, d)["fwd"]
         pre[key] = {"layers": n_layers, "median_ms": r["median_ms"],
                     "tflops": round(f5 / (r["median_ms"] * 1e-3) / 1e12, 1)}
