@@ -331,13 +331,16 @@ struct ScoreCfg {
   // overlaps the next tile's math); the forward pass 3 + 1 K stages, the two
   // staging slots and a slot for its row-statistics exchange; the dS pass
   // 3 + 2 V stages and 2 P stages.
-  static constexpr int kExtraStages = kTS ? (MODE == kScoreFwd ? 1 : 2) : 0;
+  static constexpr int kExtraStages = kTS ? (MODE == kScoreFwd ? 1 : 2) : (D == 256 && MODE == kScorePdS ? 2 : 0);
   static constexpr int kRingStages = kStages + kExtraStages;
   static constexpr int kPStages = 2;
-  // d256 S-and-dP pass: Q moves into TMEM (S = Q K^T as a TS MMA; dP = dO V^T
-  // stays SS with dO in shared memory), which frees Q's 64 KB of shared
-  // memory for one P and one dS staging slot.  TMEM: S double-buffered at
-  // b*128, Q at 256, dP single-buffered at 384.
+  // d256 S-and-dP pass: Q and dO move into TMEM, so S = Q K^T and dP = dO V^T
+  // are both TS MMAs that read only K or V from shared memory.  Q's 64 KB of
+  // shared memory then hold one P and one dS staging slot, dO's 64 KB two more
+  // K/V ring stages (five in all: the stream of 128 KB of K and V per key tile
+  // is bound by the bytes in flight per SM).  TMEM: S at 0 and dP at 128, each
+  // single-buffered (the math warps read both into registers first, then the
+  // next tile's MMAs run under their arithmetic), Q at 256, dO at 384.
   static constexpr bool kQT = D == 256 && MODE == kScorePdS;
   // P tiles leave through a shared-memory staging slot and one bulk store
   // (a warp's direct 16-B row-chunk stores would touch 32 lines each).
@@ -364,7 +367,6 @@ struct ScoreMisc {
   uint64_t drain;
   uint64_t stg_free[2];   // staging slot j & 1 read by tile j's bulk store
   uint64_t stg_ready[2];  // every math thread wrote tile j's chunks (slot parity j & 1)
-  uint64_t dp_free;       // single dP buffer read by every math thread (d256 PdS)
   uint32_t tmem_base;
   int abort;
 };
@@ -437,7 +439,6 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     mbar_init(&misc->stg_free[1], 1);
     mbar_init(&misc->stg_ready[0], kScoreMathThreads);
     mbar_init(&misc->stg_ready[1], kScoreMathThreads);
-    mbar_init(&misc->dp_free, kScoreMathThreads);
     misc->abort = 0;
     fence_mbar_init();
     if (cap_ok && n_kt > 0) {
@@ -476,17 +477,19 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
   // TMEM: PdS mode: buffer b holds S at b*256 and dP at b*256+128.  TS
   // variant: buffer b at b*128, the resident A operand (bf16 pairs) at 256.
   auto s_col = [](int b) {
-    return static_cast<uint32_t>(Cfg::kTS || Cfg::kQT ? b * 128 : b * 256);
+    return static_cast<uint32_t>(Cfg::kTS ? b * 128 : (Cfg::kQT ? 0 : b * 256));
   };
   auto dp_col = [](int b) {
-    return static_cast<uint32_t>(Cfg::kTS ? b * 128 : (Cfg::kQT ? 384 : b * 256 + 128));
+    return static_cast<uint32_t>(Cfg::kTS ? b * 128 : (Cfg::kQT ? 128 : b * 256 + 128));
   };
   uint8_t* res_area = Cfg::kS ? q_s : do_s;
   // ring stage s: the first kStages in the ring area, the rest in the
-  // resident area (usable once the resident operand has moved to TMEM)
+  // resident area (usable once the resident operand has moved to TMEM; the
+  // d256 S-and-dP pass uses dO's area, Q's holds its staging slots)
+  uint8_t* xtra_area = Cfg::kQT ? do_s : res_area;
   auto stage_ptr = [&](uint32_t st) -> uint8_t* {
     return st < static_cast<uint32_t>(Cfg::kStages) ? ring + st * 32768
-                                                     : res_area + (st - Cfg::kStages) * 32768;
+                                                     : xtra_area + (st - Cfg::kStages) * 32768;
   };
   // TS dS pass: P ring after the extra V stages in the resident area; P and
   // forward passes: the staging slot there
@@ -498,7 +501,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     if (work > 0) {
       uint32_t it = 0;
       bool ok = true;
-      bool res_free = !Cfg::kTS;
+      bool res_free = !(Cfg::kTS || Cfg::kQT);
       for (int j = 0; j < work && ok; ++j) {
         const int krow = si.k_base + qtile_key(p, g, rg, j) * kTileN;
         for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
@@ -588,8 +591,13 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           ok = mbar_wait(&misc->res_full[qp], 0, ab, kDevTimeoutTma);
       for (int j = 0; j < work && ok; ++j) {
         const int b = j & 1;
-        if (j >= 2 &&
+        // S (and dP) buffers: double-buffered TMEM columns wait for tile j-2's
+        // reads; the single-buffered d256 S-and-dP pair for tile j-1's
+        if (!Cfg::kQT && j >= 2 &&
             !(ok = mbar_wait(&misc->buf_free[b], ((j - 2) >> 1) & 1, ab, kDevTimeoutPeer)))
+          break;
+        if (Cfg::kQT && j >= 1 &&
+            !(ok = mbar_wait(&misc->buf_free[b ^ 1], ((j - 1) >> 1) & 1, ab, kDevTimeoutPeer)))
           break;
         tc_fence_after();
         for (int c = 0; c < Cfg::kChunksPerTile && ok; ++c) {
@@ -597,7 +605,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           ++it;
           if (!(ok = mbar_wait(&misc->ring_full[st], ph, ab, kDevTimeoutTma))) break;
           const bool is_k = Cfg::kS && c < D / 128;
-          if ((Cfg::kTS || (Cfg::kQT && is_k)) && j == 0) {
+          if ((Cfg::kTS || Cfg::kQT) && j == 0) {
             // K elements [128 cc, +128) of the TMEM operand: quarters
             // 2cc / kBpp .. (2cc + 1) / kBpp
             constexpr int kBpp = (D / 64) / kResParts;
@@ -606,10 +614,6 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
               ok = mbar_wait(&misc->a_ready[qp], 0, ab, kDevTimeoutPeer);
             if (!ok) break;
           }
-          // single dP buffer: tile j's dP waits until every math thread read tile j-1's
-          if (Cfg::kQT && c == D / 128 && j > 0 &&
-              !(ok = mbar_wait(&misc->dp_free, (j - 1) & 1, ab, kDevTimeoutPeer)))
-            break;
           tc_fence_after();
           const int cc = is_k ? c : c - (Cfg::kS ? D / 128 : 0);
           const uint32_t abase = is_k ? qb : db;
@@ -619,8 +623,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
           for (int kk = 0; kk < 8; ++kk) {
             const int gk = cc * 8 + kk;
             const uint64_t bdesc = sdesc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-            if (Cfg::kTS || (Cfg::kQT && is_k))
-              umma_ts_w(tmem + dcol, tmem + 256 + gk * 8, bdesc, kId, (cc | kk) != 0);
+            if (Cfg::kTS || Cfg::kQT)  // A from TMEM: Q (or the d256 pass's dO at 384)
+              umma_ts_w(tmem + dcol, tmem + ((Cfg::kQT && !is_k) ? 384 : 256) + gk * 8, bdesc,
+                        kId, (cc | kk) != 0);
             else
               umma_ss_w(tmem + dcol,
                         sdesc_sw128(abase + (gk >> 2) * 16384 + (gk & 3) * 32, 16, 1024), bdesc,
@@ -680,6 +685,26 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             v[4 * ch + 3] = w.w;
           }
           tmem_st32(lane_base + 256 + dblk * 32, v);
+        }
+        if (Cfg::kQT) {  // dO too (it lands with the last quarter), to column 384
+          if (ok && grp != kResParts - 1)
+            ok = mbar_wait(&misc->res_full[kResParts - 1], 0, ab, kDevTimeoutTma);
+          ok = __all_sync(0xffffffffu, ok);
+#pragma unroll 1
+          for (int blk = 0; blk < kBlkPerGroup && ok; ++blk) {
+            uint32_t v[32];
+            const int dblk = grp * kBlkPerGroup + blk;
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+              const uint4 w = *reinterpret_cast<const uint4*>(do_s + dblk * 16384 + r * 128 +
+                                                              ((ch ^ (r & 7)) << 4));
+              v[4 * ch + 0] = w.x;
+              v[4 * ch + 1] = w.y;
+              v[4 * ch + 2] = w.z;
+              v[4 * ch + 3] = w.w;
+            }
+            tmem_st32(lane_base + 384 + dblk * 32, v);
+          }
         }
         tmem_wait_st();
       }
@@ -851,7 +876,6 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
         if (c == c_begin + kChunksPerWarp - 1) {  // this warp's TMEM values are in registers
           tc_fence_before();
           mbar_arrive(&misc->buf_free[b]);
-          if (Cfg::kQT) mbar_arrive(&misc->dp_free);
         }
         float pv[32];
         if (MODE == kScoreDs) {
