@@ -987,7 +987,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
 // sizes (the k-steps of a key tile), so interleaving the two products doubles
 // the number of CTAs of each size and evens out the end of the launch (the
 // largest CTA is a smaller share of each SM's work).
-enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2, kGemmO = 3, kGemmDvDk = 4 };
+enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2, kGemmO = 3, kGemmDvDk = 4,
+                       kGemmDq2 = 5 };
 
 // dQ CTAs produce all D output columns (A loaded once); dV / dK CTAs produce
 // one 256-column half each, which doubles the KV-major grid for load balance.
@@ -1001,13 +1002,18 @@ enum GemmWhich : int { kGemmDv = 0, kGemmDk = 1, kGemmDq = 2, kGemmO = 3, kGemmD
 // arrive on the leader's o_ready.
 template <int D, int WHICH, bool PAIR = false>
 struct GemmCfg {
-  static constexpr bool kQMajor = WHICH == kGemmDq || WHICH == kGemmO;  // dQ and the forward O
-  static constexpr int kNB = kQMajor ? D : 256;     // output columns per CTA
+  // d256 dQ of the two query heads of a KV group in one CTA: both dS tiles of
+  // a key tile are multiplied by one copy of its K rows (a third less operand
+  // traffic than one head per CTA), into two 256-column accumulators
+  static constexpr bool kDuo = WHICH == kGemmDq2;
+  static constexpr bool kQMajor = WHICH == kGemmDq || WHICH == kGemmO || kDuo;  // dQ, forward O
+  static constexpr int kNB = kQMajor ? D : 256;     // output columns per CTA (and head)
   static constexpr int kHalves = D / kNB;
-  static constexpr int kABytes = 16384;             // 128 rows x 64 deep
+  static constexpr int kABytes = 16384 * (kDuo ? 2 : 1);  // 128 rows x 64 deep (per head)
   static constexpr int kBBytes = 64 * (PAIR ? kNB / 2 : kNB) * 2;  // 64 deep x (this CTA's) columns
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = kStageBytes > 64 * 1024 ? 2 : 4;
+  static constexpr int kStages = kDuo ? 3 : (kStageBytes > 64 * 1024 ? 2 : 4);
+  static_assert(!kDuo || D == 256, "two heads per CTA fill TMEM at d256");
 };
 
 constexpr int kQListCap = 2048;  // query tiles of one sequence listed in shared memory
@@ -1068,13 +1074,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int seq, tile, head;  // tile: key tile (dV/dK) or query tile (dQ) within the sequence
   int qg = 0;           // dQ: global query-tile index
   int half = 0;         // dV/dK: which 256-column half
-  int which = WHICH;    // kGemmDvDk: this CTA's product (dV or dK)
+  int which = WHICH == kGemmDq2 ? kGemmDq : WHICH;  // kGemmDvDk: this CTA's product (dV or dK)
   if (Cfg::kQMajor) {
     const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
     // grid (band heads, band query tiles), head fastest: longest-first over the band
     qg = band_qtile(p, static_cast<int>(blockIdx.y));
     if (qg < 0 || qg >= n) return;
-    head = p.band_h0 * G + static_cast<int>(blockIdx.x);
+    head = p.band_h0 * G + (Cfg::kDuo ? 2 : 1) * static_cast<int>(blockIdx.x);  // (and head + 1)
     seq = p.ranges[qg].w;
     tile = packed ? p.q_tiles[qg].y : qg % p.n_qt_fixed;
   } else {
@@ -1274,6 +1280,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               mbar_expect_tx(&misc->full[st], Cfg::kStageBytes);
               if (Cfg::kQMajor) {
                 bulk_load(dst, t + h * 16384, 16384, &misc->full[st]);
+                if (Cfg::kDuo)  // the next head's dS tile of the same key tile
+                  bulk_load(dst + 16384, t + p.head_cap_tiles * kTileBytes + h * 16384, 16384,
+                            &misc->full[st]);
               } else {
                 bulk_load(dst, t + h * 8192, 8192, &misc->full[st]);
                 bulk_load(dst + 8192, t + 16384 + h * 8192, 8192, &misc->full[st]);
@@ -1383,6 +1392,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               umma_ss_w(tmem + nh * 256, adesc,
                         sdesc_sw128(bb + nh * 32768 + kk * 2048, 8192, 1024), kId,
                         !(first && kk == 0));
+            if (Cfg::kDuo)  // second head: its dS half against the same K rows
+              umma_ss_w(tmem + 256, sdesc_sw128(a + 16384 + kk * 32, 16, 1024),
+                        sdesc_sw128(bb + kk * 2048, 8192, 1024), kId, !(first && kk == 0));
           }
           umma_commit_w(&misc->empty[st]);
         }
@@ -1448,7 +1460,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     const bool have = ok && n_steps > 0;
-    const uint32_t lane_base = lane_base0;
+    const uint32_t lane_base = lane_base0;  // the first (or only) accumulator
     const int row = tile * 128 + er;
     constexpr int kHalfChunks = Cfg::kNB / 64;  // 32-column chunks per epilogue warp
     const int c_lo = ehalf * kHalfChunks;
@@ -1528,6 +1540,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     } else {
+    for (int u = 0; u < (Cfg::kDuo ? 2 : 1); ++u) {  // kDuo: both heads' accumulators
+    const int hu = head + u;
+    const uint32_t lane_base = lane_base0 + u * 256;
+    uint8_t* const stg_out = smem + u * 65536;
     float out_scale = 1.f;
     __nv_bfloat16* dst;
     if (WHICH == kGemmO) {
@@ -1537,7 +1553,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             static_cast<int64_t>(si.q_base + row) * p.o_stride[1] + static_cast<int64_t>(head) * p.o_stride[2];
     } else if (which == kGemmDq)
       dst = p.dq + static_cast<int64_t>(si.b_coord) * p.dq_stride[0] +
-            static_cast<int64_t>(si.q_base + row) * p.dq_stride[1] + static_cast<int64_t>(head) * p.dq_stride[2];
+            static_cast<int64_t>(si.q_base + row) * p.dq_stride[1] + static_cast<int64_t>(hu) * p.dq_stride[2];
     else if (which == kGemmDv)
       dst = p.dv + static_cast<int64_t>(si.b_coord) * p.dv_stride[0] +
             static_cast<int64_t>(si.k_base + row) * p.dv_stride[1] + static_cast<int64_t>(head) * p.dv_stride[2];
@@ -1576,7 +1592,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_wait_ld();
         reg_fence32(r[0]);
         reg_fence32(r[1]);
-        uint8_t* rowp = smem + (c >> 1) * 16384 + er * 128;
+        uint8_t* rowp = stg_out + (c >> 1) * 16384 + er * 128;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
@@ -1593,7 +1609,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_proxy_async_smem();
         asm volatile("bar.sync %0, %1;" ::"r"(2 + ehalf), "n"(kGemmEpiThreads / 2) : "memory");
         if (issuer) {
-          tma_store_4d(mo, smem + (c >> 1) * 16384, half * 256 + (c >> 1) * 64, head, tok0,
+          tma_store_4d(mo, stg_out + (c >> 1) * 16384, half * 256 + (c >> 1) * 64, hu, tok0,
                        si.b_coord);
           asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
@@ -1628,6 +1644,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
+    }  // heads
     }  // bf16 outputs
   }
 
@@ -1736,6 +1753,7 @@ static int launch_gemm_impl(const CUtensorMap& tb, const CUtensorMap& tout, cons
     grid_x *= grid_y * Cfg::kHalves * (WHICH == kGemmDvDk ? 2 : 1);
     grid_y = 1;
   }
+  if (Cfg::kDuo) grid_y /= 2;  // head pairs
   const int smem = Cfg::kStages * Cfg::kStageBytes + sizeof(GemmMisc);
   auto kernel = bwd_tile_gemm_kernel<D, WHICH, PAIR>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1776,6 +1794,8 @@ int launch_bwd_tile_gemm(int d, int which, const CUtensorMap& tb, const CUtensor
       return launch_gemm_impl<256, kGemmDv>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
     if (which == kGemmDk)
       return launch_gemm_impl<256, kGemmDk>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
+    if (p.group % 2 == 0 && p.acc_q == 0 && grid_y % 2 == 0)  // head pairs of a KV group
+      return launch_gemm_impl<256, kGemmDq2>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
     return launch_gemm_impl<256, kGemmDq>(tb, tout, a, tb, tout, p, grid_x, grid_y, stream);
   }
   if (which == kGemmDv)
