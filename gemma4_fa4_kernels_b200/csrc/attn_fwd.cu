@@ -468,10 +468,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int i = 0; i < 16; ++i)
           pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l,
                               __uint_as_float(r[2 * i + 1]) * inv_l);
-        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        st_global_64B(orow + c * 32, pk);
       }
     }
     if (row_valid && slab == 0 && half == 0) {
@@ -982,10 +979,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           for (int i = 0; i < 16; ++i)
             pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l,
                                 __uint_as_float(r[2 * i + 1]) * inv_l);
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          st_global_64B(orow + c * 32, pk);
         }
       }
       tc_fence_before();

@@ -264,6 +264,25 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
 
 // Bulk copy shared -> global (both addresses 16-B aligned, size a multiple of
 // 16 bytes), tracked per issuing thread as one bulk async-group.
+// 64 bytes of one row to global memory: two 32-B stores when the address is
+// 32-B aligned (whole sectors, half the store instructions of a warp writing
+// 32 rows), else four 16-B stores.
+__device__ __forceinline__ void st_global_64B(void* dst, const uint32_t (&w)[16]) {
+  if ((reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(w[0]),
+                 "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+    asm volatile("st.global.v8.b32 [%0+32], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst),
+                 "r"(w[8]), "r"(w[9]), "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]),
+                 "r"(w[15])
+                 : "memory");
+  } else {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  }
+}
+
 __device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
                    reinterpret_cast<uint64_t>(gdst)),
