@@ -91,7 +91,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   const int tid = threadIdx.x;
   const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);  // provably warp-uniform
-  const int lane = tid & 31;
   // grid (heads, work items, slabs): the head index varies fastest in launch
   // order, so the longest causal rows of every head are dispatched first
   const int head = blockIdx.x;
@@ -558,10 +557,17 @@ __device__ __forceinline__ int fwd_ktile(const FwdItem& it, int j) {
   return it.klist ? (it.klist[j] & kTileEntryIndex) : it.kt_lo + j;
 }
 
+// Four more warps write each item's O: the softmax warps hand over the row
+// normalisers and go on with the next item while O leaves TMEM (the next
+// item's first P V, which overwrites O, waits for them through o_free).
+constexpr int kFwdPThreads = kFwdThreads + 128;  // warps 10-13
+
 struct FwdPMisc {
   uint64_t q_full;
   uint64_t q_free;
   uint64_t o_free;
+  uint64_t epi_full;          // the softmax warps wrote an item's 1/l (256 arrivals)
+  uint64_t epi_empty;         // the epilogue warps read it (128 arrivals)
   uint64_t ring_full[8];
   uint64_t ring_empty[8];
   uint64_t s_full[2];
@@ -571,10 +577,11 @@ struct FwdPMisc {
   uint32_t tmem_base;
   int abort;
   float xbuf[2][2 * kTileM];  // as FwdMisc::xbuf, indexed by the global tile parity
+  float inv_l[kTileM];        // the current item's 1 / rowsum, for the epilogue warps
 };
 static_assert(sizeof(FwdPMisc) <= 3072, "persistent forward misc block exceeds its budget");
 
-__global__ void __launch_bounds__(kFwdThreads, 1)
+__global__ void __launch_bounds__(kFwdPThreads, 1)
     attn_fwd_persistent_kernel(const __grid_constant__ CUtensorMap tmQ,
                                const __grid_constant__ CUtensorMap tmK,
                                const __grid_constant__ CUtensorMap tmV, const FwdParams p,
@@ -596,7 +603,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (tid == 0) {
     mbar_init(&misc->q_full, 1);
     mbar_init(&misc->q_free, 1);
-    mbar_init(&misc->o_free, kFwdSoftThreads);
+    mbar_init(&misc->o_free, 128);  // the epilogue warps
+    mbar_init(&misc->epi_full, kFwdSoftThreads);
+    mbar_init(&misc->epi_empty, 128);
     for (int s2 = 0; s2 < Cfg::kStages; ++s2) {
       mbar_init(&misc->ring_full[s2], 1);
       mbar_init(&misc->ring_empty[s2], 1);
@@ -768,8 +777,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     umma_commit_w(&misc->drain);
     mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
     __syncwarp();
-  } else {
-    // ======================= softmax + epilogue (warps 0-7) =======================
+  } else if (warp < kFwdSoftWarps) {
+    // ======================= softmax (warps 0-7) =======================
     // Control flow stays uniform over the 256 softmax threads: every item and
     // tile reaches named barrier 1 the same number of times whatever `ok` says.
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
@@ -922,10 +931,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         l_half = l_half * alpha + rowsum;
         tmem_wait_st();
-        if (j > 0) {
+        if (j > 0 || I > 0) {
+          // o_done phases are waited in order: P V of this item's previous tile
+          // (or, at an item's first tile, of the previous item's last tile)
           ok = mbar_wait(&misc->o_done, (t - 1) & 1, ab, kDevTimeoutMma);
           ok = __all_sync(0xffffffffu, ok);
-          if (ok && __any_sync(0xffffffffu, rescale)) {
+          if (j > 0 && ok && __any_sync(0xffffffffu, rescale)) {
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < 4; c += 2) {
@@ -950,7 +961,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_before();
         if (ok) mbar_arrive(&misc->p_full[t & 1]);
       }
-      // ---- epilogue: O / l -> bf16, LSE; then O is free for the next item ----
+      // ---- item end: LSE, and 1/l for the epilogue warps, which write O ----
       float* ls = misc->xbuf[(T + n) & 1];
       ls[half * kTileM + row] = l_half;
       asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
@@ -958,34 +969,72 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // every thread has read the sums before the next item's first tile reuses
       // this buffer for its row maxima
       asm volatile("bar.sync 1, %0;" ::"n"(kFwdSoftThreads) : "memory");
+      // the epilogue warps have read the previous item's 1/l
+      if (I > 0 && ok) ok = mbar_wait(&misc->epi_empty, (I - 1) & 1, ab, kDevTimeoutPeer);
+      ok = __all_sync(0xffffffffu, ok);
+      if (half == 0) misc->inv_l[row] = (l_run > 0.f) ? 1.f / l_run : 0.f;
+      mbar_arrive(&misc->epi_full);
+      if (row_valid && half == 0)
+        *lse_row = (l_run > 0.f) ? (m_run + __log2f(l_run)) * kLn2 : -INFINITY;
+      T += n;
+      ++I;
+    }
+  } else {
+    // ======================= O epilogue (warps 10-13) =======================
+    // Warp w reads TMEM lane quarter w % 4: one row per thread, all 256
+    // columns, normalised by the softmax warps' 1/l and stored to O; then O is
+    // free for the next item's first P V.
+    const int q4 = warp & 3;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    const int row = q4 * 32 + (tid & 31);
+    bool ok = true;
+    int64_t T = 0;
+    int I = 0;
+    for (int64_t i = 0;; ++i) {
+      const FwdItem wi = fwd_item(p, fwd_item_index(i), num_q_heads);
+      if (!wi.valid) break;
+      const int n = wi.n_kt;
+      if (n == 0) continue;  // the softmax warps wrote that item's zeros
+      const SeqInfo& si = wi.si;
+      const int q_idx = wi.qt * kTileM + row;
+      const bool row_valid = q_idx < si.len_q;
+      __nv_bfloat16* orow = p.o + static_cast<int64_t>(si.b_coord) * p.o_stride[0] +
+                            static_cast<int64_t>(si.q_base + q_idx) * p.o_stride[1] +
+                            static_cast<int64_t>(wi.head) * p.o_stride[2];
+      if (ok) ok = mbar_wait(&misc->epi_full, I & 1, ab, kDevTimeoutPeer);
+      ok = __all_sync(0xffffffffu, ok);
+      const float inv_l = misc->inv_l[row];
+      mbar_arrive(&misc->epi_empty);
       if (ok) ok = mbar_wait(&misc->o_done, (T + n - 1) & 1, ab, kDevTimeoutMma);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
-      const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
+      for (int c = 0; c < 8; c += 2) {
+        uint32_t r[2][32];
         if (ok) {
-          tmem_ld32(lane_base + 256 + half * 128 + c * 32, r);
+          tmem_ld32(lane_base + 256 + c * 32, r[0]);
+          tmem_ld32(lane_base + 256 + c * 32 + 32, r[1]);
           tmem_wait_ld();
-          reg_fence32(r);
+          reg_fence32(r[0]);
+          reg_fence32(r[1]);
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = 0u;
+          for (int i2 = 0; i2 < 32; ++i2) r[0][i2] = r[1][i2] = 0u;
         }
         if (row_valid) {
-          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l,
-                                __uint_as_float(r[2 * i + 1]) * inv_l);
-          st_global_64B(orow + c * 32, pk);
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i2 = 0; i2 < 16; ++i2)
+              pk[i2] = pack_bf16x2(__uint_as_float(r[hh][2 * i2]) * inv_l,
+                                   __uint_as_float(r[hh][2 * i2 + 1]) * inv_l);
+            st_global_64B(orow + (c + hh) * 32, pk);
+          }
         }
       }
       tc_fence_before();
       mbar_arrive(&misc->o_free);
-      if (row_valid && half == 0)
-        *lse_row = (l_run > 0.f) ? (m_run + __log2f(l_run)) * kLn2 : -INFINITY;
       T += n;
       ++I;
     }
@@ -1005,7 +1054,7 @@ int launch_fwd_persistent(const CUtensorMap& tq, const CUtensorMap& tk, const CU
   cudaError_t e = cudaFuncSetAttribute(attn_fwd_persistent_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
-  e = launch_chained(attn_fwd_persistent_kernel, dim3(ctas), dim3(kFwdThreads), Cfg::kSmemBytes,
+  e = launch_chained(attn_fwd_persistent_kernel, dim3(ctas), dim3(kFwdPThreads), Cfg::kSmemBytes,
                      stream, tq, tk, tv, p, num_q_heads);
   if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
