@@ -572,7 +572,7 @@ struct FwdPMisc {
   uint64_t ring_empty[8];
   uint64_t s_full[2];
   uint64_t p_full[2];
-  uint64_t o_done;
+  uint64_t o_done[2];         // P V of tile t complete (o_done[t & 1], phase t >> 1)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -614,7 +614,8 @@ __global__ void __launch_bounds__(kFwdPThreads, 1)
       mbar_init(&misc->s_full[b], 1);
       mbar_init(&misc->p_full[b], kFwdSoftThreads);
     }
-    mbar_init(&misc->o_done, 1);
+    mbar_init(&misc->o_done[0], 1);
+    mbar_init(&misc->o_done[1], 1);
     mbar_init(&misc->drain, 1);
     misc->abort = 0;
     fence_mbar_init();
@@ -645,11 +646,47 @@ __global__ void __launch_bounds__(kFwdPThreads, 1)
       const uint32_t ph = (it / Cfg::kStages) & 1;
       return mbar_wait(&misc->ring_empty[stage], ph ^ 1, ab, kDevTimeoutMma);
     };
+    // K / V chunks in the MMA warp's order: K of tile t + 1 before V of tile
+    // t, across items too (the next item's first K goes before the current
+    // item's last V, which is held back until then)
+    auto load_k = [&](const FwdItem& w, int kt) {
+      const int kv_head = w.head / p.group;
+      for (int c = 0; c < Cfg::kKChunks && ok; ++c) {
+        uint32_t st;
+        if (!(ok = acquire(st))) break;
+        if (elect_one()) {
+          mbar_expect_tx(&misc->ring_full[st], Cfg::kStageBytes);
+          uint8_t* dst = ring + st * Cfg::kStageBytes;
+          for (int h = 0; h < 2; ++h)
+            tma_load_4d(dst + h * 16384, &tmK, &misc->ring_full[st], (2 * c + h) * 64, kv_head,
+                        w.si.k_base + kt * kTileN, w.si.b_coord);
+        }
+        __syncwarp();
+        ++it;
+      }
+    };
+    auto load_v = [&](const FwdItem& w, int kt) {
+      const int kv_head = w.head / p.group;
+      for (int c = 0; c < Cfg::kVChunks && ok; ++c) {
+        uint32_t st;
+        if (!(ok = acquire(st))) break;
+        if (elect_one()) {
+          mbar_expect_tx(&misc->ring_full[st], Cfg::kStageBytes);
+          uint8_t* dst = ring + st * Cfg::kStageBytes;
+          for (int blk = 0; blk < 4; ++blk)
+            tma_load_4d(dst + blk * 8192, &tmV, &misc->ring_full[st], blk * 64, kv_head,
+                        w.si.k_base + kt * kTileN + c * 64, w.si.b_coord);
+        }
+        __syncwarp();
+        ++it;
+      }
+    };
+    FwdItem held;  // the item whose last V tile is held back
+    int held_kt = -1;
     for (int64_t i = 0; ok; ++i) {
       const FwdItem wi = fwd_item(p, fwd_item_index(i), num_q_heads);
       if (!wi.valid) break;
       if (wi.n_kt == 0) continue;
-      const int kv_head = wi.head / p.group;
       // Q of this item once the previous item's S MMAs have read the last one
       if (I > 0 && !(ok = mbar_wait(&misc->q_free, (I - 1) & 1, ab, kDevTimeoutMma))) break;
       if (elect_one()) {
@@ -659,43 +696,20 @@ __global__ void __launch_bounds__(kFwdPThreads, 1)
                       wi.si.q_base + wi.qt * kTileM, wi.si.b_coord);
       }
       __syncwarp();
-      auto load_k = [&](int kt) {
-        for (int c = 0; c < Cfg::kKChunks && ok; ++c) {
-          uint32_t st;
-          if (!(ok = acquire(st))) break;
-          if (elect_one()) {
-            mbar_expect_tx(&misc->ring_full[st], Cfg::kStageBytes);
-            uint8_t* dst = ring + st * Cfg::kStageBytes;
-            for (int h = 0; h < 2; ++h)
-              tma_load_4d(dst + h * 16384, &tmK, &misc->ring_full[st], (2 * c + h) * 64, kv_head,
-                          wi.si.k_base + kt * kTileN, wi.si.b_coord);
-          }
-          __syncwarp();
-          ++it;
-        }
-      };
-      auto load_v = [&](int kt) {
-        for (int c = 0; c < Cfg::kVChunks && ok; ++c) {
-          uint32_t st;
-          if (!(ok = acquire(st))) break;
-          if (elect_one()) {
-            mbar_expect_tx(&misc->ring_full[st], Cfg::kStageBytes);
-            uint8_t* dst = ring + st * Cfg::kStageBytes;
-            for (int blk = 0; blk < 4; ++blk)
-              tma_load_4d(dst + blk * 8192, &tmV, &misc->ring_full[st], blk * 64, kv_head,
-                          wi.si.k_base + kt * kTileN + c * 64, wi.si.b_coord);
-          }
-          __syncwarp();
-          ++it;
-        }
-      };
-      load_k(fwd_ktile(wi, 0));
+      load_k(wi, fwd_ktile(wi, 0));
+      if (held_kt >= 0) load_v(held, held_kt);
       for (int j = 0; j < wi.n_kt && ok; ++j) {
-        if (j + 1 < wi.n_kt) load_k(fwd_ktile(wi, j + 1));
-        load_v(fwd_ktile(wi, j));
+        if (j + 1 < wi.n_kt) {
+          load_k(wi, fwd_ktile(wi, j + 1));
+          load_v(wi, fwd_ktile(wi, j));
+        } else {
+          held = wi;
+          held_kt = fwd_ktile(wi, j);
+        }
       }
       ++I;
     }
+    if (held_kt >= 0 && ok) load_v(held, held_kt);
     __syncwarp();
   } else if (warp == kFwdMmaWarp) {
     // ============================ MMA issuer ============================
@@ -746,23 +760,42 @@ __global__ void __launch_bounds__(kFwdPThreads, 1)
         umma_commit_w(&misc->ring_empty[st]);
         ++it;
       }
-      umma_commit_w(&misc->o_done);
+      umma_commit_w(&misc->o_done[t & 1]);
     };
-    for (int64_t i = 0; ok; ++i) {
-      const FwdItem wi = fwd_item(p, fwd_item_index(i), num_q_heads);
-      if (!wi.valid) break;
-      const int n = wi.n_kt;
-      if (n == 0) continue;
-      if (!(ok = mbar_wait(&misc->q_full, I & 1, ab, kDevTimeoutTma))) break;
-      tc_fence_after();
-      // S of tile j; once the item's last S is issued, Q may be replaced
-      auto item_s = [&](int j) {
-        issue_s(T + j);
-        if (j + 1 == n) umma_commit_w(&misc->q_free);
-      };
-      item_s(0);
+    // Items with key tiles, in order; the next item's first S is issued before
+    // the current item's last P V (it waits only for the next Q), so the
+    // softmax warps find it ready when they finish an item.
+    int64_t cursor = 0;
+    auto next_item = [&]() {
+      for (;; ++cursor) {
+        const FwdItem w = fwd_item(p, fwd_item_index(cursor), num_q_heads);
+        if (!w.valid || w.n_kt > 0) {
+          ++cursor;
+          return w;
+        }
+      }
+    };
+    FwdItem cur = next_item();
+    if (cur.valid) {
+      if ((ok = mbar_wait(&misc->q_full, 0, ab, kDevTimeoutTma))) {
+        tc_fence_after();
+        issue_s(0);
+        if (cur.n_kt == 1) umma_commit_w(&misc->q_free);
+      }
+    }
+    while (cur.valid && ok) {
+      const int n = cur.n_kt;
+      const FwdItem nxt = next_item();
       for (int j = 0; j < n && ok; ++j) {
-        if (j + 1 < n) item_s(j + 1);
+        if (j + 1 < n) {
+          issue_s(T + j + 1);
+          if (j + 2 == n) umma_commit_w(&misc->q_free);  // the item's last S: Q may be replaced
+        } else if (nxt.valid) {
+          if (!(ok = mbar_wait(&misc->q_full, (I + 1) & 1, ab, kDevTimeoutTma))) break;
+          tc_fence_after();
+          issue_s(T + n);
+          if (nxt.n_kt == 1) umma_commit_w(&misc->q_free);
+        }
         const int64_t t = T + j;
         if (!(ok = mbar_wait(&misc->p_full[t & 1], (t >> 1) & 1, ab, kDevTimeoutPeer))) break;
         if (j == 0 && I > 0 &&
@@ -773,6 +806,7 @@ __global__ void __launch_bounds__(kFwdPThreads, 1)
       }
       T += n;
       ++I;
+      cur = nxt;
     }
     umma_commit_w(&misc->drain);
     mbar_wait(&misc->drain, 0, ab, kDevTimeoutMma);
@@ -931,12 +965,13 @@ __global__ void __launch_bounds__(kFwdPThreads, 1)
         }
         l_half = l_half * alpha + rowsum;
         tmem_wait_st();
-        if (j > 0 || I > 0) {
-          // o_done phases are waited in order: P V of this item's previous tile
-          // (or, at an item's first tile, of the previous item's last tile)
-          ok = mbar_wait(&misc->o_done, (t - 1) & 1, ab, kDevTimeoutMma);
+        // a warp that rescales O waits for the previous tile's P V first; the
+        // others hand P over at once (P V of tile t - 1 reads the other buffer).
+        // With a barrier per tile parity, no wait is ever two phases behind.
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+          if (ok) ok = mbar_wait(&misc->o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, ab, kDevTimeoutMma);
           ok = __all_sync(0xffffffffu, ok);
-          if (j > 0 && ok && __any_sync(0xffffffffu, rescale)) {
+          if (ok) {
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < 4; c += 2) {
@@ -1005,7 +1040,8 @@ __global__ void __launch_bounds__(kFwdPThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       const float inv_l = misc->inv_l[row];
       mbar_arrive(&misc->epi_empty);
-      if (ok) ok = mbar_wait(&misc->o_done, (T + n - 1) & 1, ab, kDevTimeoutMma);
+      if (ok)
+        ok = mbar_wait(&misc->o_done[(T + n - 1) & 1], ((T + n - 1) >> 1) & 1, ab, kDevTimeoutMma);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
 #pragma unroll 1
