@@ -190,3 +190,31 @@ def test_causal_shift(sq, sk, shift):
     assert rel_l2(bshd_to_bhsd_np(out), ro) <= REL_L2_TOL
     assert lse_abs_err(lse.cpu().numpy(), rl) <= LSE_ABS_TOL
     _check_grads((dq, dk, dv), (rq, rk, rv), bshd_to_bhsd_np)
+
+
+
+def test_local_many_short_segments():
+    """Packed local d256 attention over many short segments (1 to 300 tokens):
+    the persistent forward walks hundreds of one-to-three-tile items, so the
+    look-ahead across items (the next item's Q and first S before the current
+    item's last P V) and the epilogue warps' hand-over run at almost every
+    tile.  Every segment is checked against the float64 oracle."""
+    rng = np.random.default_rng(12)
+    lens = [int(x) for x in rng.integers(1, 301, size=40)]
+    lens[3] = 128
+    lens[7] = 129
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device="cuda")
+    t, hq, hkv, d, w = int(sum(lens)), 4, 2, 256, 256
+    q, k, v, do = make_inputs((t, hq, d), (t, hkv, d), (t, hkv, d), seed=12)
+    kw = dict(cu_seqlens_q=cu, cu_seqlens_k=cu, max_seqlen_q=max(lens), max_seqlen_k=max(lens),
+              window=w)
+    out, lse = ops.attn_fwd(q, k, v, **kw)
+    dq, dk, dv = ops.attn_bwd(q, k, v, out, lse, do, **kw)
+    torch.cuda.synchronize()
+    cu_np = cu.cpu().numpy()
+    ro, rl, rq, rk, rv = oracle.attention_fwd_bwd_varlen(thd_np(q), thd_np(k), thd_np(v),
+                                                         thd_np(do), cu_np, cu_np,
+                                                         sliding_window=w)
+    assert rel_l2(thd_np(out), ro) <= REL_L2_TOL
+    assert lse_abs_err(lse.cpu().numpy(), rl) <= LSE_ABS_TOL
+    _check_grads((dq, dk, dv), (rq, rk, rv), thd_np)
