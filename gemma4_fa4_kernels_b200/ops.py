@@ -75,6 +75,32 @@ def _build_args(q, k, v, o, lse, *, window, vision_ids, document_ids, cu_seqlens
     return a
 
 
+# Argument blocks and workspace sizes depend only on shapes, strides, flags and
+# which optional tensors are present, not on the data: a call with a known
+# signature copies its cached block and writes the pointers.  (Marshalling the
+# block field by field costs more host time than a short kernel.)
+_SIG_CACHE: dict = {}
+_SIG_CACHE_MAX = 512
+
+
+def _sig(t: torch.Tensor | None):
+    return None if t is None else (tuple(t.shape), t.stride())
+
+
+def _cached_args(key, build, sizes):
+    """(argument block, workspace sizes) of a signature: a fresh copy of the
+    cached block (pointers still to be written) and the sizes `sizes(block)`
+    computed once."""
+    hit = _SIG_CACHE.get(key)
+    if hit is None:
+        a = build()
+        hit = (bytes(a), sizes(a))
+        if len(_SIG_CACHE) >= _SIG_CACHE_MAX:
+            _SIG_CACHE.clear()
+        _SIG_CACHE[key] = hit
+    return _lib.G4AttnArgs.from_buffer_copy(hit[0]), hit[1]
+
+
 def _workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
@@ -111,7 +137,15 @@ def _pick_workspace(full: int, small: int, force_small: bool, device,
         return _workspace(small, device)
 
 
+# The raw handle of the current stream without building a Stream object (a
+# microsecond per call on the host); the public API where torch lacks it.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device) -> int:
+    if _raw_stream is not None:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return _raw_stream(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -136,13 +170,24 @@ def attn_fwd(q, k, v, *, window=0, vision_ids=None, document_ids=None, cu_seqlen
     else:
         lse = torch.empty(q.shape[0], q.shape[2], q.shape[1], dtype=torch.float32, device=dev)
     vis, doc = _meta(vision_ids, dev), _meta(document_ids, dev)
-    a = _build_args(q, k, v, out, lse, window=window, vision_ids=vis, document_ids=doc,
-                    cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
-                    max_seqlen_q=max_seqlen_q, max_seqlen_k=max_seqlen_k)
-    a.causal_shift = int(causal_shift)
-    ws = _pick_workspace(lib.g4_attn_fwd_workspace_bytes(ctypes.byref(a)),
-                         lib.g4_attn_fwd_min_workspace_bytes(ctypes.byref(a)),
-                         algorithm in ("single", "recompute"), dev, workspace_bytes)
+
+    def build():
+        a = _build_args(q, k, v, out, lse, window=window, vision_ids=vis, document_ids=doc,
+                        cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
+                        max_seqlen_q=max_seqlen_q, max_seqlen_k=max_seqlen_k)
+        a.causal_shift = int(causal_shift)
+        return a
+
+    key = ("fwd", dev.index, q.dtype, _sig(q), _sig(k), _sig(v), _sig(out), _sig(lse),
+           int(window or 0), vis is not None, doc is not None, _sig(cu_seqlens_q),
+           _sig(cu_seqlens_k), max_seqlen_q, max_seqlen_k, int(causal_shift))
+    a, (full, small) = _cached_args(
+        key, build, lambda a: (lib.g4_attn_fwd_workspace_bytes(ctypes.byref(a)),
+                               lib.g4_attn_fwd_min_workspace_bytes(ctypes.byref(a))))
+    a.q, a.k, a.v, a.o, a.lse = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr()
+    a.vision_ids, a.document_ids = _ptr(vis), _ptr(doc)
+    a.cu_seqlens_q, a.cu_seqlens_k = _ptr(cu_seqlens_q), _ptr(cu_seqlens_k)
+    ws = _pick_workspace(full, small, algorithm in ("single", "recompute"), dev, workspace_bytes)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _raise_for(lib.g4_attn_fwd(ctypes.byref(a), _stream(dev)), "g4_attn_fwd")
     return out, lse
@@ -170,29 +215,43 @@ def attn_bwd(q, k, v, out, lse, dout, *, dlse=None, window=0, vision_ids=None,
     dk = torch.empty_like(k) if dk is None else dk
     dv = torch.empty_like(v) if dv is None else dv
     vis, doc = _meta(vision_ids, dev), _meta(document_ids, dev)
-    a = _build_args(q, k, v, out, lse, window=window, vision_ids=vis, document_ids=doc,
-                    cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
-                    max_seqlen_q=max_seqlen_q, max_seqlen_k=max_seqlen_k)
     if dout.stride(-1) != 1:
         dout = dout.contiguous()
-    a.dout = _ptr(dout)
     if dlse is not None:
         dlse = dlse.to(torch.float32).contiguous()
         if dlse.shape != lse.shape:
             raise ValueError("dlse must match the LSE shape")
-        a.dlse = _ptr(dlse)
-    a.do_stride = _strides3(dout, packed)
-    a.dq, a.dk, a.dv = _ptr(dq), _ptr(dk), _ptr(dv)
-    a.dq_stride = _strides3(dq, packed)
-    a.dk_stride = _strides3(dk, packed)
-    a.dv_stride = _strides3(dv, packed)
     if algorithm not in ("auto", "materialized", "recompute"):
         raise ValueError(f"unknown backward algorithm {algorithm!r}")
-    a.causal_shift = int(causal_shift)
-    a.grad_accumulate = 1 if accumulate else 0
-    ws = _pick_workspace(lib.g4_attn_bwd_workspace_bytes(ctypes.byref(a)),
-                         lib.g4_attn_bwd_min_workspace_bytes(ctypes.byref(a)),
-                         algorithm == "recompute", dev, workspace_bytes)
+
+    def build():
+        a = _build_args(q, k, v, out, lse, window=window, vision_ids=vis, document_ids=doc,
+                        cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
+                        max_seqlen_q=max_seqlen_q, max_seqlen_k=max_seqlen_k)
+        a.dout = _ptr(dout)
+        a.dlse = _ptr(dlse)
+        a.do_stride = _strides3(dout, packed)
+        a.dq, a.dk, a.dv = _ptr(dq), _ptr(dk), _ptr(dv)
+        a.dq_stride = _strides3(dq, packed)
+        a.dk_stride = _strides3(dk, packed)
+        a.dv_stride = _strides3(dv, packed)
+        a.causal_shift = int(causal_shift)
+        a.grad_accumulate = 1 if accumulate else 0
+        return a
+
+    key = ("bwd", dev.index, q.dtype, dq.dtype, _sig(q), _sig(k), _sig(v), _sig(out), _sig(lse),
+           _sig(dout), dlse is not None, _sig(dq), _sig(dk), _sig(dv), int(window or 0),
+           vis is not None, doc is not None, _sig(cu_seqlens_q), _sig(cu_seqlens_k),
+           max_seqlen_q, max_seqlen_k, int(causal_shift), bool(accumulate))
+    a, (full, small) = _cached_args(
+        key, build, lambda a: (lib.g4_attn_bwd_workspace_bytes(ctypes.byref(a)),
+                               lib.g4_attn_bwd_min_workspace_bytes(ctypes.byref(a))))
+    a.q, a.k, a.v, a.o, a.lse = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr()
+    a.vision_ids, a.document_ids = _ptr(vis), _ptr(doc)
+    a.cu_seqlens_q, a.cu_seqlens_k = _ptr(cu_seqlens_q), _ptr(cu_seqlens_k)
+    a.dout, a.dlse = dout.data_ptr(), _ptr(dlse)
+    a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    ws = _pick_workspace(full, small, algorithm == "recompute", dev, workspace_bytes)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _raise_for(lib.g4_attn_bwd(ctypes.byref(a), _stream(dev)), "g4_attn_bwd")
     return dq, dk, dv
