@@ -90,3 +90,37 @@ def test_missing_workspace_is_reported():
     lib = _lib.load()
     a = _args()
     assert lib.g4_attn_fwd(ctypes.byref(a), None) == _lib.G4_ERR_WORKSPACE
+
+
+def test_argument_blocks_are_cached_per_signature():
+    """ops caches an argument block and its workspace sizes per call signature
+    (shapes, strides, flags); each call gets a fresh copy whose pointers it
+    writes, so a cached block never carries another call's pointers and a new
+    signature builds (and sizes) its own block."""
+    from gemma4_fa4_kernels_b200 import _lib, ops
+
+    ops._SIG_CACHE.clear()
+    builds, sizings = [], []
+
+    def build_for(tag):
+        def build():
+            a = _lib.G4AttnArgs()
+            a.batch, a.window = tag, 7
+            a.q = 0x1000 * tag  # a pointer the caller must overwrite
+            builds.append(tag)
+            return a
+        return build
+
+    def sizes(a):
+        sizings.append(a.batch)
+        return (100 * a.batch, 10 * a.batch)
+
+    a1, s1 = ops._cached_args(("k", 1), build_for(1), sizes)
+    a1.q = 0xAAAA
+    a2, s2 = ops._cached_args(("k", 1), build_for(1), sizes)
+    a3, s3 = ops._cached_args(("k", 2), build_for(2), sizes)
+    assert builds == [1, 2] and sizings == [1, 2]
+    assert s1 == s2 == (100, 10) and s3 == (200, 20)
+    assert a2.q == 0x1000 and a2.window == 7  # a fresh copy, not the first call's block
+    assert a1 is not a2 and a3.batch == 2
+    ops._SIG_CACHE.clear()
