@@ -54,6 +54,14 @@ def test_local_d256_text_fixed(s):
     _fixed(1, s, s, 4, 2, 256, 1024, seed=200 + s)
 
 
+@pytest.mark.parametrize("hq,hkv", [(2, 2), (6, 2), (8, 2)], ids=["g1", "g3", "g4"])
+def test_local_d256_group_sizes(hq, hkv):
+    """Query groups of 1, 3 and 4 heads per KV head: the persistent forward's
+    KV-head mapping, and dQ with head pairs per CTA (even groups) or one head
+    per CTA (odd groups)."""
+    _fixed(1, 700, 700, hq, hkv, 256, 1024, seed=210 + hq)
+
+
 @pytest.mark.parametrize("s", [1, 130, 400])
 def test_global_d512_causal_fixed(s):
     _fixed(1, s, s, 8, 1, 512, 0, seed=300 + s)
