@@ -62,12 +62,15 @@ struct ShortCfg {
   static constexpr int kKeys = decode_short_keys(D, G);  // keys per CTA at most
   static constexpr int kKeysPerWarp = kKeys / kShortWarps;
   static constexpr int kOut = G * D / kShortThreads;     // combined outputs per thread
-  // merge: split partials requested per batch and output
-  static constexpr int kBatch = kOut >= 8 ? 4 : 32 / kOut;
+  // merge: split partials requested per batch and output (one batch covers the
+  // 18 splits of a 16-KV-head d256 cache with groups of up to two heads)
+  static constexpr int kBatch = kOut >= 8 ? 4 : 40 / kOut;
   // warp partials: O [warp][G][D], max and sum [warp][G]
   static constexpr int kSmemBytes = (kShortWarps * G * D + 2 * kShortWarps * G) * 4;
   static_assert(kKeysPerWarp >= 1 && kKeys == kKeysPerWarp * kShortWarps, "keys per warp");
   static_assert(G * D % kShortThreads == 0, "outputs per thread");
+  // the merge keeps each split's weight and sum in the warp partials' space
+  static_assert(2 * kDecodeShortMaxSplits <= kShortWarps * D, "merge scratch fits");
 };
 
 }  // namespace
@@ -264,18 +267,33 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // Merge: per head the splits' weights 2^(m_s - M) / L (warp h, in shared
-  // memory over the warp partials, which are no longer read), then every
-  // thread sums its outputs over the splits with kBatch loads per output in
-  // flight.
-  float* wts = wo;  // [G][ns]
+  // Merge: every thread requests its outputs' first batch of split partials
+  // and warps < G the splits' (max, sum) at once; then per head the weights
+  // 2^(m_s - M) / L (warp h, in shared memory over the warp partials, which are
+  // no longer read), and every thread sums its outputs over the splits.
+  float v[Cfg::kOut][Cfg::kBatch];
+  auto load_batch = [&](int s0) {
+#pragma unroll
+    for (int c = 0; c < Cfg::kOut; ++c) {
+      const int i = tid + c * kShortThreads;
+      const int h = i / D, d = i % D;
+      const float* po = p.part_o + (static_cast<int64_t>(seq) * hq + head0 + h) * ns * D + d;
+#pragma unroll
+      for (int b = 0; b < Cfg::kBatch; ++b)
+        v[c][b] = s0 + b < ns ? __ldcg(po + static_cast<int64_t>(s0 + b) * D) : 0.f;
+    }
+  };
+  load_batch(0);
+  float* wts = wo;         // [G][ns] split weights
+  float* lsum = wo + G * ns;  // [G][ns] split sums
   if (warp < G) {
     const float2* ml = p.part_ml + (static_cast<int64_t>(seq) * hq + head0 + warp) * ns;
     float M = -INFINITY;
     for (int s2 = lane; s2 < ns; s2 += 32) {
-      const float2 v = __ldcg(ml + s2);
-      const float mv = v.y > 0.f ? v.x : -INFINITY;
+      const float2 mv2 = __ldcg(ml + s2);
+      const float mv = mv2.y > 0.f ? mv2.x : -INFINITY;
       wts[warp * ns + s2] = mv;
+      lsum[warp * ns + s2] = mv2.y;
       M = fmaxf(M, mv);
     }
 #pragma unroll
@@ -284,7 +302,7 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
     for (int s2 = lane; s2 < ns; s2 += 32) {
       const float w = M == -INFINITY ? 0.f : ex2(wts[warp * ns + s2] - M);
       wts[warp * ns + s2] = w;
-      L = fmaf(w, __ldcg(ml + s2).y, L);
+      L = fmaf(w, lsum[warp * ns + s2], L);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
@@ -301,16 +319,7 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
 #pragma unroll
   for (int c = 0; c < Cfg::kOut; ++c) out[c] = 0.f;
   for (int s0 = 0; s0 < ns; s0 += Cfg::kBatch) {
-    float v[Cfg::kOut][Cfg::kBatch];
-#pragma unroll
-    for (int c = 0; c < Cfg::kOut; ++c) {
-      const int i = tid + c * kShortThreads;
-      const int h = i / D, d = i % D;
-      const float* po = p.part_o + (static_cast<int64_t>(seq) * hq + head0 + h) * ns * D + d;
-#pragma unroll
-      for (int b = 0; b < Cfg::kBatch; ++b)
-        v[c][b] = s0 + b < ns ? __ldcg(po + static_cast<int64_t>(s0 + b) * D) : 0.f;
-    }
+    if (s0 > 0) load_batch(s0);
 #pragma unroll
     for (int c = 0; c < Cfg::kOut; ++c) {
       const int h = (tid + c * kShortThreads) / D;
