@@ -451,25 +451,47 @@ def decode_measure(ops, _lib, dev, seed, iters):
         for _ in range(3):
             ops.attn_fwd(q, k, v, window=c["window"])
         torch.cuda.synchronize(dev)
+        # the call: events around it alone (no per-launch events inside)
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(iters)]
-        _lib.profile_reset()
-        _lib.profile_enable(True)
         for a, b in evs:
             flush.max()
             a.record()
             ops.attn_fwd(q, k, v, window=c["window"])
             b.record()
         torch.cuda.synchronize(dev)
+        call_us = statistics.median(a.elapsed_time(b) for a, b in evs) * 1e3
+        # device time a call adds to a stream of calls: batches of (flush, call)
+        # against batches of the flush alone (no event inside a batch, so the
+        # launches of one call overlap as they do in a decode loop)
+        def batch(with_call, n=40):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(dev)
+            a.record()
+            for _ in range(n):
+                flush.max()
+                if with_call:
+                    ops.attn_fwd(q, k, v, window=c["window"])
+            b.record()
+            torch.cuda.synchronize(dev)
+            return a.elapsed_time(b) * 1e3 / n
+        added_us = statistics.median(batch(True) - batch(False) for _ in range(5))
+        # the decode kernel: a second pass with events around each launch
+        _lib.profile_reset()
+        _lib.profile_enable(True)
+        for _ in range(iters):
+            flush.max()
+            ops.attn_fwd(q, k, v, window=c["window"])
+        torch.cuda.synchronize(dev)
         _lib.profile_enable(False)
         prof = _lib.profile_read()
-        call_us = statistics.median(a.elapsed_time(b) for a, b in evs) * 1e3
         kname = "decode_short" if prof.get("decode_short", (0, 0.0))[0] > 0 else "decode"
         n_dec, dec_ms = prof.get(kname, (0, 0.0))
         kern_us = dec_ms / max(n_dec, 1) * 1e3
         nbytes = 2 * cap * hkv * d * 2 + 2 * hq * d * 2 + hq * 4
         gbs = nbytes / (kern_us * 1e-6) / 1e9
         out[c["key"]] = {"workload": c["name"], "us_per_call": round(call_us, 2),
+                         "device_us_per_call_in_a_loop": round(added_us, 2),
                          "traffic": load_traffic().get(f"decode@{c['key']}"),
                          "decode_kernel": kname, "decode_kernel_us": round(kern_us, 2),
                          "bytes": nbytes,

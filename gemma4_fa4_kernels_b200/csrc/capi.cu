@@ -62,6 +62,7 @@ enum KernelId {
   kKMerge,
   kKAdd,
   kKDecodeShort,
+  kKDecodeReset,
   kKCount
 };
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
@@ -71,7 +72,7 @@ const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq
                                            "decode_combine", "prep_fwd",  "prep_bwd",
                                            "prep_dw_reduce", "selftest_wait", "bwd_gemm_dvdk",
                                            "cast_f32_bf16", "ring_merge", "add_f32",
-                                           "decode_short"};
+                                           "decode_short", "decode_reset"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -185,6 +186,8 @@ int check_common(const g4_attn_args* a) {
     return fail(G4_ERR_INVALID, "q, k, v, o and lse are required");
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o))
     return fail(G4_ERR_INVALID, "q, k, v and o base pointers must be 16-byte aligned");
+  if (a->workspace && !aligned16(a->workspace))  // bulk copies and tensor maps of the scratch
+    return fail(G4_ERR_INVALID, "workspace must be 16-byte aligned");
   if (a->k == a->v) return fail(G4_ERR_INVALID, "K and V must be distinct operands");
   if (a->batch <= 0 || a->seqlen_q <= 0 || a->seqlen_k <= 0)
     return fail(G4_ERR_INVALID, "batch and sequence lengths must be positive");
@@ -880,8 +883,15 @@ int run_decode(const g4_attn_args* a, cudaStream_t st) {
   const size_t reset = short_kernel ? align256(w.decode_counters + sizeof(int) * size_t(a->batch) *
                                                                    size_t(a->num_kv_heads))
                                     : 256;
-  cudaError_t ce = cudaMemsetAsync(a->workspace, 0, reset, st);
-  if (ce != cudaSuccess) return cuda_fail(ce, "workspace reset");
+  if (short_kernel) {
+    // a one-CTA kernel instead of a memset: the decode kernel overlaps it
+    LaunchScope ls(kKDecodeReset, st);
+    const int e = g4::launch_decode_reset(a->workspace, reset, st);
+    if (e) return cuda_fail(static_cast<cudaError_t>(e), "workspace reset");
+  } else {
+    cudaError_t ce = cudaMemsetAsync(a->workspace, 0, reset, st);
+    if (ce != cudaSuccess) return cuda_fail(ce, "workspace reset");
+  }
   const bool packed = a->cu_seqlens_q != nullptr;
   g4::DecodeParams p;
   memset(&p, 0, sizeof(p));

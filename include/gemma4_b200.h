@@ -10,7 +10,8 @@
  * Conventions
  *  - All tensors are device pointers owned by the caller; the library never
  *    allocates or frees caller memory.  Scratch memory is passed in as
- *    `workspace` (size from the matching *_workspace_bytes query).
+ *    `workspace` (size from the matching *_workspace_bytes query, base
+ *    16-byte aligned).
  *  - Q/K/V/O and gradients are bf16 with unit stride along the head dimension;
  *    the other strides are in elements and must be multiples of 8 (16 bytes),
  *    base pointers 16-byte aligned.  LSE/dLSE are fp32 natural-log values.

@@ -68,6 +68,7 @@ def test_workspace_queries_need_no_device():
     (dict(num_q_heads=30), _lib.G4_ERR_INVALID, "multiple of KV heads"),
     (dict(seqlen_q=4096), _lib.G4_ERR_UNSUPPORTED, "Sq <= Sk"),
     (dict(window=-1), _lib.G4_ERR_INVALID, "window"),
+    (dict(workspace=0x3008, workspace_bytes=1 << 30), _lib.G4_ERR_INVALID, "workspace"),
 ])
 def test_malformed_arguments_fail_before_launch(over, code, needle):
     assert _call(_args(**over)) == code
