@@ -262,8 +262,9 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
   }
   __threadfence();
   __syncthreads();
-  // The counters were zeroed by decode_reset_kernel, which let this grid launch
-  // at once: everything above ran under it, the first counter access waits.
+  // The counters were zeroed by the call's workspace reset kernel, which let
+  // this grid launch at once: everything above ran under it, the first counter
+  // access waits for it.
   pdl_enter();
   int* counter = p.counters + static_cast<int64_t>(seq) * gridDim.y + kvh;
   if (tid == 0) last = atomicAdd(counter, 1) == ns - 1;
@@ -371,24 +372,6 @@ static int launch_short_d(const DecodeParams& p, int num_kv_heads, cudaStream_t 
     case 4: return launch_short_dg<D, 4>(p, num_kv_heads, stream);
     default: return static_cast<int>(cudaErrorInvalidValue);
   }
-}
-
-// Zeroes a call's workspace header and the arrival counters (16-byte words) in
-// place of a memset, and lets the decode kernel, launched next as a chained
-// launch, start at once (griddepcontrol.launch_dependents): its K/V loads,
-// scores and partials overlap this kernel, and it waits for it (pdl_enter)
-// only before its first counter access.  Launched plainly, so it starts after
-// every earlier kernel of the stream has completed (the cache update that wrote
-// K and V among them).
-__global__ void __launch_bounds__(256) decode_reset_kernel(int4* words, int n) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  for (int i = threadIdx.x; i < n; i += blockDim.x) words[i] = make_int4(0, 0, 0, 0);
-}
-
-int launch_decode_reset(void* words, size_t bytes, cudaStream_t stream) {
-  decode_reset_kernel<<<1, 256, 0, stream>>>(static_cast<int4*>(words),
-                                              static_cast<int>(bytes / sizeof(int4)));
-  return static_cast<int>(cudaGetLastError());
 }
 
 int launch_decode_short(int d, const DecodeParams& p, int num_kv_heads, cudaStream_t stream) {

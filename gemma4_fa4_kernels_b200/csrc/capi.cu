@@ -62,7 +62,7 @@ enum KernelId {
   kKMerge,
   kKAdd,
   kKDecodeShort,
-  kKDecodeReset,
+  kKReset,
   kKCount
 };
 const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq", "bwd_dkv",
@@ -72,7 +72,7 @@ const char* const kKernelNames[kKCount] = {"attn_fwd", "bwd_preprocess", "bwd_dq
                                            "decode_combine", "prep_fwd",  "prep_bwd",
                                            "prep_dw_reduce", "selftest_wait", "bwd_gemm_dvdk",
                                            "cast_f32_bf16", "ring_merge", "add_f32",
-                                           "decode_short", "decode_reset"};
+                                           "decode_short", "workspace_reset"};
 std::atomic<long long> g_launches[kKCount];
 std::atomic<bool> g_profile{false};
 struct ProfRecord {
@@ -726,13 +726,34 @@ bool plan_bands(const g4_attn_args* a, const Workspace& w, bool backward, size_t
   return false;
 }
 
+// Zeroes a call's workspace header (and the short-window decode's arrival
+// counters): `bytes` (a multiple of 16) at a 16-byte aligned `words`, by one CTA
+// instead of a memset.  It triggers griddepcontrol.launch_dependents at once, so
+// the call's first kernel (a chained launch) is dispatched while it runs; that
+// kernel waits for it (pdl_enter) before touching the header: at its start for
+// the attention kernels, only before its first counter access for the
+// short-window decode, whose loads and arithmetic overlap it.  A plain launch,
+// it starts after every earlier kernel of the stream has completed.
+__global__ void __launch_bounds__(256) workspace_reset_kernel(int4* words, int n) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int i = threadIdx.x; i < n; i += blockDim.x) words[i] = make_int4(0, 0, 0, 0);
+}
+
+int reset_workspace(void* words, size_t bytes, cudaStream_t st) {
+  LaunchScope ls(kKReset, st);
+  workspace_reset_kernel<<<1, 256, 0, st>>>(static_cast<int4*>(words),
+                                             static_cast<int>(bytes / sizeof(int4)));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? G4_OK : cuda_fail(e, "workspace reset");
+}
+
 // Common prologue: zero the header, plan packed tiles and metadata bounds.
 int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream_t st,
             g4::MaskSpec* mask) {
   if (!a->workspace || a->workspace_bytes < w.total)
     return fail(G4_ERR_WORKSPACE, "workspace of %zu bytes required", w.total);
-  cudaError_t e = cudaMemsetAsync(a->workspace, 0, 256, st);
-  if (e != cudaSuccess) return cuda_fail(e, "workspace reset");
+  if (int rc = reset_workspace(a->workspace, 256, st)) return rc;
+  cudaError_t e = cudaSuccess;
   const g4::SeqLayout layout = make_layout(a);
   int* hdr = ws_ptr<int>(a, 0);
   if (a->cu_seqlens_q) {
@@ -883,15 +904,7 @@ int run_decode(const g4_attn_args* a, cudaStream_t st) {
   const size_t reset = short_kernel ? align256(w.decode_counters + sizeof(int) * size_t(a->batch) *
                                                                    size_t(a->num_kv_heads))
                                     : 256;
-  if (short_kernel) {
-    // a one-CTA kernel instead of a memset: the decode kernel overlaps it
-    LaunchScope ls(kKDecodeReset, st);
-    const int e = g4::launch_decode_reset(a->workspace, reset, st);
-    if (e) return cuda_fail(static_cast<cudaError_t>(e), "workspace reset");
-  } else {
-    cudaError_t ce = cudaMemsetAsync(a->workspace, 0, reset, st);
-    if (ce != cudaSuccess) return cuda_fail(ce, "workspace reset");
-  }
+  if (int rc = reset_workspace(a->workspace, reset, st)) return rc;
   const bool packed = a->cu_seqlens_q != nullptr;
   g4::DecodeParams p;
   memset(&p, 0, sizeof(p));

@@ -203,9 +203,6 @@ __host__ __device__ constexpr int decode_short_keys(int d, int g) {
   return (g > 2 ? 8192 : 16384) / d;
 }
 int launch_decode_short(int d, const DecodeParams& p, int num_kv_heads, cudaStream_t stream);
-// Zeroes `bytes` (a multiple of 16) at a 16-byte aligned `words` and lets the
-// short-window decode kernel launched next on the stream start at once.
-int launch_decode_reset(void* words, size_t bytes, cudaStream_t stream);
 constexpr int kDecodeMaxSplits = 1024;
 constexpr int kDecodeStages = 6;   // 32 KB ring stages
 int decode_smem_bytes(int d);
