@@ -67,6 +67,14 @@ def test_global_d512_causal_fixed(s):
     _fixed(1, s, s, 8, 1, 512, 0, seed=300 + s)
 
 
+@pytest.mark.parametrize("hq,hkv", [(2, 2), (4, 2), (6, 2)], ids=["g1", "g2", "g3"])
+def test_global_d512_group_sizes(hq, hkv):
+    """Query groups of 1, 2 and 3 heads per KV head at d512: the dQ GEMM runs
+    as 2-CTA pairs over heads 2i, 2i+1 of a group for even groups, one CTA per
+    head otherwise, and dK / dV sum every group size in TMEM."""
+    _fixed(1, 300, 300, hq, hkv, 512, 0, seed=220 + hq)
+
+
 def test_global_d512_rectangular_with_dlse():
     _fixed(1, 90, 260, 8, 1, 512, 0, seed=41, with_dlse=True)
 

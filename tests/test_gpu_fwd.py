@@ -46,6 +46,13 @@ def test_global_d512_causal_fixed(s):
     _fixed_case(1, s, s, 8, 1, 512, 0, seed=100 + s)
 
 
+@pytest.mark.parametrize("hq,hkv", [(2, 2), (4, 2), (6, 2)], ids=["g1", "g2", "g3"])
+def test_global_d512_group_sizes(hq, hkv):
+    """Groups of 1, 2 and 3 query heads at d512: the O GEMM of the two-pass
+    forward runs as 2-CTA head pairs for even groups, one CTA per head else."""
+    _fixed_case(1, 300, 300, hq, hkv, 512, 0, seed=120 + hq)
+
+
 def test_global_d512_rectangular_lower_right():
     _fixed_case(2, 70, 333, 8, 1, 512, 0, seed=7)
 
