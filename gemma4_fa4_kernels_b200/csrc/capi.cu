@@ -275,6 +275,48 @@ int sm_count() {
   return n;
 }
 
+// A second stream per device for the backward's dQ GEMM, which needs nothing of
+// the dV / dK GEMMs: forked from the caller's stream after a band's score
+// passes and joined back before the next launch, so each GEMM's last, partly
+// empty wave runs beside the other's CTAs.  The fork and join events are
+// shared by every call on the device, so one mutex keeps each record / wait
+// pair together (calls from several host threads stay correct; their dQ
+// launches are merely ordered on the one side stream).  Stream capture forks
+// the side stream into the graph and the join brings it back.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr;
+  cudaEvent_t join = nullptr;
+};
+std::mutex g_side_mu;
+
+SideStream* side_stream() {  // call with g_side_mu held; nullptr when unavailable
+  constexpr int kDev = 64;
+  static SideStream side[kDev];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDev) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  SideStream& sd = side[dev];
+  if (!sd.stream) {
+    cudaStream_t st = nullptr;
+    cudaEvent_t f = nullptr, j = nullptr;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&f, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&j, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      if (st) cudaStreamDestroy(st);
+      if (f) cudaEventDestroy(f);
+      return nullptr;
+    }
+    sd.fork = f;
+    sd.join = j;
+    sd.stream = st;
+  }
+  return &sd;
+}
+
 // One query token per sequence: the split-key decode kernels serve the call.
 bool decode_eligible(const g4_attn_args* a) {
   const bool packed = a->cu_seqlens_q != nullptr;
@@ -753,7 +795,6 @@ int prepare(const g4_attn_args* a, const Workspace& w, bool backward, cudaStream
   if (!a->workspace || a->workspace_bytes < w.total)
     return fail(G4_ERR_WORKSPACE, "workspace of %zu bytes required", w.total);
   if (int rc = reset_workspace(a->workspace, 256, st)) return rc;
-  cudaError_t e = cudaSuccess;
   const g4::SeqLayout layout = make_layout(a);
   int* hdr = ws_ptr<int>(a, 0);
   if (a->cu_seqlens_q) {
@@ -1399,26 +1440,45 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
         e = g4::launch_bwd_score(D, pass, tq, tk, tv, tdo, mb, b.rows, st);
         if (e) return cuda_fail(static_cast<cudaError_t>(e), "score launch");
       }
+      // dQ on the side stream, forked after the score passes, joined after dV / dK
+      std::unique_lock<std::mutex> side_lock(g_side_mu);
+      SideStream* sd = side_stream();
+      if (sd && (cudaEventRecord(sd->fork, st) != cudaSuccess ||
+                 cudaStreamWaitEvent(sd->stream, sd->fork, 0) != cudaSuccess)) {
+        cudaGetLastError();
+        sd = nullptr;  // dQ stays on the caller's stream
+      }
+      {
+        cudaStream_t sq = sd ? sd->stream : st;
+        LaunchScope ls(kKGemmDq, sq);
+        e = g4::launch_bwd_tile_gemm(D, 2, tk64, tdq, pairs ? &tds : nullptr, mb, b.rows,
+                                     b.nh * p.group, sq);
+        if (!e && sd) e = static_cast<int>(cudaEventRecord(sd->join, sd->stream));
+        if (e) {
+          if (sd) cudaStreamWaitEvent(st, sd->join, 0);
+          return cuda_fail(static_cast<cudaError_t>(e), "dQ launch");
+        }
+      }
       if (b.kv_items > 0) {
         if (b_bytes <= (int64_t(80) << 20)) {
           LaunchScope ls(kKGemmDvDk, st);
           e = g4::launch_bwd_tile_gemm_dvdk(D, tdo64, tdv, tq64, tdk, mb, b.kv_items, b.nh, st);
-          if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV/dK launch");
         } else {
           {
             LaunchScope ls(kKGemmDv, st);
             e = g4::launch_bwd_tile_gemm(D, 0, tdo64, tdv, nullptr, mb, b.kv_items, b.nh, st);
-            if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV launch");
           }
-          LaunchScope ls(kKGemmDk, st);
-          e = g4::launch_bwd_tile_gemm(D, 1, tq64, tdk, nullptr, mb, b.kv_items, b.nh, st);
-          if (e) return cuda_fail(static_cast<cudaError_t>(e), "dK launch");
+          if (!e) {
+            LaunchScope ls(kKGemmDk, st);
+            e = g4::launch_bwd_tile_gemm(D, 1, tq64, tdk, nullptr, mb, b.kv_items, b.nh, st);
+          }
         }
       }
-      LaunchScope ls(kKGemmDq, st);
-      e = g4::launch_bwd_tile_gemm(D, 2, tk64, tdq, pairs ? &tds : nullptr, mb, b.rows,
-                                   b.nh * p.group, st);
-      if (e) return cuda_fail(static_cast<cudaError_t>(e), "dQ launch");
+      if (sd) {
+        const cudaError_t je = cudaStreamWaitEvent(st, sd->join, 0);  // join before any return
+        if (!e && je != cudaSuccess) e = static_cast<int>(je);
+      }
+      if (e) return cuda_fail(static_cast<cudaError_t>(e), "dV/dK launch");
     }
     if (mp.own_acc) {
       const int64_t rows_b = a->seqlen_k;  // packed: one "batch" of Tk rows
