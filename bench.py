@@ -284,7 +284,8 @@ def roofline_of(prof, kflops, steps, peaks, clocks, region_s, traffic_key):
             "frac_of_sustained_peak": round(achieved / peak_sus, 4),
             "traffic": traffic, "launch_ms": round(per_ms, 4),
             "kernel_share": {n: round(prof[n][1] / total_ms, 4) for n in prof},
-            "kernel_pass": "separate profiled pass of the same steps (events around each launch)"}
+            "kernel_pass": "separate profiled pass of the same steps (events around each launch; "
+                           "the library serialises its launches while they are profiled)"}
 
 
 class ClockSampler:

@@ -1441,8 +1441,10 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
         if (e) return cuda_fail(static_cast<cudaError_t>(e), "score launch");
       }
       // dQ on the side stream, forked after the score passes, joined after dV / dK
+      // (serialised on the caller's stream while launches are being profiled, so
+      // that every launch's events time that kernel alone)
       std::unique_lock<std::mutex> side_lock(g_side_mu);
-      SideStream* sd = side_stream();
+      SideStream* sd = g_profile.load() ? nullptr : side_stream();
       if (sd && (cudaEventRecord(sd->fork, st) != cudaSuccess ||
                  cudaStreamWaitEvent(sd->stream, sd->fork, 0) != cudaSuccess)) {
         cudaGetLastError();
