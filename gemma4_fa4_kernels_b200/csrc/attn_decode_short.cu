@@ -260,17 +260,24 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
     p.part_o[row * D + d] = co[c];
     if (d == 0) p.part_ml[row] = make_float2(cm[c], cl[c]);
   }
-  __threadfence();
+  // Release and acquire through one thread (the pattern of a grid-wide
+  // barrier): the CTA barrier orders every thread's partial stores before
+  // thread 0's fence and ticket; in the CTA that takes the last ticket, thread
+  // 0's fence after it orders every split's partials before the barrier that
+  // releases the merge's loads.
   __syncthreads();
   // The counters were zeroed by the call's workspace reset kernel, which let
   // this grid launch at once: everything above ran under it, the first counter
   // access waits for it.
   pdl_enter();
   int* counter = p.counters + static_cast<int64_t>(seq) * gridDim.y + kvh;
-  if (tid == 0) last = atomicAdd(counter, 1) == ns - 1;
+  if (tid == 0) {
+    __threadfence();
+    last = atomicAdd(counter, 1) == ns - 1;
+    if (last) __threadfence();
+  }
   __syncthreads();
   if (!last) return;
-  __threadfence();
   // Merge: every thread requests its outputs' first batch of split partials
   // and warps < G the splits' (max, sum) at once; then per head the weights
   // 2^(m_s - M) / L (warp h, in shared memory over the warp partials, which are
