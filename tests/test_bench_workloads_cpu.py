@@ -54,3 +54,19 @@ def test_c3_packing_shape_and_vision_share():
     for a, b in zip(cu[:-1], cu[1:]):  # images stay inside their segment (document)
         seg = vis[a:b]
         assert (seg >= 0).sum() % 256 == 0
+
+
+def test_peak_choice_follows_the_window_clocks():
+    """A line's fraction is taken against the burst peak only for a short window
+    at full clock with no power capping; otherwise against the sustained one."""
+    peaks = (1400.0, 1660.0, "measured")
+    full = {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
+    capped = {"sm_mhz": 1250.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"]}
+    slow = {"sm_mhz": 1500.0, "sm_max_mhz": 1965.0, "reasons": []}
+    assert bench.pick_peak(peaks, full, 0.5)[0] == 1660.0
+    assert "burst" in bench.pick_peak(peaks, full, 0.5)[1]
+    assert bench.pick_peak(peaks, full, 30.0)[0] == 1400.0  # long window
+    assert bench.pick_peak(peaks, capped, 0.5)[0] == 1400.0
+    assert bench.pick_peak(peaks, slow, 0.5)[0] == 1400.0
+    assert bench.pick_peak(peaks, {"sm_mhz": None, "sm_max_mhz": None, "reasons": []},
+                           0.5)[0] == 1400.0  # no samples: the conservative figure
