@@ -52,12 +52,19 @@ struct PreCfg {
 template <int DV>
 __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const BwdParams p, int64_t tokens_q) {
   constexpr int kRows = PreCfg<DV>::kRows, kIters = PreCfg<DV>::kIters;
-  pdl_enter();
+  // This kernel reads only the call's inputs (O, dO, LSE, dLSE: written before
+  // the call's plain-launched workspace reset started) and writes delta and
+  // log2 LSE, which no kernel of the call before it touches, so it waits for its
+  // predecessor (pdl_enter) only at its end: the reset and the packed-layout
+  // planning run under its loads, and its completion still implies theirs.
   const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t rows = tokens_q * p.num_q_heads;
   const int64_t row0 = warp_id * kRows;
-  if (row0 >= rows) return;
+  if (row0 >= rows) {
+    pdl_enter();
+    return;
+  }
   uint4 ov[kRows][kIters], gv[kRows][kIters];
   int64_t bs[kRows], ss[kRows], tk[kRows];
   int hs[kRows];
@@ -125,6 +132,7 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const BwdParams p, 
     p.delta[wi] = a - (isfinite(dl) ? dl : 0.f);
     p.lse2[wi] = lse == -INFINITY ? -INFINITY : lse * kLog2e;
   }
+  pdl_enter();
 }
 
 int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int64_t tokens_q,
