@@ -15,10 +15,15 @@ namespace g4 {
 // Chained launches (programmatic dependent launch).  The attention kernels of
 // one call run back to back on a stream; launched with launch_chained, a
 // kernel is launched ahead and its CTAs are dispatched as the previous
-// kernel's CTAs exit, instead of after a full launch gap.  Every kernel
-// launched this way calls pdl_enter() before its first global memory access:
-// it waits until the previous grid in the stream has completed and its writes
-// are visible (a predecessor that is not a chained kernel passes at once).
+// kernel's CTAs exit, instead of after a full launch gap.  A kernel launched
+// this way calls pdl_enter() before its first access to memory that an earlier
+// kernel of the call writes: it waits until the previous grid in the stream has
+// completed and its writes are visible (a predecessor that is not a chained
+// kernel passes at once).  Most kernels wait at their start; the backward
+// preprocess (which touches nothing an earlier kernel of the call writes) waits
+// at its end, and the short-window decode before its first arrival counter,
+// so both run under the call's workspace reset; every chained kernel waits
+// somewhere, so its completion implies its predecessor's.
 // There is no early trigger (griddepcontrol.launch_dependents): with one, the
 // successor's waiting CTAs took SMs during the long c1 kernels' last wave and
 // the step got 1% slower; without it c0 is 3% and c1 0.6% faster.
