@@ -88,7 +88,10 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
   const SeqInfo si = p.layout.seq(seq);
-  if (si.len_q <= 0) return;  // packed segment without a query token (whole CTA)
+  if (si.len_q <= 0) {  // packed segment without a query token (whole CTA)
+    pdl_enter();  // every exit waits: the grid's completion implies the reset's
+    return;
+  }
   const int q_abs = si.len_k - 1;
   const int k_lo = p.window > 0 ? max(0, q_abs - p.window + 1) : 0;
   const int total = max(0, si.len_k - k_lo);
@@ -248,6 +251,7 @@ __global__ void __launch_bounds__(kShortThreads, 2) decode_short_kernel(const De
               static_cast<int64_t>(head0 + h) * p.lse_stride[1] + si.q_base] =
             cl[c] > 0.f ? (cm[c] + __log2f(cl[c])) * kLn2 : -INFINITY;
     }
+    pdl_enter();
     return;
   }
 
