@@ -50,8 +50,12 @@ struct PreCfg {
 };
 
 template <int DV>
-__global__ void __launch_bounds__(256) bwd_preprocess_kernel(const BwdParams p, int64_t tokens_q) {
+__global__ void __launch_bounds__(256) bwd_preprocess_kernel(const BwdParams p, int64_t tokens_q,
+                                                             int early_trigger) {
   constexpr int kRows = PreCfg<DV>::kRows, kIters = PreCfg<DV>::kIters;
+  // A successor that waits for this kernel only at its own end (the one-CTA
+  // range planner of fixed layouts) is let in at once: it plans under the loads.
+  if (early_trigger) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // This kernel reads only the call's inputs (O, dO, LSE, dLSE: written before
   // the call's plain-launched workspace reset started) and writes delta and
   // log2 LSE, which no kernel of the call before it touches, so it waits for its
@@ -136,7 +140,7 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const BwdParams p, 
 }
 
 int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int64_t tokens_q,
-                          cudaStream_t stream) {
+                          bool early_trigger, cudaStream_t stream) {
   const int64_t rows = tokens_q * p.num_q_heads;
   const int threads = 256;
   const int per_warp = head_dim_v == 256 ? PreCfg<256>::kRows : PreCfg<512>::kRows;
@@ -146,8 +150,10 @@ int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int64_t tokens_q,
   const dim3 grid(static_cast<unsigned>(blocks));
   const cudaError_t e =
       head_dim_v == 256
-          ? launch_chained(bwd_preprocess_kernel<256>, grid, dim3(threads), 0, stream, p, tokens_q)
-          : launch_chained(bwd_preprocess_kernel<512>, grid, dim3(threads), 0, stream, p, tokens_q);
+          ? launch_chained(bwd_preprocess_kernel<256>, grid, dim3(threads), 0, stream, p, tokens_q,
+                           early_trigger ? 1 : 0)
+          : launch_chained(bwd_preprocess_kernel<512>, grid, dim3(threads), 0, stream, p, tokens_q,
+                           early_trigger ? 1 : 0);
   if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }

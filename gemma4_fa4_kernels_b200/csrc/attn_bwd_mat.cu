@@ -256,9 +256,14 @@ __global__ void __launch_bounds__(kPlanThreads) plan_qtile_lists_kernel(const Ma
 __global__ void plan_qtile_ranges_kernel(const MatParams p) {
   __shared__ int scan[1024];
   __shared__ int carry;
-  pdl_enter();
-  const int tid = threadIdx.x;
+  // Fixed layouts without key-tile lists compute every range from the
+  // arguments alone (nothing an earlier kernel of the call writes), so they
+  // wait for the predecessor only at the end: behind the backward preprocess,
+  // which lets this kernel in at once, the planning runs under its loads.
   const bool packed = p.layout.packed();
+  const bool late = !packed && p.klist == nullptr;
+  if (!late) pdl_enter();
+  const int tid = threadIdx.x;
   const int n = packed ? *p.n_q_tiles : p.layout.batch * p.n_qt_fixed;
   if (tid == 0) carry = 0;
   __syncthreads();
@@ -304,6 +309,7 @@ __global__ void plan_qtile_ranges_kernel(const MatParams p) {
     if (tid == 1023) carry += scan[1023];
     __syncthreads();
   }
+  if (late) pdl_enter();
 }
 
 // =====================================================================================

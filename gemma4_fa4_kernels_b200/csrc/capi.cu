@@ -1274,7 +1274,10 @@ int g4_attn_bwd(const g4_attn_args* a, void* stream) {
   int e;
   {
     LaunchScope ls(kKBwdPre, st);
-    e = g4::launch_bwd_preprocess(p, a->head_dim_v, w.tokens_q, st);
+    // the range planner follows at once when the band plan is made and the
+    // layout is fixed without key-tile lists (it then waits late, see there)
+    const bool early = (mp.ok || defer) && !packed && !lists;
+    e = g4::launch_bwd_preprocess(p, a->head_dim_v, w.tokens_q, early, st);
   }
   if (e) return cuda_fail(static_cast<cudaError_t>(e), "backward preprocess launch");
   const int D = a->head_dim_qk;

@@ -20,10 +20,11 @@ namespace g4 {
 // kernel of the call writes: it waits until the previous grid in the stream has
 // completed and its writes are visible (a predecessor that is not a chained
 // kernel passes at once).  Most kernels wait at their start; the backward
-// preprocess (which touches nothing an earlier kernel of the call writes) waits
-// at its end, and the short-window decode before its first arrival counter,
-// so both run under the call's workspace reset; every chained kernel waits
-// somewhere, so its completion implies its predecessor's.
+// preprocess and the range planner of fixed layouts without key-tile lists
+// (which touch nothing an earlier kernel of the call writes) wait at their end,
+// and the short-window decode before its first arrival counter, so they run
+// under their predecessor; every chained kernel waits somewhere, so its
+// completion implies its predecessor's.
 // There is no early trigger (griddepcontrol.launch_dependents): with one, the
 // successor's waiting CTAs took SMs during the long c1 kernels' last wave and
 // the step got 1% slower; without it c0 is 3% and c1 0.6% faster.
@@ -305,8 +306,10 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
 int launch_fwd_persistent(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                           const FwdParams& p, int ctas, int num_q_heads, cudaStream_t stream);
 
+// early_trigger: the next launch is the range planner of a fixed layout without
+// key-tile lists, which waits for the preprocess only at its end.
 int launch_bwd_preprocess(const BwdParams& p, int head_dim_v, int64_t tokens_q,
-                          cudaStream_t stream);
+                          bool early_trigger, cudaStream_t stream);
 
 // dQ: grid (grid_x query tiles, Hq, D/256 slabs).  Maps: Q/K/V/dO with 128-row
 // boxes and K with 64-row boxes.
