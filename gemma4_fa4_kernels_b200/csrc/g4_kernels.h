@@ -25,9 +25,12 @@ namespace g4 {
 // and the short-window decode before its first arrival counter, so they run
 // under their predecessor; every chained kernel waits somewhere, so its
 // completion implies its predecessor's.
-// There is no early trigger (griddepcontrol.launch_dependents): with one, the
-// successor's waiting CTAs took SMs during the long c1 kernels' last wave and
-// the step got 1% slower; without it c0 is 3% and c1 0.6% faster.
+// The attention kernels give no early trigger (griddepcontrol.launch_dependents):
+// with one, the successor's waiting CTAs took SMs during the long c1 kernels'
+// last wave and the step got 1% slower; without it c0 is 3% and c1 0.6% faster.
+// Only a predecessor whose successor works before it waits triggers at its
+// start: the one-CTA workspace reset, and the backward preprocess when the
+// late-waiting range planner follows.
 #ifdef __CUDACC__
 __device__ __forceinline__ void pdl_enter() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 #endif
